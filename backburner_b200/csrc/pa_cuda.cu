@@ -1,0 +1,647 @@
+// pa_cuda.cu - libpacuda.so: the C ABI of include/pa_cuda.h over the sm_100a kernels (pa_decode.cuh, pa_merge.cuh).
+// Host side: contexts, plans (the split of a call into chunk jobs), the pa::engine page/begin/end path, and the
+// device status word that bounded in-kernel waits report into.
+#include "pa_cuda.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "pa_decode.cuh"
+#include "pa_merge.cuh"
+
+namespace {
+
+constexpr int kMaxSmem = 227 * 1024;
+
+struct Plan;
+
+}  // namespace
+
+struct pa_cuda_ctx {
+    int device = 0;
+    int n_sm = 148;
+    cudaStream_t stream = nullptr;
+    int *d_status = nullptr;
+    uint64_t timeout_ns = 2000000000ull;
+    uint64_t launches = 0;
+    int stall_test = 0;
+    std::string err;
+    // pa::engine state (begin/end)
+    pa_cuda_plan *eng_plan = nullptr;
+    std::vector<pa_cuda_seg> eng_segs;
+    uint16_t *h_q = nullptr;      // pinned staging
+    float *h_out = nullptr;       // pinned staging: O, then m, then l
+    size_t h_q_bytes = 0, h_out_bytes = 0;
+    uint16_t *d_q = nullptr;
+    float *d_out = nullptr;
+    size_t d_q_bytes = 0, d_out_bytes = 0;
+    cudaEvent_t ev_begin = nullptr, ev_end = nullptr;
+    std::chrono::steady_clock::time_point t_begin;
+    int eng_ng = 0, eng_nt = 0, eng_rows = 0, eng_nkv = 0, eng_hd = 0;
+    bool eng_active = false;
+    double last_exec_ms = 0;
+};
+
+struct pa_cuda_plan {
+    pa_cuda_ctx *ctx = nullptr;
+    pa_cuda_shape sh{};
+    uint32_t n_sets = 0, n_jobs = 0, n_slots = 0;
+    pa::dec::Job *d_jobs = nullptr;
+    uint32_t *d_crange = nullptr;
+    float *d_op = nullptr, *d_mp = nullptr, *d_lp = nullptr;
+    size_t scratch = 0;
+    // decode launch shape
+    uint32_t hg = 1, rgc = 1, n_rg = 1, pw = 1, n_consumers = 1, str = 0, grid_y = 1;
+    size_t smem = 0;
+};
+
+namespace {
+
+int fail(pa_cuda_ctx *ctx, int code, const std::string &msg) {
+    if (ctx) ctx->err = msg;
+    return code;
+}
+int cuda_fail(pa_cuda_ctx *ctx, cudaError_t e, const char *what) {
+    return fail(ctx, PA_CUDA_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+#define PA_CK(call, what)                                    \
+    do {                                                     \
+        cudaError_t e_ = (call);                             \
+        if (e_ != cudaSuccess) return cuda_fail(ctx, e_, what); \
+    } while (0)
+
+cudaStream_t pick(pa_cuda_ctx *ctx, void *stream) { return stream ? (cudaStream_t) stream : ctx->stream; }
+
+size_t head_bytes(uint32_t quant, uint32_t hd) { return quant == PA_CUDA_Q8_0 ? hd / 32 * 34 : hd / 32 * 18; }
+
+int check_shape(pa_cuda_ctx *ctx, const pa_cuda_shape *sh) {
+    if (!sh) return fail(ctx, PA_CUDA_EINVAL, "shape is null");
+    if (sh->hd != 128 && sh->hd != 256) return fail(ctx, PA_CUDA_EUNSUPPORTED, "hd must be 128 or 256");
+    if (sh->quant != PA_CUDA_Q8_0 && sh->quant != PA_CUDA_Q4_0)
+        return fail(ctx, PA_CUDA_EUNSUPPORTED, "quant must be Q8_0 (1) or Q4_0 (2)");
+    if (sh->nkv < 1 || sh->nkv > 64) return fail(ctx, PA_CUDA_EINVAL, "nkv out of range");
+    if (sh->rows < 1) return fail(ctx, PA_CUDA_EINVAL, "rows must be >= 1");
+    if (sh->hb != head_bytes(sh->quant, sh->hd)) return fail(ctx, PA_CUDA_EINVAL, "hb does not match quant/hd");
+    if (sh->rs < (uint64_t) sh->nkv * sh->hb) return fail(ctx, PA_CUDA_EINVAL, "rs < nkv * hb");
+    if (sh->rs % 16) return fail(ctx, PA_CUDA_EUNSUPPORTED, "rs must be a multiple of 16 bytes");
+    return PA_CUDA_OK;
+}
+
+// launch shape of the decode kernel for a geometry
+int plan_decode_shape(pa_cuda_ctx *ctx, pa_cuda_plan *p) {
+    const pa_cuda_shape &sh = p->sh;
+    const uint32_t maxw = sh.hd == 128 ? 16 : 12;
+    p->n_rg = (sh.rows + 7) / 8;
+    uint32_t hg = 0;
+    for (uint32_t c = std::min(sh.nkv, maxw); c >= 1; c--) {
+        if (sh.nkv % c) continue;
+        if ((c * sh.hb) % 16) continue;
+        hg = c;
+        break;
+    }
+    if (!hg) return fail(ctx, PA_CUDA_EUNSUPPORTED, "no head grouping gives 16-byte aligned rows (nkv * hb)");
+    p->hg = hg;
+    p->rgc = std::min(p->n_rg, maxw / hg);
+    const uint32_t S = hg * p->rgc;
+    p->pw = 2 * S <= maxw ? 2 : 1;
+    p->n_consumers = S * p->pw;
+    p->grid_y = (sh.nkv / hg) * ((p->n_rg + p->rgc - 1) / p->rgc);
+    uint32_t str = (uint32_t) ((hg * sh.hb + 15) / 16 * 16);
+    if ((str / 16) % 2 == 0) str += 16;
+    p->str = str;
+    p->smem = (size_t) pa::dec::NSTAGE * 2 * pa::dec::STAGE_KEYS * str + pa::dec::SMEM_SLACK +
+              (2 * pa::dec::NSTAGE + 3) * 8 + 16;
+    if (p->smem > (size_t) kMaxSmem) return fail(ctx, PA_CUDA_EUNSUPPORTED, "rows of this head group do not fit shared memory");
+    return PA_CUDA_OK;
+}
+
+template <int HD, int Q>
+cudaError_t launch_decode(const pa_cuda_plan *p, const pa::dec::Params &prm, cudaStream_t st) {
+    auto kern = pa::dec::decode_kernel<HD, Q>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) p->smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid(p->n_jobs, p->grid_y);
+    kern<<<grid, 32 * (p->n_consumers + 1), p->smem, st>>>(prm);
+    return cudaGetLastError();
+}
+
+template <int HD>
+cudaError_t launch_merge(const pa::mrg::Params &mp, cudaStream_t st) {
+    const uint64_t warps = (uint64_t) mp.n_sets * mp.rows_per_set;
+    if (warps == 0) return cudaSuccess;
+    pa::mrg::merge_kernel<HD><<<(unsigned) ((warps + 7) / 8), 256, 0, st>>>(mp);
+    return cudaGetLastError();
+}
+
+int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, cudaStream_t st) {
+    pa_cuda_ctx *ctx = p->ctx;
+    const pa_cuda_shape &sh = p->sh;
+    if (p->n_jobs > 0) {
+        pa::dec::Params prm{};
+        prm.jobs = p->d_jobs;
+        prm.Qs = Qs;
+        prm.Op = p->d_op;
+        prm.Mp = p->d_mp;
+        prm.Lp = p->d_lp;
+        prm.status = ctx->d_status;
+        prm.rs = sh.rs;
+        prm.hb = sh.hb;
+        prm.nkv = sh.nkv;
+        prm.rows = sh.rows;
+        prm.hg = p->hg;
+        prm.rgc = p->rgc;
+        prm.n_rg = p->n_rg;
+        prm.str = p->str;
+        prm.pw = p->pw;
+        prm.n_consumers = p->n_consumers;
+        prm.timeout_ns = ctx->timeout_ns;
+        prm.stall = ctx->stall_test;
+        cudaError_t e;
+        if (sh.hd == 128) e = sh.quant == PA_CUDA_Q8_0 ? launch_decode<128, 1>(p, prm, st) : launch_decode<128, 2>(p, prm, st);
+        else e = sh.quant == PA_CUDA_Q8_0 ? launch_decode<256, 1>(p, prm, st) : launch_decode<256, 2>(p, prm, st);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "decode kernel launch");
+        ctx->launches++;
+    }
+    pa::mrg::Params mp{};
+    mp.Op = p->d_op;
+    mp.Mp = p->d_mp;
+    mp.Lp = p->d_lp;
+    mp.c_range = p->d_crange;
+    mp.n_parts = p->n_slots;
+    mp.part_rows = (uint64_t) sh.nkv * sh.rows;
+    mp.set_rows = 0;
+    mp.O = O;
+    mp.M = m;
+    mp.L = l;
+    mp.rows_per_set = (uint64_t) sh.nkv * sh.rows;
+    mp.n_sets = p->n_sets;
+    mp.fold = 0;
+    cudaError_t e = sh.hd == 128 ? launch_merge<128>(mp, st) : launch_merge<256>(mp, st);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "merge kernel launch");
+    ctx->launches++;
+    return PA_CUDA_OK;
+}
+
+template <class T>
+int ensure_dev(pa_cuda_ctx *ctx, T *&ptr, size_t &cap, size_t bytes) {
+    if (cap >= bytes && ptr) return PA_CUDA_OK;
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    cap = 0;
+    cudaError_t e = cudaMalloc((void **) &ptr, std::max<size_t>(bytes, 256));
+    if (e != cudaSuccess) return fail(ctx, PA_CUDA_ENOMEM, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+    cap = std::max<size_t>(bytes, 256);
+    return PA_CUDA_OK;
+}
+template <class T>
+int ensure_host(pa_cuda_ctx *ctx, T *&ptr, size_t &cap, size_t bytes) {
+    if (cap >= bytes && ptr) return PA_CUDA_OK;
+    if (ptr) cudaFreeHost(ptr);
+    ptr = nullptr;
+    cap = 0;
+    cudaError_t e = cudaMallocHost((void **) &ptr, std::max<size_t>(bytes, 256));
+    if (e != cudaSuccess) return fail(ctx, PA_CUDA_ENOMEM, std::string("cudaMallocHost: ") + cudaGetErrorString(e));
+    cap = std::max<size_t>(bytes, 256);
+    return PA_CUDA_OK;
+}
+
+}  // namespace
+
+// ====================================================================================================== C ABI
+extern "C" {
+
+int pa_cuda_abi_version(void) { return PA_CUDA_ABI_VERSION; }
+
+int pa_cuda_available(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return 0;
+    }
+    int dev = 0, major = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return 0;
+    if (major != 10) return 0;
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, pa::dec::decode_kernel<128, 1>) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return 1;
+}
+
+int pa_cuda_create(int device, pa_cuda_ctx **out) {
+    if (!out) return PA_CUDA_EINVAL;
+    *out = nullptr;
+    auto *ctx = new pa_cuda_ctx();
+    ctx->device = device;
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) { delete ctx; return PA_CUDA_ECUDA; }
+    cudaDeviceGetAttribute(&ctx->n_sm, cudaDevAttrMultiProcessorCount, device);
+    if ((e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaMalloc((void **) &ctx->d_status, 16)) != cudaSuccess ||
+        (e = cudaMemset(ctx->d_status, 0, 16)) != cudaSuccess || (e = cudaEventCreate(&ctx->ev_begin)) != cudaSuccess ||
+        (e = cudaEventCreate(&ctx->ev_end)) != cudaSuccess) {
+        pa_cuda_destroy(ctx);
+        return PA_CUDA_ECUDA;
+    }
+    *out = ctx;
+    return PA_CUDA_OK;
+}
+
+void pa_cuda_destroy(pa_cuda_ctx *ctx) {
+    if (!ctx) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+    if (ctx->eng_plan) pa_cuda_plan_destroy(ctx->eng_plan);
+    if (ctx->h_q) cudaFreeHost(ctx->h_q);
+    if (ctx->h_out) cudaFreeHost(ctx->h_out);
+    if (ctx->d_q) cudaFree(ctx->d_q);
+    if (ctx->d_out) cudaFree(ctx->d_out);
+    if (ctx->ev_begin) cudaEventDestroy(ctx->ev_begin);
+    if (ctx->ev_end) cudaEventDestroy(ctx->ev_end);
+    if (ctx->d_status) cudaFree(ctx->d_status);
+    if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    delete ctx;
+}
+
+const char *pa_cuda_last_error(const pa_cuda_ctx *ctx) { return ctx ? ctx->err.c_str() : "no context"; }
+
+void pa_cuda_set_timeout_ns(pa_cuda_ctx *ctx, uint64_t ns) {
+    if (ctx) ctx->timeout_ns = ns;
+}
+
+uint64_t pa_cuda_launch_count(const pa_cuda_ctx *ctx) { return ctx ? ctx->launches : 0; }
+
+void pa_cuda_set_stall_test(pa_cuda_ctx *ctx, int on) {
+    if (ctx) ctx->stall_test = on ? 1 : 0;
+}
+
+int pa_cuda_status(pa_cuda_ctx *ctx, void *stream) {
+    if (!ctx) return PA_CUDA_EINVAL;
+    cudaStream_t st = pick(ctx, stream);
+    PA_CK(cudaStreamSynchronize(st), "stream synchronize");
+    int h = 0;
+    PA_CK(cudaMemcpy(&h, ctx->d_status, sizeof h, cudaMemcpyDeviceToHost), "status read");
+    if (h != pa::ST_OK) {
+        PA_CK(cudaMemset(ctx->d_status, 0, sizeof h), "status clear");
+        return fail(ctx, PA_CUDA_ETIMEOUT, "a kernel gave up a bounded wait (code " + std::to_string(h) + ")");
+    }
+    return PA_CUDA_OK;
+}
+
+int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n_sets, const pa_cuda_seg *segs,
+                        uint32_t n_segs, uint32_t chunk_keys, pa_cuda_plan **out) {
+    if (!ctx || !out) return PA_CUDA_EINVAL;
+    *out = nullptr;
+    int rc = check_shape(ctx, shape);
+    if (rc) return rc;
+    if (n_segs && !segs) return fail(ctx, PA_CUDA_EINVAL, "segs is null");
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, PA_CUDA_ECUDA, "cudaSetDevice");
+    auto *p = new pa_cuda_plan();
+    p->ctx = ctx;
+    p->sh = *shape;
+    p->n_sets = n_sets;
+    if ((rc = plan_decode_shape(ctx, p))) { delete p; return rc; }
+
+    uint64_t total = 0;
+    for (uint32_t i = 0; i < n_segs; i++) {
+        if (segs[i].set >= n_sets) { delete p; return fail(ctx, PA_CUDA_EINVAL, "segment set index >= n_sets"); }
+        if (segs[i].nk && (((uintptr_t) segs[i].k | (uintptr_t) segs[i].v) & 15)) {
+            delete p;
+            return fail(ctx, PA_CUDA_EINVAL, "segment K/V pointers must be 16-byte aligned");
+        }
+        total += segs[i].nk;
+    }
+    uint32_t chunk = chunk_keys;
+    if (chunk == 0) {
+        // about 16 waves of CTAs over the SMs (one CTA per SM), 128..16384 keys per job
+        const uint64_t per_y = std::max<uint64_t>(1, (uint64_t) ctx->n_sm * 16 / std::max<uint32_t>(1, p->grid_y));
+        chunk = (uint32_t) std::min<uint64_t>(16384, std::max<uint64_t>(128, (total + per_y - 1) / per_y));
+    }
+    chunk = (chunk + 31) / 32 * 32;
+
+    // jobs grouped by set, so that the slots of a set are contiguous
+    std::vector<pa::dec::Job> jobs;
+    std::vector<uint32_t> crange(n_sets + 1, 0);
+    for (uint32_t s = 0; s < n_sets; s++) {
+        crange[s] = (uint32_t) jobs.size();
+        for (uint32_t i = 0; i < n_segs; i++) {
+            if (segs[i].set != s || segs[i].nk == 0) continue;
+            const uint32_t nk = segs[i].nk;
+            const uint32_t nj = (nk + chunk - 1) / chunk;
+            const uint32_t cj = ((nk + nj - 1) / nj + 31) / 32 * 32;   // equal chunks of whole stages
+            for (uint32_t k0 = 0; k0 < nk; k0 += cj) {
+                pa::dec::Job j;
+                j.k = segs[i].k;
+                j.v = segs[i].v;
+                j.key0 = k0;
+                j.nk = std::min(cj, nk - k0);
+                j.set = s;
+                j.slot = (uint32_t) jobs.size();
+                jobs.push_back(j);
+            }
+        }
+    }
+    crange[n_sets] = (uint32_t) jobs.size();
+    p->n_jobs = p->n_slots = (uint32_t) jobs.size();
+    if (p->n_jobs > 0 && p->grid_y > 65535) { delete p; return fail(ctx, PA_CUDA_EUNSUPPORTED, "too many head/row groups"); }
+
+    const size_t rows_all = (size_t) shape->nkv * shape->rows;
+    const size_t op_b = (size_t) p->n_slots * rows_all * shape->hd * 4, ml_b = (size_t) p->n_slots * rows_all * 4;
+    p->scratch = op_b + 2 * ml_b;
+    cudaError_t e = cudaSuccess;
+    if (p->n_jobs) {
+        if ((e = cudaMalloc((void **) &p->d_jobs, jobs.size() * sizeof(pa::dec::Job))) == cudaSuccess &&
+            (e = cudaMalloc((void **) &p->d_op, op_b)) == cudaSuccess &&
+            (e = cudaMalloc((void **) &p->d_mp, ml_b)) == cudaSuccess &&
+            (e = cudaMalloc((void **) &p->d_lp, ml_b)) == cudaSuccess)
+            e = cudaMemcpy(p->d_jobs, jobs.data(), jobs.size() * sizeof(pa::dec::Job), cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess && (e = cudaMalloc((void **) &p->d_crange, crange.size() * 4)) == cudaSuccess)
+        e = cudaMemcpy(p->d_crange, crange.data(), crange.size() * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        pa_cuda_plan_destroy(p);
+        return fail(ctx, PA_CUDA_ENOMEM, std::string("plan allocation: ") + cudaGetErrorString(e));
+    }
+    *out = p;
+    return PA_CUDA_OK;
+}
+
+size_t pa_cuda_plan_scratch_bytes(const pa_cuda_plan *p) { return p ? p->scratch : 0; }
+uint32_t pa_cuda_plan_jobs(const pa_cuda_plan *p) { return p ? p->n_jobs : 0; }
+uint32_t pa_cuda_plan_launches(const pa_cuda_plan *p) { return p ? (p->n_jobs ? 2u : 1u) : 0u; }
+
+int pa_cuda_plan_run(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, void *stream) {
+    if (!p) return PA_CUDA_EINVAL;
+    pa_cuda_ctx *ctx = p->ctx;
+    if (!O || !m || !l || (p->n_jobs && !Qs)) return fail(ctx, PA_CUDA_EINVAL, "null Q/O/m/l");
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, PA_CUDA_ECUDA, "cudaSetDevice");
+    return run_plan(p, Qs, O, m, l, pick(ctx, stream));
+}
+
+void pa_cuda_plan_destroy(pa_cuda_plan *p) {
+    if (!p) return;
+    cudaSetDevice(p->ctx->device);
+    if (p->d_jobs) cudaFree(p->d_jobs);
+    if (p->d_crange) cudaFree(p->d_crange);
+    if (p->d_op) cudaFree(p->d_op);
+    if (p->d_mp) cudaFree(p->d_mp);
+    if (p->d_lp) cudaFree(p->d_lp);
+    delete p;
+}
+
+int pa_cuda_attn(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, const uint16_t *Qs, uint32_t n_sets,
+                 const pa_cuda_seg *segs, uint32_t n_segs, float *O, float *m, float *l, void *stream) {
+    pa_cuda_plan *p = nullptr;
+    int rc = pa_cuda_plan_create(ctx, shape, n_sets, segs, n_segs, 0, &p);
+    if (rc) return rc;
+    rc = pa_cuda_plan_run(p, Qs, O, m, l, stream);
+    cudaStreamSynchronize(pick(ctx, stream));
+    pa_cuda_plan_destroy(p);
+    return rc;
+}
+
+int pa_cuda_scale_q(pa_cuda_ctx *ctx, const float *Q, float scale, uint64_t n, uint16_t *Qs, void *stream) {
+    if (!ctx || (n && (!Q || !Qs))) return fail(ctx, PA_CUDA_EINVAL, "null argument");
+    if (n == 0) return PA_CUDA_OK;
+    cudaSetDevice(ctx->device);
+    const unsigned blocks = (unsigned) std::min<uint64_t>((n + 255) / 256, (uint64_t) ctx->n_sm * 8);
+    pa::mrg::scale_q_kernel<<<blocks, 256, 0, pick(ctx, stream)>>>(Q, scale, n, Qs);
+    PA_CK(cudaGetLastError(), "scale_q launch");
+    ctx->launches++;
+    return PA_CUDA_OK;
+}
+
+int pa_cuda_attn_partial(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, const float *Q, float scale, const uint8_t *K,
+                         const uint8_t *V, uint32_t nk, float *O, float *m, float *l, void *stream) {
+    if (!ctx) return PA_CUDA_EINVAL;
+    int rc = check_shape(ctx, shape);
+    if (rc) return rc;
+    const uint64_t n = (uint64_t) shape->nkv * shape->rows * shape->hd;
+    uint16_t *Qs = nullptr;
+    PA_CK(cudaMalloc((void **) &Qs, n * 2), "cudaMalloc Qs");
+    rc = pa_cuda_scale_q(ctx, Q, scale, n, Qs, stream);
+    if (!rc) {
+        pa_cuda_seg seg{K, V, nk, 0};
+        rc = pa_cuda_attn(ctx, shape, Qs, 1, &seg, nk ? 1u : 0u, O, m, l, stream);
+    }
+    cudaStreamSynchronize(pick(ctx, stream));
+    cudaFree(Qs);
+    if (!rc) rc = pa_cuda_status(ctx, stream);
+    return rc;
+}
+
+int pa_cuda_plan_run_host(pa_cuda_plan *p, const uint16_t *Qs_host, float *O_host, float *m_host, float *l_host,
+                          void *stream) {
+    if (!p) return PA_CUDA_EINVAL;
+    pa_cuda_ctx *ctx = p->ctx;
+    if (!Qs_host || !O_host || !m_host || !l_host) return fail(ctx, PA_CUDA_EINVAL, "null host buffer");
+    cudaSetDevice(ctx->device);
+    cudaStream_t st = pick(ctx, stream);
+    const size_t rows = (size_t) p->n_sets * p->sh.nkv * p->sh.rows;
+    const size_t qb = rows * p->sh.hd * 2, ob = rows * p->sh.hd * 4, mb = rows * 4;
+    int rc;
+    if ((rc = ensure_dev(ctx, ctx->d_q, ctx->d_q_bytes, qb))) return rc;
+    if ((rc = ensure_dev(ctx, ctx->d_out, ctx->d_out_bytes, ob + 2 * mb))) return rc;
+    PA_CK(cudaMemcpyAsync(ctx->d_q, Qs_host, qb, cudaMemcpyHostToDevice, st), "Q to device");
+    float *dO = ctx->d_out, *dm = (float *) ((char *) ctx->d_out + ob), *dl = dm + rows;
+    if ((rc = run_plan(p, ctx->d_q, dO, dm, dl, st))) return rc;
+    PA_CK(cudaMemcpyAsync(O_host, dO, ob, cudaMemcpyDeviceToHost, st), "O to host");
+    PA_CK(cudaMemcpyAsync(m_host, dm, mb, cudaMemcpyDeviceToHost, st), "m to host");
+    PA_CK(cudaMemcpyAsync(l_host, dl, mb, cudaMemcpyDeviceToHost, st), "l to host");
+    PA_CK(cudaStreamSynchronize(st), "stream synchronize");
+    return PA_CUDA_OK;
+}
+
+int pa_cuda_merge(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, uint32_t n_parts, const float *Op, const float *mp,
+                  const float *lp, float *O, float *m, float *l, int fold, void *stream) {
+    if (!ctx) return PA_CUDA_EINVAL;
+    if (hd != 128 && hd != 256) return fail(ctx, PA_CUDA_EUNSUPPORTED, "hd must be 128 or 256");
+    if (!O || !m || !l || (n_parts && (!Op || !mp || !lp))) return fail(ctx, PA_CUDA_EINVAL, "null argument");
+    cudaSetDevice(ctx->device);
+    pa::mrg::Params prm{};
+    prm.Op = Op;
+    prm.Mp = mp;
+    prm.Lp = lp;
+    prm.c_range = nullptr;
+    prm.n_parts = n_parts;
+    prm.part_rows = rows;
+    prm.set_rows = 0;
+    prm.O = O;
+    prm.M = m;
+    prm.L = l;
+    prm.rows_per_set = rows;
+    prm.n_sets = 1;
+    prm.fold = fold ? 1 : 0;
+    cudaError_t e = hd == 128 ? launch_merge<128>(prm, pick(ctx, stream)) : launch_merge<256>(prm, pick(ctx, stream));
+    PA_CK(e, "merge launch");
+    ctx->launches++;
+    return PA_CUDA_OK;
+}
+
+int pa_cuda_normalize(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, const float *O, const float *m, const float *l,
+                      uint16_t *Oh, float *lse, void *stream) {
+    if (!ctx) return PA_CUDA_EINVAL;
+    if (hd != 128 && hd != 256) return fail(ctx, PA_CUDA_EUNSUPPORTED, "hd must be 128 or 256");
+    if (rows == 0) return PA_CUDA_OK;
+    if (!O || !m || !l || !Oh || !lse) return fail(ctx, PA_CUDA_EINVAL, "null argument");
+    cudaSetDevice(ctx->device);
+    const unsigned blocks = (unsigned) ((rows + 7) / 8);
+    if (hd == 128) pa::mrg::normalize_kernel<128><<<blocks, 256, 0, pick(ctx, stream)>>>(O, m, l, rows, Oh, lse);
+    else pa::mrg::normalize_kernel<256><<<blocks, 256, 0, pick(ctx, stream)>>>(O, m, l, rows, Oh, lse);
+    PA_CK(cudaGetLastError(), "normalize launch");
+    ctx->launches++;
+    return PA_CUDA_OK;
+}
+
+// ------------------------------------------------------------------------------------------ pa::engine
+int pa_cuda_alloc_page(pa_cuda_ctx *ctx, size_t bytes, pa_cuda_page *pg) {
+    if (!ctx || !pg) return PA_CUDA_EINVAL;
+    cudaSetDevice(ctx->device);
+    uint8_t *k = nullptr, *v = nullptr;
+    const size_t n = (bytes + 4095) / 4096 * 4096 + 64;   // +64: readable slack past the last row
+    cudaError_t e = cudaMallocManaged((void **) &k, n, cudaMemAttachGlobal);
+    if (e == cudaSuccess) e = cudaMallocManaged((void **) &v, n, cudaMemAttachGlobal);
+    if (e != cudaSuccess) {
+        if (k) cudaFree(k);
+        return fail(ctx, PA_CUDA_ENOMEM, std::string("page allocation: ") + cudaGetErrorString(e));
+    }
+#if CUDART_VERSION >= 13000
+    cudaMemLocation loc{cudaMemLocationTypeDevice, ctx->device};
+    cudaMemAdvise(k, n, cudaMemAdviseSetPreferredLocation, loc);
+    cudaMemAdvise(v, n, cudaMemAdviseSetPreferredLocation, loc);
+#else
+    cudaMemAdvise(k, n, cudaMemAdviseSetPreferredLocation, ctx->device);
+    cudaMemAdvise(v, n, cudaMemAdviseSetPreferredLocation, ctx->device);
+#endif
+    cudaGetLastError();
+    pg->k = k;
+    pg->v = v;
+    pg->hk = k;
+    pg->hv = v;
+    return PA_CUDA_OK;
+}
+
+void pa_cuda_free_page(pa_cuda_ctx *ctx, pa_cuda_page *pg) {
+    if (!ctx || !pg) return;
+    cudaSetDevice(ctx->device);
+    if (ctx->eng_active) cudaStreamSynchronize(ctx->stream);
+    if (pg->k) cudaFree(pg->k);
+    if (pg->v) cudaFree(pg->v);
+    pg->k = pg->v = nullptr;
+    pg->hk = pg->hv = nullptr;
+}
+
+int pa_cuda_begin(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *nkeys, int n_pages,
+                  const uint16_t *Qs_host, const pa_cuda_shape *shape, int ng, int ntok) {
+    if (!ctx) return PA_CUDA_EINVAL;
+    if (ctx->eng_active) return fail(ctx, PA_CUDA_EINVAL, "begin while a call is in flight (call end first)");
+    if (ng < 1 || n_pages < 0 || (n_pages && (!pages || !nkeys)) || !Qs_host)
+        return fail(ctx, PA_CUDA_EINVAL, "bad begin arguments");
+    cudaSetDevice(ctx->device);
+    const int NR = 48;
+    pa_cuda_shape sh = *shape;
+    const int nt = (ng == 1 && ntok >= 1 && ntok < 8) ? ntok : 0;   // packed real rows (pa-metal.mm:627-646)
+    sh.rows = nt ? 6u * (uint32_t) nt : (uint32_t) NR;
+    int rc = check_shape(ctx, &sh);
+    if (rc) return rc;
+    const uint32_t nkv = sh.nkv, hd = sh.hd;
+    // one output set per group
+    ctx->eng_segs.clear();
+    for (int g = 0; g < ng; g++)
+        for (int i = 0; i < n_pages; i++)
+            if (nkeys[i]) ctx->eng_segs.push_back(pa_cuda_seg{pages[i].k, pages[i].v, nkeys[i], (uint32_t) g});
+    if (ctx->eng_plan) { pa_cuda_plan_destroy(ctx->eng_plan); ctx->eng_plan = nullptr; }
+    if ((rc = pa_cuda_plan_create(ctx, &sh, (uint32_t) ng, ctx->eng_segs.data(), (uint32_t) ctx->eng_segs.size(), 0,
+                                  &ctx->eng_plan)))
+        return rc;
+    const size_t rows = (size_t) ng * nkv * sh.rows;
+    const size_t qb = rows * hd * 2, ob = rows * hd * 4, mb = rows * 4;
+    if ((rc = ensure_host(ctx, ctx->h_q, ctx->h_q_bytes, qb))) return rc;
+    if ((rc = ensure_host(ctx, ctx->h_out, ctx->h_out_bytes, ob + 2 * mb))) return rc;
+    if ((rc = ensure_dev(ctx, ctx->d_q, ctx->d_q_bytes, qb))) return rc;
+    if ((rc = ensure_dev(ctx, ctx->d_out, ctx->d_out_bytes, ob + 2 * mb))) return rc;
+    // pack Q: wire row r = g*8 + t of head h; packed (nt) row = g*nt + t
+    for (int gi = 0; gi < ng; gi++)
+        for (uint32_t h = 0; h < nkv; h++) {
+            const uint16_t *src = Qs_host + ((size_t) gi * nkv + h) * NR * hd;
+            uint16_t *dst = ctx->h_q + ((size_t) gi * nkv + h) * sh.rows * hd;
+            if (!nt) memcpy(dst, src, (size_t) NR * hd * 2);
+            else
+                for (int gg = 0; gg < 6; gg++) memcpy(dst + (size_t) gg * nt * hd, src + (size_t) gg * 8 * hd, (size_t) nt * hd * 2);
+        }
+    for (int i = 0; i < n_pages; i++) {
+        // stream-ordered migration of pages the host wrote since the last call
+#if CUDART_VERSION >= 13000
+        cudaMemLocation loc{cudaMemLocationTypeDevice, ctx->device};
+        cudaMemPrefetchAsync(pages[i].k, (size_t) nkeys[i] * sh.rs, loc, 0, ctx->stream);
+        cudaMemPrefetchAsync(pages[i].v, (size_t) nkeys[i] * sh.rs, loc, 0, ctx->stream);
+#else
+        cudaMemPrefetchAsync(pages[i].k, (size_t) nkeys[i] * sh.rs, ctx->device, ctx->stream);
+        cudaMemPrefetchAsync(pages[i].v, (size_t) nkeys[i] * sh.rs, ctx->device, ctx->stream);
+#endif
+    }
+    cudaGetLastError();
+    ctx->t_begin = std::chrono::steady_clock::now();
+    PA_CK(cudaEventRecord(ctx->ev_begin, ctx->stream), "event");
+    PA_CK(cudaMemcpyAsync(ctx->d_q, ctx->h_q, qb, cudaMemcpyHostToDevice, ctx->stream), "Q to device");
+    float *dO = ctx->d_out, *dm = (float *) ((char *) ctx->d_out + ob), *dl = dm + rows;
+    if ((rc = run_plan(ctx->eng_plan, ctx->d_q, dO, dm, dl, ctx->stream))) return rc;
+    PA_CK(cudaMemcpyAsync(ctx->h_out, ctx->d_out, ob + 2 * mb, cudaMemcpyDeviceToHost, ctx->stream), "O to host");
+    PA_CK(cudaEventRecord(ctx->ev_end, ctx->stream), "event");
+    ctx->eng_ng = ng;
+    ctx->eng_nt = nt;
+    ctx->eng_rows = (int) sh.rows;
+    ctx->eng_nkv = (int) nkv;
+    ctx->eng_hd = (int) hd;
+    ctx->eng_active = true;
+    return PA_CUDA_OK;
+}
+
+double pa_cuda_end(pa_cuda_ctx *ctx, float *O, float *m, float *l) {
+    if (!ctx || !ctx->eng_active) return -1;
+    ctx->eng_active = false;
+    const int NR = 48, ng = ctx->eng_ng, nt = ctx->eng_nt, nkv = ctx->eng_nkv, hd = ctx->eng_hd, rows = ctx->eng_rows;
+    const size_t out_rows = (size_t) ng * nkv * NR;
+    cudaError_t e = cudaEventSynchronize(ctx->ev_end);
+    const int st = e == cudaSuccess ? pa_cuda_status(ctx, nullptr) : PA_CUDA_ECUDA;
+    if (e != cudaSuccess || st != PA_CUDA_OK) {
+        for (size_t r = 0; r < out_rows; r++) { m[r] = -INFINITY; l[r] = 0; }
+        if (e != cudaSuccess) ctx->err = std::string("GPU call failed: ") + cudaGetErrorString(e);
+        return -1;
+    }
+    float ms = 0;
+    cudaEventElapsedTime(&ms, ctx->ev_begin, ctx->ev_end);
+    ctx->last_exec_ms = ms;
+    const size_t prow = (size_t) ng * nkv * rows;
+    const float *hO = ctx->h_out, *hm = hO + prow * hd, *hl = hm + prow;
+    for (int gi = 0; gi < ng; gi++)
+        for (int h = 0; h < nkv; h++)
+            for (int r = 0; r < NR; r++) {
+                const size_t orow = ((size_t) gi * nkv + h) * NR + r;
+                int pr = r;
+                if (nt) pr = (r % 8) < nt ? (r / 8) * nt + (r % 8) : -1;
+                if (pr < 0) {
+                    memset(O + orow * hd, 0, (size_t) hd * 4);
+                    m[orow] = -INFINITY;
+                    l[orow] = 0;
+                    continue;
+                }
+                const size_t srow = ((size_t) gi * nkv + h) * rows + pr;
+                memcpy(O + orow * hd, hO + srow * hd, (size_t) hd * 4);
+                m[orow] = hm[srow];
+                l[orow] = hl[srow];
+            }
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - ctx->t_begin).count();
+}
+
+double pa_cuda_exec_ms(const pa_cuda_ctx *ctx) { return ctx ? ctx->last_exec_ms : 0; }
+
+}  // extern "C"

@@ -1,0 +1,449 @@
+// pa_decode.cuh - split-K partial attention over quantised (Q8_0 / Q4_0) key/value rows, for the query shapes of
+// decode and verify calls (a few rows per KV head).
+//
+// Reference semantics: pa_attn_big (phone-attn/pa-metal.mm:379-487) and sme_attn_partial
+// (scripts/sme/sme_attn.c:274-306): K/V blocks are dequantised to f16 (f16(d * q)), S = Qs.K^T with fp32
+// accumulation, online softmax in fp32 with P rounded to f16, O = diag(alpha) O + P.V, tail keys masked
+// (pa-metal.mm:452-464). Output per chunk of keys: the unnormalised partial (O, m, l); pa_merge.cuh folds chunks.
+//
+// B200 design (one CTA = one key chunk x a group of heads x a group of query rows):
+//   * a producer warp streams each 32-key stage of K and V rows from HBM into shared memory with 1-D bulk copies
+//     (TMA engine), one copy per key row, into rows padded to an odd number of 16-byte units so the consumers'
+//     32-bit reads hit at most 2 lanes per bank; full/empty mbarriers ring NSTAGE stages;
+//   * each consumer warp owns one (head, 8-row group) and, when there are few such groups, every other 16-key tile;
+//   * the raw int8/int4 bytes go straight from shared memory into registers and are dequantised there into the
+//     operand fragments of mma.m16n8k16 (f16 in, fp32 accumulate), keys on the M side ("swap AB"):
+//       S^T[16 keys][8 rows] = K[16 keys][d] . Qs^T,   O^T[d][8 rows] += V^T[d][16 keys] . P^T
+//     Because QK^T sums over d, the order of d inside a k-step is free: each lane takes whole 4-byte groups of its
+//     own quant block (Q's fragments use the same permutation), so one scale per lane and no unpacking shuffles.
+//     V needs keys in pairs along k: two rows' words are byte-interleaved with one PRMT. P's accumulator fragment
+//     becomes P^T's operand fragment with movmatrix (8x8 transpose).
+#pragma once
+#include "pa_common.cuh"
+
+namespace pa {
+namespace dec {
+
+constexpr int STAGE_KEYS = 32;   // keys per pipeline stage (= lanes of the producer warp)
+constexpr int TILE_KEYS = 16;    // keys per MMA tile
+constexpr int NSTAGE = 3;
+constexpr int SMEM_SLACK = 64;   // readable bytes past the last row (a lane may load one unused word there)
+constexpr uint64_t DRAIN_NS = 1000000000ull;   // bound on waiting for copies in flight after an abort (>= 1 s)
+
+// one chunk of keys of one segment, and where its partial goes
+struct Job {
+    const uint8_t *k, *v;   // segment base (key 0 of the segment)
+    uint32_t key0, nk;      // keys [key0, key0 + nk) of the segment
+    uint32_t set, slot;     // output set (selects Q) and partial slot
+};
+
+struct Params {
+    const Job *jobs;
+    const uint16_t *Qs;   // f16(q*scale) [n_sets][nkv][rows][hd]
+    float *Op;            // partials [slot][nkv][rows][hd]
+    float *Mp, *Lp;       // [slot][nkv][rows]
+    int *status;
+    uint64_t rs, hb;      // bytes per key position; bytes per head in a position
+    uint32_t nkv, rows;
+    uint32_t hg;          // heads per CTA
+    uint32_t rgc;         // 8-row groups per CTA
+    uint32_t n_rg;        // 8-row groups in total = ceil(rows / 8)
+    uint32_t str;         // shared-memory row stride (bytes, multiple of 16, odd number of 16-byte units)
+    uint32_t pw;          // consumer warps per (head, row group): 1 or 2 (they split the 16-key tiles)
+    uint32_t n_consumers; // consumer warps per CTA (launch shape)
+    uint64_t timeout_ns;
+    int stall;            // test hook: consumers first wait on a barrier that nothing completes (bounded)
+};
+
+__host__ __device__ constexpr int q_group_bytes(int quant) { return quant == 1 ? 34 : 18; }
+
+// ---------------------------------------------------------------- d permutations (host + device)
+// QK^T: lane t of a quad feeds k = {2t, 2t+1, 2t+8, 2t+9} of each k-step s. Those 4 values are one 4-byte group of the
+// lane's own quant block. dK(s, t, i) is the head-dim index of the i-th of them (i: 0,1 -> k = 2t,2t+1; 2,3 -> 2t+8,2t+9).
+__host__ __device__ inline int dK(int quant, int s, int t, int i) {
+    const int blk = t + 4 * (s / 8), ss = s % 8;
+    if (quant == 1) {
+        // a pair of q8_0 blocks = 68 bytes = 17 aligned words; even block: (d,q0,q1)(q2..q5)...(q30,q31,d'), odd: d' then
+        // 8 aligned words. The even block's first group joins q0,q1 with q30,q31.
+        int off;
+        if (blk % 2) off = 4 * ss + i;
+        else if (ss == 0) { const int e[4] = {0, 1, 30, 31}; off = e[i]; }
+        else off = 4 * ss - 2 + i;
+        return 32 * blk + off;
+    }
+    // q4_0: a pair of blocks = 36 bytes = 9 words; byte j holds elements j (low nibble) and j+16 (high nibble).
+    // Group (x0,x1,x2,x3) gives k-step 2g: lows (x0,x2 | x1,x3) and k-step 2g+1: highs.
+    const int grp = ss / 2, hi = ss % 2;
+    int j[4];
+    if (blk % 2) { for (int u = 0; u < 4; u++) j[u] = 4 * grp + u; }
+    else if (grp == 0) { j[0] = 0; j[1] = 1; j[2] = 14; j[3] = 15; }
+    else { for (int u = 0; u < 4; u++) j[u] = 4 * grp - 2 + u; }
+    const int order[4] = {j[0], j[2], j[1], j[3]};
+    return 32 * blk + 16 * hi + order[i];
+}
+
+// P.V: lane g of the A fragment (V^T) holds two head-dim rows per m-tile mt: dV(mt, g, 0) (row g) and dV(mt, g, 1)
+// (row g + 8). Lane g owns a contiguous byte range of one quant block.
+__host__ __device__ inline int dV(int quant, int hd, int mt, int g, int half) {
+    if (quant == 1) {
+        const int base = hd == 128 ? 16 * g : 32 * g;
+        return base + 2 * mt + half;
+    }
+    const int b = hd == 128 ? g / 2 : g;
+    const int e0 = hd == 128 ? 8 * (g % 2) : 0;
+    const int u = mt / 2, e = e0 + 2 * u;
+    return 32 * b + e + (mt % 2 ? 16 : 0) + half;
+}
+
+// ---------------------------------------------------------------- fragment builders
+// 4 int8 values (one aligned word) -> two f16x2 of f16(d * q): (v0,v1) and (v2,v3)
+__device__ __forceinline__ void q8_word(uint32_t w, uint32_t s2, uint32_t &lo, uint32_t &hi) {
+    const uint32_t u = w ^ 0x80808080u;                       // q + 128
+    const uint32_t magic = 0x64646464u;
+    lo = hmul2(hsub2(prmt(u, magic, 0x4140u), 0x64806480u), s2);   // (1024 + u) - 1152 = q
+    hi = hmul2(hsub2(prmt(u, magic, 0x4342u), 0x64806480u), s2);
+}
+// 4 bytes of q4_0 nibbles -> (x0.lo, x2.lo), (x1.lo, x3.lo), (x0.hi, x2.hi), (x1.hi, x3.hi) as f16x2 of f16(d*(n-8))
+__device__ __forceinline__ void q4_word(uint32_t w, uint32_t s2, uint32_t &l02, uint32_t &l13, uint32_t &h02,
+                                        uint32_t &h13) {
+    const uint32_t m = 0x000F000Fu, magic = 0x64006400u, off = 0x64086408u;   // (1024 + n) - 1032 = n - 8
+    l02 = hmul2(hsub2(and_or(w, m, magic), off), s2);
+    l13 = hmul2(hsub2(and_or(w >> 8, m, magic), off), s2);
+    h02 = hmul2(hsub2(and_or(w >> 4, m, magic), off), s2);
+    h13 = hmul2(hsub2(and_or(w >> 12, m, magic), off), s2);
+}
+
+// ---------------------------------------------------------------- the kernel
+template <int HD, int QUANT>
+__global__ void __launch_bounds__(32 * (HD == 128 ? 17 : 13), 1) decode_kernel(const Params p) {
+    constexpr int NMT = HD / 16;   // k-steps of QK^T = m-tiles of P.V
+    constexpr int GB = q_group_bytes(QUANT);
+    constexpr int PAIR = 2 * GB;   // bytes of an aligned pair of quant blocks
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t str = p.str;
+    const uint32_t stage_bytes = 2u * STAGE_KEYS * str;   // K rows then V rows
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + NSTAGE * stage_bytes + SMEM_SLACK);
+    uint64_t *empty = full + NSTAGE;
+    uint64_t *done = empty + NSTAGE;   // every active consumer is past the pipeline (stage memory is free)
+    uint64_t *xchg = done + 1;         // the second warp of each (head, row group) pair has published its partial
+    uint64_t *never = xchg + 1;        // completed by nobody: the stall test hook waits on it
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(never + 1);
+
+    const Job job = p.jobs[blockIdx.x];
+    const uint32_t n_hgroups = p.nkv / p.hg;
+    const uint32_t hgi = blockIdx.y % n_hgroups, rbi = blockIdx.y / n_hgroups;
+    const uint32_t h0 = hgi * p.hg;
+    const uint32_t rg0 = rbi * p.rgc;
+    const uint32_t nrg = min(p.rgc, p.n_rg - rg0);
+    const uint32_t S = p.hg * nrg;                // (head, row group) streams in this CTA
+    const uint32_t n_active = S * p.pw;           // consumer warps with work
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t n_stages = (job.nk + STAGE_KEYS - 1) / STAGE_KEYS;
+    const uint32_t copy_bytes = (uint32_t) (p.hg * p.hb);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NSTAGE; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], n_active); }
+        mbar_init(done, n_active);
+        mbar_init(xchg, S);
+        mbar_init(never, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == p.n_consumers) {
+        // ------------------------------------------------ producer warp
+        const uint8_t *kb = job.k + (uint64_t) job.key0 * p.rs + h0 * p.hb;
+        const uint8_t *vb = job.v + (uint64_t) job.key0 * p.rs + h0 * p.hb;
+        uint32_t issued = 0;
+        bool ok = true;
+        for (uint32_t it = 0; it < n_stages; it++) {
+            const uint32_t s = it % NSTAGE;
+            if (it >= NSTAGE) {
+                bool w = true;
+                if (lane == 0) w = mbar_wait_bounded(&empty[s], ((it / NSTAGE) & 1) ^ 1, p.timeout_ns, abort_flag);
+                w = __shfl_sync(0xffffffffu, w, 0);
+                if (!w) { ok = false; break; }
+            }
+            const uint32_t valid = min((uint32_t) STAGE_KEYS, job.nk - it * STAGE_KEYS);
+            if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * valid * copy_bytes);
+            __syncwarp();
+            if (lane < valid) {
+                const uint64_t off = (uint64_t) (it * STAGE_KEYS + lane) * p.rs;
+                uint8_t *dst = smem + s * stage_bytes + lane * str;
+                bulk_g2s(dst, kb + off, copy_bytes, &full[s]);
+                bulk_g2s(dst + STAGE_KEYS * str, vb + off, copy_bytes, &full[s]);
+            }
+            issued = it + 1;
+        }
+        if (!ok) {
+            // consumers gave up: let the copies already issued land before the CTA exits
+            if (lane == 0) {
+                *abort_flag = 1;
+                atomicCAS(p.status, ST_OK, ST_TIMEOUT_EMPTY);
+                const uint32_t first = issued > NSTAGE ? issued - NSTAGE : 0;
+                const uint64_t drain_ns = p.timeout_ns > DRAIN_NS ? p.timeout_ns : DRAIN_NS;
+                for (uint32_t it = first; it < issued; it++)
+                    if (!mbar_wait_bounded(&full[it % NSTAGE], (it / NSTAGE) & 1, drain_ns, nullptr))
+                        atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
+            }
+        }
+        return;
+    }
+    if (warp >= n_active) return;
+
+    // ------------------------------------------------ consumer warps
+    const uint32_t stream = warp % S, par = warp / S;
+    const uint32_t hl = stream % p.hg, rgl = stream / p.hg;
+    const uint32_t h = h0 + hl, rg = rg0 + rgl;
+    const uint32_t g = lane / 4, t = lane % 4;
+    const uint32_t hoff = hl * (uint32_t) p.hb;
+
+    // Q fragments (B operand of S^T = K.Q^T): row n = g of this row group, k values permuted as dK
+    uint32_t qf[NMT][2];
+    {
+        const uint32_t row = rg * 8 + g;
+        const uint16_t *q = p.Qs + (((uint64_t) job.set * p.nkv + h) * p.rows + (row < p.rows ? row : 0)) * HD;
+#pragma unroll
+        for (int s = 0; s < NMT; s++) {
+            uint16_t v[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) v[i] = row < p.rows ? q[dK(QUANT, s, t, i)] : (uint16_t) 0;
+            qf[s][0] = (uint32_t) v[0] | ((uint32_t) v[1] << 16);
+            qf[s][1] = (uint32_t) v[2] | ((uint32_t) v[3] << 16);
+        }
+    }
+
+    float o[NMT][4];
+#pragma unroll
+    for (int mt = 0; mt < NMT; mt++) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    float m0 = M_EMPTY, m1 = M_EMPTY, l0 = 0.f, l1 = 0.f;   // rows 2t, 2t+1 of the 8-row group
+    bool ok = true;
+    if (p.stall && !mbar_wait_bounded(never, 0, p.timeout_ns, abort_flag)) ok = false;
+
+    for (uint32_t it = 0; ok && it < n_stages; it++) {
+        const uint32_t s = it % NSTAGE;
+        if (!mbar_wait_bounded(&full[s], (it / NSTAGE) & 1, p.timeout_ns, abort_flag)) { ok = false; break; }
+        const uint32_t valid = min((uint32_t) STAGE_KEYS, job.nk - it * STAGE_KEYS);
+        const uint32_t kbase = smem_u32(smem + s * stage_bytes) + hoff;
+        const uint32_t vbase = kbase + STAGE_KEYS * str;
+        for (uint32_t tt = par; tt < STAGE_KEYS / TILE_KEYS; tt += p.pw) {
+            const int tvalid = (int) valid - (int) tt * TILE_KEYS;
+            if (tvalid <= 0) break;
+            const uint32_t tk = kbase + tt * TILE_KEYS * str;
+            const uint32_t tv = vbase + tt * TILE_KEYS * str;
+
+            // ---- S^T = K . Qs^T  (lane: keys g, g+8; its quant block(s) t (+4))
+            float c[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int rep = 0; rep < HD / 128; rep++) {
+                const int blk = t + 4 * rep;
+                const uint32_t odd = blk % 2;
+                const uint32_t pb = (uint32_t) (PAIR * (blk / 2));
+                constexpr int NWK = QUANT == 1 ? 9 : 5;   // aligned words covering the lane's block (+ its scale)
+                uint32_t w[2][NWK], s2[2];
+#pragma unroll
+                for (int kk = 0; kk < 2; kk++) {
+                    const uint32_t rb = tk + (g + 8 * kk) * str + pb + 4 * (odd ? NWK - 1 : 0);
+#pragma unroll
+                    for (int i = 0; i < NWK; i++) w[kk][i] = lds32(rb + 4 * i);
+                    // scale: even block -> first word bytes 0-1; odd block -> first word (shared with the even block) bytes 2-3
+                    s2[kk] = prmt(w[kk][0], w[kk][0], odd ? 0x3232u : 0x1010u);
+                }
+                if (QUANT == 1) {
+#pragma unroll
+                    for (int ss = 0; ss < 8; ss++) {
+                        uint32_t lo[2], hi[2];
+#pragma unroll
+                        for (int kk = 0; kk < 2; kk++) {
+                            // odd block: words 1..8 are its 32 values; even block: (q0,q1 | q30,q31), then words 1..7
+                            const uint32_t grp = odd ? w[kk][1 + ss] : (ss == 0 ? prmt(w[kk][0], w[kk][8], 0x5432u) : w[kk][ss]);
+                            q8_word(grp, s2[kk], lo[kk], hi[kk]);
+                        }
+                        const int sidx = 8 * rep + ss;
+                        mma16816(c, lo[0], lo[1], hi[0], hi[1], qf[sidx][0], qf[sidx][1]);
+                    }
+                } else {
+#pragma unroll
+                    for (int gi = 0; gi < 4; gi++) {
+                        uint32_t l02[2], l13[2], h02[2], h13[2];
+#pragma unroll
+                        for (int kk = 0; kk < 2; kk++) {
+                            const uint32_t grp = odd ? w[kk][1 + gi] : (gi == 0 ? prmt(w[kk][0], w[kk][4], 0x5432u) : w[kk][gi]);
+                            q4_word(grp, s2[kk], l02[kk], l13[kk], h02[kk], h13[kk]);
+                        }
+                        const int sidx = 8 * rep + 2 * gi;
+                        mma16816(c, l02[0], l02[1], l13[0], l13[1], qf[sidx][0], qf[sidx][1]);
+                        mma16816(c, h02[0], h02[1], h13[0], h13[1], qf[sidx + 1][0], qf[sidx + 1][1]);
+                    }
+                }
+            }
+
+            // ---- online softmax over this tile (rows 2t, 2t+1; keys g, g+8)
+            if (tvalid < TILE_KEYS) {
+                if ((int) g >= tvalid) c[0] = c[1] = -INFINITY;
+                if ((int) g + 8 >= tvalid) c[2] = c[3] = -INFINITY;
+            }
+            float mx0 = fmaxf(c[0], c[2]), mx1 = fmaxf(c[1], c[3]);
+#pragma unroll
+            for (int x = 4; x < 32; x <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, x));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, x));
+            }
+            const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+            const float al0 = ex2((m0 - mn0) * LOG2E), al1 = ex2((m1 - mn1) * LOG2E);
+            const float b0 = -mn0 * LOG2E, b1 = -mn1 * LOG2E;
+            const float p0 = ex2(fmaf(c[0], LOG2E, b0)), p1 = ex2(fmaf(c[1], LOG2E, b1));
+            const float p2 = ex2(fmaf(c[2], LOG2E, b0)), p3 = ex2(fmaf(c[3], LOG2E, b1));
+            l0 = fmaf(l0, al0, p0 + p2);
+            l1 = fmaf(l1, al1, p1 + p3);
+            m0 = mn0;
+            m1 = mn1;
+            if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
+#pragma unroll
+                for (int mt = 0; mt < NMT; mt++) { o[mt][0] *= al0; o[mt][1] *= al1; o[mt][2] *= al0; o[mt][3] *= al1; }
+            }
+            const uint32_t pb0 = movtrans(pack_h2(p0, p1));   // P^T keys 2t,2t+1 for row g
+            const uint32_t pb1 = movtrans(pack_h2(p2, p3));   // keys 2t+8, 2t+9
+
+            // ---- O^T += V^T . P^T  (lane: keys 2t,2t+1,2t+8,2t+9; head-dim rows dV(mt, g, 0/1))
+            {
+                const uint32_t key[4] = {2 * t, 2 * t + 1, 2 * t + 8, 2 * t + 9};
+                // the lane's data bytes start 2 bytes into a word for even quant blocks: load the covering words and
+                // shift them into alignment (funnel shift by 8*sig bits; sig is 0 or 2), so every later index is static
+                constexpr int NB = QUANT == 1 ? (HD == 128 ? 16 : 32) : (HD == 128 ? 8 : 16);   // bytes per lane per key
+                constexpr int NW = NB / 4;
+                const int b = HD == 128 ? (int) g / 2 : (int) g;
+                const int hh = HD == 128 ? (int) g % 2 : 0;
+                const uint32_t pb = (uint32_t) (PAIR * (b / 2));
+                const uint32_t start = QUANT == 1 ? pb + ((b % 2) ? 36u : 2u) + 16u * hh : pb + ((b % 2) ? 20u : 2u) + 8u * hh;
+                const uint32_t sig = start % 4, wa = start - sig, shift = 8 * sig;
+                const uint32_t soff = pb + ((b % 2) ? (uint32_t) GB : 0u);
+                uint32_t sc[4];
+                uint32_t W[4][NW];
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const uint32_t rb = tv + key[kk] * str;
+                    sc[kk] = lds16(rb + soff);
+                    uint32_t raw[NW + 1];
+#pragma unroll
+                    for (int i = 0; i < NW; i++) raw[i] = lds32(rb + wa + 4 * i);
+                    raw[NW] = sig ? lds32(rb + wa + 4 * NW) : 0u;
+#pragma unroll
+                    for (int i = 0; i < NW; i++) W[kk][i] = __funnelshift_r(raw[i], raw[i + 1], shift);
+                }
+                // key pairs: (key0,key1) -> a0/a1, (key2,key3) -> a2/a3
+                const uint32_t s01 = sc[0] | (sc[1] << 16), s23 = sc[2] | (sc[3] << 16);
+                if (QUANT == 1) {
+#pragma unroll
+                    for (int mt = 0; mt < NMT; mt++) {
+                        constexpr uint32_t SEL[2] = {0x5140u, 0x7362u};   // (a.e, b.e, a.e+1, b.e+1), e = 2mt
+                        const int wi = mt / 2;
+                        uint32_t lo01, hi01, lo23, hi23;
+                        q8_word(prmt(W[0][wi], W[1][wi], SEL[mt % 2]), s01, lo01, hi01);
+                        q8_word(prmt(W[2][wi], W[3][wi], SEL[mt % 2]), s23, lo23, hi23);
+                        mma16816(o[mt], lo01, hi01, lo23, hi23, pb0, pb1);
+                    }
+                } else {
+#pragma unroll
+                    for (int u = 0; u < NMT / 2; u++) {
+                        constexpr uint32_t SEL[2] = {0x5410u, 0x7632u};   // (a.e, a.e+1, b.e, b.e+1), e = 2u
+                        const int wi = u / 2;
+                        uint32_t a_l0, a_l1, a_h0, a_h1, c_l0, c_l1, c_h0, c_h1;
+                        // q4_word on an interleaved word: l02 = byte e low nibble (keys a,b), l13 = byte e+1 low,
+                        // h02 = byte e high, h13 = byte e+1 high
+                        q4_word(prmt(W[0][wi], W[1][wi], SEL[u % 2]), s01, a_l0, a_l1, a_h0, a_h1);
+                        q4_word(prmt(W[2][wi], W[3][wi], SEL[u % 2]), s23, c_l0, c_l1, c_h0, c_h1);
+                        mma16816(o[2 * u], a_l0, a_l1, c_l0, c_l1, pb0, pb1);       // rows g <- e, g+8 <- e+1
+                        mma16816(o[2 * u + 1], a_h0, a_h1, c_h0, c_h1, pb0, pb1);   // rows g <- e+16, g+8 <- e+17
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (!ok) {
+        if (lane == 0) { *abort_flag = 1; atomicCAS(p.status, ST_OK, ST_TIMEOUT_FULL); }
+        return;
+    }
+
+    // ---- finish: l summed over the lanes of a row (keys g), then the partner warp (if any) folded in
+#pragma unroll
+    for (int x = 4; x < 32; x <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, x);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, x);
+    }
+    if (p.pw == 2) {
+        // the pair's second warp publishes its partial through stage memory once every consumer is past the pipeline;
+        // both waits are bounded, so a consumer that gave up cannot leave the others waiting
+        __syncwarp();
+        if (lane == 0) mbar_arrive(done);
+        float *xb = reinterpret_cast<float *>(smem) + (size_t) stream * (NMT * 4 + 4) * 32;
+        if (par == 1) {
+            bool w = true;
+            if (lane == 0) w = mbar_wait_bounded(done, 0, p.timeout_ns, abort_flag);
+            if (!__shfl_sync(0xffffffffu, w, 0)) {
+                if (lane == 0) { *abort_flag = 1; atomicCAS(p.status, ST_OK, ST_TIMEOUT_FULL); }
+                return;
+            }
+#pragma unroll
+            for (int mt = 0; mt < NMT; mt++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) xb[(mt * 4 + j) * 32 + lane] = o[mt][j];
+            xb[(NMT * 4 + 0) * 32 + lane] = m0;
+            xb[(NMT * 4 + 1) * 32 + lane] = m1;
+            xb[(NMT * 4 + 2) * 32 + lane] = l0;
+            xb[(NMT * 4 + 3) * 32 + lane] = l1;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(xchg);   // release: the writes above are visible to the waiter
+            return;
+        }
+        bool w = true;
+        if (lane == 0) w = mbar_wait_bounded(xchg, 0, p.timeout_ns, abort_flag);
+        if (!__shfl_sync(0xffffffffu, w, 0)) {
+            if (lane == 0) { *abort_flag = 1; atomicCAS(p.status, ST_OK, ST_TIMEOUT_FULL); }
+            return;
+        }
+        const float pm0 = xb[(NMT * 4 + 0) * 32 + lane], pm1 = xb[(NMT * 4 + 1) * 32 + lane];
+        const float pl0 = xb[(NMT * 4 + 2) * 32 + lane], pl1 = xb[(NMT * 4 + 3) * 32 + lane];
+        const float M0 = fmaxf(m0, pm0), M1 = fmaxf(m1, pm1);
+        const float a0 = ex2((m0 - M0) * LOG2E), a1 = ex2((m1 - M1) * LOG2E);
+        const float c0 = ex2((pm0 - M0) * LOG2E), c1 = ex2((pm1 - M1) * LOG2E);
+#pragma unroll
+        for (int mt = 0; mt < NMT; mt++) {
+            o[mt][0] = o[mt][0] * a0 + xb[(mt * 4 + 0) * 32 + lane] * c0;
+            o[mt][1] = o[mt][1] * a1 + xb[(mt * 4 + 1) * 32 + lane] * c1;
+            o[mt][2] = o[mt][2] * a0 + xb[(mt * 4 + 2) * 32 + lane] * c0;
+            o[mt][3] = o[mt][3] * a1 + xb[(mt * 4 + 3) * 32 + lane] * c1;
+        }
+        l0 = l0 * a0 + pl0 * c0;
+        l1 = l1 * a1 + pl1 * c1;
+        m0 = M0;
+        m1 = M1;
+    }
+
+    // ---- write the slot partial
+    const uint64_t rbase = ((uint64_t) job.slot * p.nkv + h) * p.rows;
+    const uint32_t r0 = rg * 8 + 2 * t, r1 = r0 + 1;
+#pragma unroll
+    for (int mt = 0; mt < NMT; mt++) {
+        const int d0 = dV(QUANT, HD, mt, (int) g, 0), d1 = dV(QUANT, HD, mt, (int) g, 1);
+        if (r0 < p.rows) {
+            p.Op[(rbase + r0) * HD + d0] = o[mt][0];
+            p.Op[(rbase + r0) * HD + d1] = o[mt][2];
+        }
+        if (r1 < p.rows) {
+            p.Op[(rbase + r1) * HD + d0] = o[mt][1];
+            p.Op[(rbase + r1) * HD + d1] = o[mt][3];
+        }
+    }
+    if (g == 0) {
+        if (r0 < p.rows) { p.Mp[rbase + r0] = l0 > 0.f ? m0 : -INFINITY; p.Lp[rbase + r0] = l0; }
+        if (r1 < p.rows) { p.Mp[rbase + r1] = l1 > 0.f ? m1 : -INFINITY; p.Lp[rbase + r1] = l1; }
+    }
+}
+
+}  // namespace dec
+}  // namespace pa

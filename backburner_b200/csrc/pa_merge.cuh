@@ -1,0 +1,113 @@
+// pa_merge.cuh - log-sum-exp merge of unnormalised partials (O, m, l), and the final normalisation.
+//
+// Reference semantics:
+//   pa_merge / pa_merge_big (phone-attn/pa-metal.mm:137-159, 490-524): M = max of the parts' m, parts with no keys
+//     skipped, L = sum_c exp(m_c - M) l_c, O = sum_c exp(m_c - M) O_c; the fold bit also takes the result already in
+//     (O, M, L) as one more part.
+//   merge_partial (phone-attn/phone-attn.h:231-239): a part with l <= 0 contributes nothing.
+//   attn_core's normalisation (phone-attn/phone-attn.h:651-655): O/l rounded to f16, lse = m + log l (-inf if l == 0).
+// One warp per output row; each lane owns hd/32 consecutive head dims (float4 loads).
+#pragma once
+#include "pa_common.cuh"
+
+namespace pa {
+namespace mrg {
+
+struct Params {
+    const float *Op, *Mp, *Lp;   // parts: row R of part c of set s at (c * part_rows + s * set_rows + R)
+    const uint32_t *c_range;     // [n_sets + 1]: parts [c_range[s], c_range[s+1]) of set s; null: [0, n_parts)
+    uint32_t n_parts;
+    uint64_t part_rows, set_rows;
+    float *O, *M, *L;            // out: row R of set s at s * rows_per_set + R
+    uint64_t rows_per_set;       // nkv * rows
+    uint32_t n_sets;
+    int fold;                    // 1: (O, M, L) already hold a partial to fold in
+};
+
+template <int HD>
+__global__ void __launch_bounds__(256) merge_kernel(const Params p) {
+    constexpr int V = HD / 32;   // floats per lane
+    const uint64_t gw = (uint64_t) blockIdx.x * 8 + threadIdx.x / 32;
+    const uint32_t lane = threadIdx.x % 32;
+    if (gw >= (uint64_t) p.n_sets * p.rows_per_set) return;
+    const uint32_t s = (uint32_t) (gw / p.rows_per_set);
+    const uint64_t R = gw % p.rows_per_set;
+    const uint32_t c0 = p.c_range ? p.c_range[s] : 0, c1 = p.c_range ? p.c_range[s + 1] : p.n_parts;
+    const uint64_t orow = (uint64_t) s * p.rows_per_set + R;
+
+    float M = -INFINITY;
+    float m_in = -INFINITY, l_in = 0.f;
+    if (p.fold) {
+        m_in = p.M[orow];
+        l_in = p.L[orow];
+        if (l_in > 0.f) M = m_in;
+    }
+    for (uint32_t c = c0; c < c1; c++) {
+        const uint64_t pr = (uint64_t) c * p.part_rows + (uint64_t) s * p.set_rows + R;
+        if (p.Lp[pr] > 0.f) M = fmaxf(M, p.Mp[pr]);
+    }
+    float acc[V];
+    float L = 0.f;
+#pragma unroll
+    for (int i = 0; i < V; i++) acc[i] = 0.f;
+    if (p.fold && l_in > 0.f) {
+        const float w = ex2((m_in - M) * LOG2E);
+        L = w * l_in;
+        const float4 *src = reinterpret_cast<const float4 *>(p.O + orow * HD + lane * V);
+#pragma unroll
+        for (int i = 0; i < V / 4; i++) {
+            const float4 x = src[i];
+            acc[4 * i] = w * x.x; acc[4 * i + 1] = w * x.y; acc[4 * i + 2] = w * x.z; acc[4 * i + 3] = w * x.w;
+        }
+    }
+    for (uint32_t c = c0; c < c1; c++) {
+        const uint64_t pr = (uint64_t) c * p.part_rows + (uint64_t) s * p.set_rows + R;
+        const float lc = p.Lp[pr];
+        if (!(lc > 0.f)) continue;
+        const float w = ex2((p.Mp[pr] - M) * LOG2E);
+        L = fmaf(w, lc, L);
+        const float4 *src = reinterpret_cast<const float4 *>(p.Op + pr * HD + lane * V);
+#pragma unroll
+        for (int i = 0; i < V / 4; i++) {
+            const float4 x = src[i];
+            acc[4 * i] = fmaf(w, x.x, acc[4 * i]);
+            acc[4 * i + 1] = fmaf(w, x.y, acc[4 * i + 1]);
+            acc[4 * i + 2] = fmaf(w, x.z, acc[4 * i + 2]);
+            acc[4 * i + 3] = fmaf(w, x.w, acc[4 * i + 3]);
+        }
+    }
+    float4 *dst = reinterpret_cast<float4 *>(p.O + orow * HD + lane * V);
+#pragma unroll
+    for (int i = 0; i < V / 4; i++) dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+    if (lane == 0) {
+        p.M[orow] = L > 0.f ? M : -INFINITY;
+        p.L[orow] = L;
+    }
+}
+
+// O/l -> f16, lse = m + log(l); rows with l == 0 give O = 0, lse = -inf
+template <int HD>
+__global__ void __launch_bounds__(256) normalize_kernel(const float *O, const float *M, const float *L, uint64_t n_rows,
+                                                        uint16_t *Oh, float *lse) {
+    constexpr int V = HD / 32;
+    const uint64_t r = (uint64_t) blockIdx.x * 8 + threadIdx.x / 32;
+    const uint32_t lane = threadIdx.x % 32;
+    if (r >= n_rows) return;
+    const float l = L[r];
+    const float inv = l > 0.f ? 1.0f / l : 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; i += 2) {
+        const uint32_t h2 = pack_h2(O[r * HD + lane * V + i] * inv, O[r * HD + lane * V + i + 1] * inv);
+        *reinterpret_cast<uint32_t *>(Oh + r * HD + lane * V + i) = h2;
+    }
+    if (lane == 0) lse[r] = l > 0.f ? M[r] + logf(l) : -INFINITY;
+}
+
+// f16(q * scale) for n fp32 values (scripts/sme/sme_attn.c:276-280; phone-attn/phone-attn.h:595-599)
+__global__ void scale_q_kernel(const float *Q, float scale, uint64_t n, uint16_t *Qs) {
+    for (uint64_t i = (uint64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t) gridDim.x * blockDim.x)
+        Qs[i] = __half_as_ushort(__float2half_rn(Q[i] * scale));
+}
+
+}  // namespace mrg
+}  // namespace pa

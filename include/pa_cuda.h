@@ -1,0 +1,152 @@
+/* pa_cuda.h - C ABI of libpacuda.so, the B200 (sm_100a) engine for Backburner's phone-attn hot path: partial attention
+ * over an offloaded, position-contiguous segment of a Q8_0 / Q4_0 KV cache, returning the unnormalised partial
+ * (O, m, l) that the host merges with its own by log-sum-exp.
+ *
+ * Every entry point is plain C: device or host pointers and sizes, no framework types. Reference interfaces each one
+ * replaces (paths inside the reference repository):
+ *   pa_cuda_available      sme2_available                 phone-attn/phone-attn.h:67
+ *   pa_cuda_attn_partial   sme_attn_partial               phone-attn/phone-attn.h:65-66, scripts/sme/sme_attn.c:271-306
+ *   pa_cuda_attn, plans    sme_attn_pipe (all heads)      phone-attn/phone-attn.h:69-70, scripts/sme/sme_attn.c:448-463
+ *                          + the engine's page batching   phone-attn/pa-metal.mm:627-714
+ *   pa_cuda_merge          pa_merge / pa_merge_big        phone-attn/pa-metal.mm:137-159, 490-524
+ *                          merge_partial                  phone-attn/phone-attn.h:231-239
+ *   pa_cuda_normalize      attn_core's O/l, lse           phone-attn/phone-attn.h:651-655
+ *   pa_cuda_scale_q        f16(q * scale)                 phone-attn/phone-attn.h:595-599, scripts/sme/sme_attn.c:276-280
+ *   pa_cuda_alloc_page,
+ *   pa_cuda_free_page,
+ *   pa_cuda_begin,
+ *   pa_cuda_end            pa::engine                     phone-attn/phone-attn.h:166-183 (pa-metal.mm:804-953)
+ *
+ * Data layout (the reference's, unchanged):
+ *   K/V rows: key position j, KV head h at base + j*rs + h*hb; Q8_0 head = hd/32 blocks of (f16 d, 32 x int8),
+ *   Q4_0 head = hd/32 blocks of (f16 d, 16 bytes: byte i = elem i | elem i+16 << 4, value (n - 8) * d).
+ *   Qs: f16(q * scale) [set][nkv][rows][hd]; O: fp32 [set][nkv][rows][hd]; m, l: fp32 [set][nkv][rows].
+ *   O is unnormalised: O = sum_j exp(s_j - m) v_j, l = sum_j exp(s_j - m), m = max_j s_j; no keys: m = -inf, l = 0.
+ *
+ * Errors: functions return PA_CUDA_OK (0) or a negative code; pa_cuda_last_error() gives the text. Kernels never trap:
+ * a bounded wait that runs out records a code on the device, which pa_cuda_status() returns.
+ * Threading: a context is used by one host thread at a time (as pa::server's session thread uses its engine).
+ */
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PA_CUDA_ABI_VERSION 1
+
+enum {
+    PA_CUDA_OK = 0,
+    PA_CUDA_EINVAL = -1,       /* bad argument (message says which) */
+    PA_CUDA_ECUDA = -2,        /* a CUDA call failed */
+    PA_CUDA_ENOMEM = -3,       /* device or host allocation failed */
+    PA_CUDA_ETIMEOUT = -4,     /* a kernel's bounded wait ran out (the context stays usable) */
+    PA_CUDA_EUNSUPPORTED = -5, /* shape the kernels do not cover */
+    PA_CUDA_ENCCL = -6         /* an NCCL call failed */
+};
+
+/* config_req.is_q8 (phone-attn/phone-attn.h:15) */
+enum { PA_CUDA_F16 = 0, PA_CUDA_Q8_0 = 1, PA_CUDA_Q4_0 = 2 };
+
+typedef struct pa_cuda_ctx pa_cuda_ctx;
+typedef struct pa_cuda_plan pa_cuda_plan;
+
+/* Geometry of a call. hd: 128 or 256. nkv: KV heads (1..16). rows: query rows per KV head (tokens x GQA group).
+ * quant: PA_CUDA_Q8_0 or PA_CUDA_Q4_0. rs: bytes per key position (multiple of 16). hb: bytes per head in a position
+ * (hd/32*34 for Q8_0, hd/32*18 for Q4_0). K/V base pointers must be 16-byte aligned. */
+typedef struct pa_cuda_shape {
+    uint32_t hd, nkv, rows, quant;
+    uint64_t rs, hb;
+} pa_cuda_shape;
+
+/* A run of nk consecutive key positions (a page, or one layer's shard) whose partial folds into output set `set`.
+ * k, v: device pointers to the run's first position. */
+typedef struct pa_cuda_seg {
+    const uint8_t *k, *v;
+    uint32_t nk, set;
+} pa_cuda_seg;
+
+/* pa::page (phone-attn/phone-attn.h:163): k, v are host-writable and device-readable (managed memory). */
+typedef struct pa_cuda_page {
+    uint8_t *k, *v;
+    void *hk, *hv;
+} pa_cuda_page;
+
+/* 1 if a device of compute capability 10.x (B200, sm_100a) is visible and the kernels load on it. */
+int pa_cuda_available(void);
+int pa_cuda_abi_version(void);
+
+int pa_cuda_create(int device, pa_cuda_ctx **out);
+void pa_cuda_destroy(pa_cuda_ctx *ctx);
+const char *pa_cuda_last_error(const pa_cuda_ctx *ctx);
+/* Synchronise `stream` (a cudaStream_t; NULL = the context's stream), then return and clear the device status word:
+ * PA_CUDA_OK, or PA_CUDA_ETIMEOUT if a kernel gave up a bounded wait since the last call. */
+int pa_cuda_status(pa_cuda_ctx *ctx, void *stream);
+/* Bound on every in-kernel wait (default 2 s). */
+void pa_cuda_set_timeout_ns(pa_cuda_ctx *ctx, uint64_t ns);
+/* Failure-detection test hook: while on, the decode kernel's consumer warps first wait on a barrier that nothing
+ * completes, so their bounded wait runs out after the timeout; the kernel records PA_CUDA_ETIMEOUT and returns
+ * without trapping, and the context stays usable. Off by default. */
+void pa_cuda_set_stall_test(pa_cuda_ctx *ctx, int on);
+/* Kernel launches made by this context since it was created (the bench reports launches per step from it). */
+uint64_t pa_cuda_launch_count(const pa_cuda_ctx *ctx);
+
+/* ---- plans: the split of a call into per-chunk jobs, built once and run many times (CUDA-graph capturable).
+ * chunk_keys: keys per CTA job (0 = chosen from the device's SM count). The plan owns its scratch (the chunk
+ * partials, pa_cuda_plan_scratch_bytes()) in device memory. */
+int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n_sets, const pa_cuda_seg *segs,
+                        uint32_t n_segs, uint32_t chunk_keys, pa_cuda_plan **out);
+size_t pa_cuda_plan_scratch_bytes(const pa_cuda_plan *plan);
+uint32_t pa_cuda_plan_jobs(const pa_cuda_plan *plan);
+/* kernel launches one pa_cuda_plan_run makes */
+uint32_t pa_cuda_plan_launches(const pa_cuda_plan *plan);
+/* Qs, O, m, l: device pointers laid out [set][nkv][rows]...; stream: cudaStream_t (NULL = the context's stream).
+ * Asynchronous. */
+int pa_cuda_plan_run(pa_cuda_plan *plan, const uint16_t *Qs, float *O, float *m, float *l, void *stream);
+void pa_cuda_plan_destroy(pa_cuda_plan *plan);
+
+/* One-shot: plan, run, free (allocates; synchronises the stream before freeing the plan). */
+int pa_cuda_attn(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, const uint16_t *Qs, uint32_t n_sets,
+                 const pa_cuda_seg *segs, uint32_t n_segs, float *O, float *m, float *l, void *stream);
+
+/* sme_attn_partial for all heads of one segment: Q fp32 [nkv][rows][hd] unscaled (device), scale applied as
+ * f16(q * scale); K, V device pointers to key 0; nk keys (any count, no 64-key alignment needed). Synchronous. */
+int pa_cuda_attn_partial(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, const float *Q, float scale, const uint8_t *K,
+                         const uint8_t *V, uint32_t nk, float *O, float *m, float *l, void *stream);
+
+/* Host-buffer call (the end-to-end path): Qs_host [n_sets][nkv][rows][hd] f16 is copied to the device, the plan
+ * runs, O/m/l are copied back into host buffers; returns after the copies land. Pinned host buffers give full
+ * copy bandwidth. */
+int pa_cuda_plan_run_host(pa_cuda_plan *plan, const uint16_t *Qs_host, float *O_host, float *m_host, float *l_host,
+                          void *stream);
+
+/* LSE merge of n_parts partials Op [n_parts][rows][hd], mp/lp [n_parts][rows] (device) into O [rows][hd], m, l.
+ * fold = 1: (O, m, l) already hold a partial, folded in as one more part (merge_partial / pa_merge_big fold). */
+int pa_cuda_merge(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, uint32_t n_parts, const float *Op, const float *mp,
+                  const float *lp, float *O, float *m, float *l, int fold, void *stream);
+/* O/l -> f16 Oh, lse = m + log l (device) */
+int pa_cuda_normalize(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, const float *O, const float *m, const float *l,
+                      uint16_t *Oh, float *lse, void *stream);
+/* Qs = f16(Q * scale) for n values (device) */
+int pa_cuda_scale_q(pa_cuda_ctx *ctx, const float *Q, float scale, uint64_t n, uint16_t *Qs, void *stream);
+
+/* ---- pa::engine (phone-attn/phone-attn.h:166-183) */
+int pa_cuda_alloc_page(pa_cuda_ctx *ctx, size_t bytes, pa_cuda_page *p);
+void pa_cuda_free_page(pa_cuda_ctx *ctx, pa_cuda_page *p);
+/* Start the partial over n_pages pages (nkeys[i] keys each) for ng groups of 48 query rows per KV head:
+ * Qs_host = f16(q*scale) [ng][nkv][48][hd] (phone-attn/phone-attn.h:170-172). ntok (1..8) for ng == 1: the group's
+ * real tokens; rows r = g*8 + t with t >= ntok are zero and come back as empty partials (m = -inf, l = 0), as
+ * pa_merge_big's ntok packing (phone-attn/pa-metal.mm:505-509). shape->rows is ignored (48). Asynchronous. */
+int pa_cuda_begin(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *nkeys, int n_pages,
+                  const uint16_t *Qs_host, const pa_cuda_shape *shape, int ng, int ntok);
+/* Wait for the call begun last; O [ng][nkv*48][hd], m, l [ng][nkv*48] (host). Returns the milliseconds from begin to
+ * completion, or -1 on failure with m = -inf, l = 0 (phone-attn/pa-metal.mm:928-937). */
+double pa_cuda_end(pa_cuda_ctx *ctx, float *O, float *m, float *l);
+/* GPU execution time of the last completed begin/end call (CUDA events), ms */
+double pa_cuda_exec_ms(const pa_cuda_ctx *ctx);
+
+#ifdef __cplusplus
+}
+#endif
