@@ -59,12 +59,16 @@ _SIGS = {
     "pa_cuda_plan_run": (ctypes.c_int, [_P, _P, _P, _P, _P, _P]),
     "pa_cuda_plan_run_host": (ctypes.c_int, [_P, _P, _P, _P, _P, _P]),
     "pa_cuda_plan_destroy": (None, [_P]),
+    "pa_cuda_plan_profile": (ctypes.c_int, [_P, ctypes.c_uint32]),
+    "pa_cuda_plan_kernel_ms": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_uint32)]),
     "pa_cuda_attn": (ctypes.c_int, [_P, ctypes.POINTER(_Shape), _P, ctypes.c_uint32, ctypes.POINTER(_Seg),
                                     ctypes.c_uint32, _P, _P, _P, _P]),
     "pa_cuda_attn_partial": (ctypes.c_int, [_P, ctypes.POINTER(_Shape), _P, ctypes.c_float, _P, _P, ctypes.c_uint32,
                                             _P, _P, _P, _P]),
     "pa_cuda_merge": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32, _P, _P, _P, _P, _P, _P,
                                      ctypes.c_int, _P]),
+    "pa_cuda_merge_gathered": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_uint32, _P, _P, _P, _P,
+                                              ctypes.c_int, _P]),
     "pa_cuda_normalize": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint64, _P, _P, _P, _P, _P, _P]),
     "pa_cuda_scale_q": (ctypes.c_int, [_P, _P, ctypes.c_float, ctypes.c_uint64, _P, _P]),
     "pa_cuda_alloc_page": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.POINTER(_Page)]),
@@ -226,6 +230,17 @@ class Plan:
         self.ctx.check(lib().pa_cuda_plan_run_host(self._h, _ptr(Qs_host), _ptr(O_host), _ptr(m_host), _ptr(l_host),
                                                    _stream_ptr(stream)), "plan_run_host")
 
+    def profile(self, max_runs: int):
+        """Record CUDA events around the decode kernel of the next max_runs runs (0: off)."""
+        self.ctx.check(lib().pa_cuda_plan_profile(self._h, max_runs), "plan_profile")
+
+    def kernel_ms(self):
+        """(summed decode-kernel milliseconds, runs) since profile() / the last call."""
+        t = ctypes.c_double()
+        n = ctypes.c_uint32()
+        self.ctx.check(lib().pa_cuda_plan_kernel_ms(self._h, ctypes.byref(t), ctypes.byref(n)), "plan_kernel_ms")
+        return float(t.value), int(n.value)
+
     def close(self):
         if self._h:
             lib().pa_cuda_plan_destroy(self._h)
@@ -282,6 +297,26 @@ def merge(ctx: Context, hd: int, Op, mp, lp, out=None, fold: bool = False, strea
     ctx.check(lib().pa_cuda_merge(ctx.handle, hd, rows, n, _ptr(Op), _ptr(mp), _ptr(lp), _ptr(O), _ptr(m), _ptr(l),
                                   1 if fold else 0, _stream_ptr(stream)), "merge")
     return O, m, l
+
+
+def merge_gathered(ctx: Context, hd: int, rows: int, packed, n_parts: int, out=None, fold: bool = False, stream=None):
+    """Merge n_parts partials packed as [n_parts][rows*hd + 2*rows] (O, then m, then l, per part), as one all-gather
+    of each rank's packed partial delivers them (pa_cuda_merge_gathered). Returns (O [rows][hd], m, l)."""
+    import torch
+    if out is None:
+        O = torch.empty((rows, hd), dtype=torch.float32, device=packed.device)
+        m = torch.empty((rows,), dtype=torch.float32, device=packed.device)
+        l = torch.empty_like(m)
+    else:
+        O, m, l = out
+    ctx.check(lib().pa_cuda_merge_gathered(ctx.handle, hd, rows, n_parts, _ptr(packed), _ptr(O), _ptr(m), _ptr(l),
+                                           1 if fold else 0, _stream_ptr(stream)), "merge_gathered")
+    return O, m, l
+
+
+def packed_views(buf, rows: int, hd: int):
+    """(O, m, l) views into one packed partial buffer of rows*(hd+2) floats."""
+    return buf[:rows * hd].view(rows, hd), buf[rows * hd:rows * hd + rows], buf[rows * hd + rows:rows * (hd + 2)]
 
 
 def normalize(ctx: Context, hd: int, O, m, l, stream=None):

@@ -59,6 +59,10 @@ struct pa_cuda_plan {
     // decode launch shape
     uint32_t hg = 1, rgc = 1, n_rg = 1, pw = 1, n_consumers = 1, str = 0, grid_y = 1;
     size_t smem = 0;
+    // profiling: event pairs around the decode kernel of each run (a ring, summed by pa_cuda_plan_kernel_ms)
+    bool profile = false;
+    std::vector<cudaEvent_t> ev;
+    uint32_t ev_used = 0;
 };
 
 namespace {
@@ -162,10 +166,16 @@ int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, 
         prm.n_consumers = p->n_consumers;
         prm.timeout_ns = ctx->timeout_ns;
         prm.stall = ctx->stall_test;
+        const bool prof = p->profile && p->ev_used + 2 <= p->ev.size();
+        if (prof) cudaEventRecord(p->ev[p->ev_used], st);
         cudaError_t e;
         if (sh.hd == 128) e = sh.quant == PA_CUDA_Q8_0 ? launch_decode<128, 1>(p, prm, st) : launch_decode<128, 2>(p, prm, st);
         else e = sh.quant == PA_CUDA_Q8_0 ? launch_decode<256, 1>(p, prm, st) : launch_decode<256, 2>(p, prm, st);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "decode kernel launch");
+        if (prof) {
+            cudaEventRecord(p->ev[p->ev_used + 1], st);
+            p->ev_used += 2;
+        }
         ctx->launches++;
     }
     pa::mrg::Params mp{};
@@ -174,7 +184,8 @@ int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, 
     mp.Lp = p->d_lp;
     mp.c_range = p->d_crange;
     mp.n_parts = p->n_slots;
-    mp.part_rows = (uint64_t) sh.nkv * sh.rows;
+    mp.op_stride = (uint64_t) sh.nkv * sh.rows * sh.hd;
+    mp.ml_stride = (uint64_t) sh.nkv * sh.rows;
     mp.set_rows = 0;
     mp.O = O;
     mp.M = m;
@@ -386,9 +397,42 @@ int pa_cuda_plan_run(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, fl
     return run_plan(p, Qs, O, m, l, pick(ctx, stream));
 }
 
+int pa_cuda_plan_profile(pa_cuda_plan *p, uint32_t max_runs) {
+    if (!p) return PA_CUDA_EINVAL;
+    pa_cuda_ctx *ctx = p->ctx;
+    cudaSetDevice(ctx->device);
+    for (auto e : p->ev) cudaEventDestroy(e);
+    p->ev.clear();
+    p->ev_used = 0;
+    p->profile = max_runs > 0;
+    for (uint32_t i = 0; i < 2 * max_runs; i++) {
+        cudaEvent_t e;
+        PA_CK(cudaEventCreate(&e), "event create");
+        p->ev.push_back(e);
+    }
+    return PA_CUDA_OK;
+}
+
+int pa_cuda_plan_kernel_ms(pa_cuda_plan *p, double *total_ms, uint32_t *n_runs) {
+    if (!p || !total_ms || !n_runs) return PA_CUDA_EINVAL;
+    pa_cuda_ctx *ctx = p->ctx;
+    double t = 0;
+    for (uint32_t i = 0; i + 1 < p->ev_used; i += 2) {
+        PA_CK(cudaEventSynchronize(p->ev[i + 1]), "event synchronize");
+        float ms = 0;
+        PA_CK(cudaEventElapsedTime(&ms, p->ev[i], p->ev[i + 1]), "event elapsed");
+        t += ms;
+    }
+    *total_ms = t;
+    *n_runs = p->ev_used / 2;
+    p->ev_used = 0;
+    return PA_CUDA_OK;
+}
+
 void pa_cuda_plan_destroy(pa_cuda_plan *p) {
     if (!p) return;
     cudaSetDevice(p->ctx->device);
+    for (auto e : p->ev) cudaEventDestroy(e);
     if (p->d_jobs) cudaFree(p->d_jobs);
     if (p->d_crange) cudaFree(p->d_crange);
     if (p->d_op) cudaFree(p->d_op);
@@ -472,7 +516,36 @@ int pa_cuda_merge(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, uint32_t n_parts
     prm.Lp = lp;
     prm.c_range = nullptr;
     prm.n_parts = n_parts;
-    prm.part_rows = rows;
+    prm.op_stride = rows * hd;
+    prm.ml_stride = rows;
+    prm.set_rows = 0;
+    prm.O = O;
+    prm.M = m;
+    prm.L = l;
+    prm.rows_per_set = rows;
+    prm.n_sets = 1;
+    prm.fold = fold ? 1 : 0;
+    cudaError_t e = hd == 128 ? launch_merge<128>(prm, pick(ctx, stream)) : launch_merge<256>(prm, pick(ctx, stream));
+    PA_CK(e, "merge launch");
+    ctx->launches++;
+    return PA_CUDA_OK;
+}
+
+int pa_cuda_merge_gathered(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, uint32_t n_parts, const float *packed,
+                           float *O, float *m, float *l, int fold, void *stream) {
+    if (!ctx) return PA_CUDA_EINVAL;
+    if (hd != 128 && hd != 256) return fail(ctx, PA_CUDA_EUNSUPPORTED, "hd must be 128 or 256");
+    if (!O || !m || !l || (n_parts && !packed)) return fail(ctx, PA_CUDA_EINVAL, "null argument");
+    cudaSetDevice(ctx->device);
+    const uint64_t stride = rows * (hd + 2);
+    pa::mrg::Params prm{};
+    prm.Op = packed;
+    prm.Mp = packed + rows * hd;
+    prm.Lp = packed + rows * hd + rows;
+    prm.c_range = nullptr;
+    prm.n_parts = n_parts;
+    prm.op_stride = stride;
+    prm.ml_stride = stride;
     prm.set_rows = 0;
     prm.O = O;
     prm.M = m;

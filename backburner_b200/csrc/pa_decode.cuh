@@ -333,6 +333,13 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 17 : 13), 1) decode_kernel(c
 #pragma unroll
                     for (int i = 0; i < NW; i++) W[kk][i] = __funnelshift_r(raw[i], raw[i + 1], shift);
                 }
+                // keys past the stage's valid count hold whatever the buffer held before (possibly never written):
+                // a zero scale makes their V exactly 0, so P = 0 times it cannot produce NaN
+                if (tvalid < TILE_KEYS) {
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        if ((int) key[kk] >= tvalid) sc[kk] = 0u;
+                }
                 // key pairs: (key0,key1) -> a0/a1, (key2,key3) -> a2/a3
                 const uint32_t s01 = sc[0] | (sc[1] << 16), s23 = sc[2] | (sc[3] << 16);
                 if (QUANT == 1) {

@@ -14,10 +14,11 @@ namespace pa {
 namespace mrg {
 
 struct Params {
-    const float *Op, *Mp, *Lp;   // parts: row R of part c of set s at (c * part_rows + s * set_rows + R)
+    const float *Op, *Mp, *Lp;   // parts: row R of part c of set s at Op + c * op_stride + (s * set_rows + R) * HD,
+                                 // Mp / Lp + c * ml_stride + s * set_rows + R
     const uint32_t *c_range;     // [n_sets + 1]: parts [c_range[s], c_range[s+1]) of set s; null: [0, n_parts)
     uint32_t n_parts;
-    uint64_t part_rows, set_rows;
+    uint64_t op_stride, ml_stride, set_rows;
     float *O, *M, *L;            // out: row R of set s at s * rows_per_set + R
     uint64_t rows_per_set;       // nkv * rows
     uint32_t n_sets;
@@ -42,8 +43,9 @@ __global__ void __launch_bounds__(256) merge_kernel(const Params p) {
         l_in = p.L[orow];
         if (l_in > 0.f) M = m_in;
     }
+    const uint64_t rr = (uint64_t) s * p.set_rows + R;
     for (uint32_t c = c0; c < c1; c++) {
-        const uint64_t pr = (uint64_t) c * p.part_rows + (uint64_t) s * p.set_rows + R;
+        const uint64_t pr = (uint64_t) c * p.ml_stride + rr;
         if (p.Lp[pr] > 0.f) M = fmaxf(M, p.Mp[pr]);
     }
     float acc[V];
@@ -61,12 +63,12 @@ __global__ void __launch_bounds__(256) merge_kernel(const Params p) {
         }
     }
     for (uint32_t c = c0; c < c1; c++) {
-        const uint64_t pr = (uint64_t) c * p.part_rows + (uint64_t) s * p.set_rows + R;
+        const uint64_t pr = (uint64_t) c * p.ml_stride + rr;
         const float lc = p.Lp[pr];
         if (!(lc > 0.f)) continue;
         const float w = ex2((p.Mp[pr] - M) * LOG2E);
         L = fmaf(w, lc, L);
-        const float4 *src = reinterpret_cast<const float4 *>(p.Op + pr * HD + lane * V);
+        const float4 *src = reinterpret_cast<const float4 *>(p.Op + (uint64_t) c * p.op_stride + rr * HD + lane * V);
 #pragma unroll
         for (int i = 0; i < V / 4; i++) {
             const float4 x = src[i];

@@ -1,0 +1,385 @@
+#!/usr/bin/env python
+"""bench.py - phone-attn partial attention on B200: BASELINE.json's decode workload (config 1).
+
+One step = one decode step of a 64-layer, Qwen3-27B-shaped model over its offloaded KV: per layer, 40 query heads
+(8 KV heads, GQA 5), head dim 128, one query token with fresh seeded Q, against 131,072 Q8_0 key/value positions;
+softmax scale 1/sqrt(128). The KV is sharded by position across the N GPUs (one process per GPU, rank r holds
+positions [r*S, (r+1)*S) of every layer); every step each rank computes its partial (O, m, l) for all 64 layers
+(one decode-kernel launch + one merge launch), the partials are exchanged with ONE NCCL all-gather (N > 1) and
+folded by log-sum-exp on every rank.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    (N > 1: python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 ... bench.py ...)
+
+Prints ONE JSON line (rank 0). `value` is whole-job GB/s of algorithmic bytes (quantised K+V read, f16 Q read,
+(O, m, l) written) with inputs resident in HBM, timed with CUDA events over K steps, max over ranks; `e2e` is the
+same metric through the host-buffer path (pinned Q in, O/m/l out, copies inside the timed region). The per-step KV
+(18.3 GB) is far larger than L2, so no flush is needed. `--impl reference` times the CPU restatement of the
+reference's own kernel (the oracle's fp32 port of sme_attn_partial) on all host threads instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LAYERS, KEYS, NKV, GQA, HD = 64, 131072, 8, 5, 128
+Q_HEADS = NKV * GQA
+SEED = 20260127
+GEN_CHUNK = 16384   # keys per generator draw (the data does not depend on the number of GPUs)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--keys", type=int, default=KEYS)
+    ap.add_argument("--e2e-steps", type=int, default=16)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def layer_bytes(keys: int) -> dict:
+    """Algorithmic bytes of one layer's partial over `keys` positions (the roofline's unit)."""
+    kv = 2 * keys * NKV * (HD // 32 * 34)
+    q = Q_HEADS * HD * 2                    # f16(q * scale) read
+    oml = Q_HEADS * (HD + 2) * 4            # (O, m, l) written
+    return dict(kv=kv, q=q, oml=oml, total=kv + q + oml)
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except Exception:
+            pass
+        finally:
+            try:
+                os.unlink(self.path)
+            except Exception:
+                pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        load = [x for x in sm if mx and x > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------------------------- data
+def make_layer(torch, pa, layer: int, k0: int, nk: int, device):
+    """Quantised K and V rows [nk][NKV*136] for positions [k0, k0+nk) of `layer`: N(0,1) values, 4 K channels per
+    head scaled x8, Q8_0 (the BASELINE distributions)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED * 1000 + layer)
+    ch = torch.stack([torch.randperm(HD, generator=g, device=device)[:4] for _ in range(NKV)])   # [NKV, 4]
+    out_k, out_v = [], []
+    c0 = (k0 // GEN_CHUNK) * GEN_CHUNK
+    for c in range(c0, k0 + nk, GEN_CHUNK):
+        g.manual_seed((SEED * 1000 + layer) * 4096 + c // GEN_CHUNK)
+        kf = torch.randn((GEN_CHUNK, NKV, HD), generator=g, device=device)
+        vf = torch.randn((GEN_CHUNK, NKV, HD), generator=g, device=device)
+        for h in range(NKV):
+            kf[:, h, ch[h]] *= 8.0
+        a, b = max(k0, c) - c, min(k0 + nk, c + GEN_CHUNK) - c
+        out_k.append(pa.quantize_q8_0(kf[a:b]).reshape(b - a, -1))
+        out_v.append(pa.quantize_q8_0(vf[a:b]).reshape(b - a, -1))
+    return torch.cat(out_k), torch.cat(out_v)
+
+
+def make_q(torch, steps: int, layers: int, device):
+    """Fresh seeded Q per step: f16(q * scale) [steps][layers][NKV][GQA][HD] with q ~ N(0,1)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED + 7)
+    q = torch.randn((steps, layers, NKV, GQA, HD), generator=g, device=device)
+    return (q * (1.0 / HD ** 0.5)).to(torch.float16)
+
+
+# --------------------------------------------------------------------------------------------- CPU baseline
+def cpu_baseline(target_s: float = 10.0):
+    """The oracle's fp32 restatement of the reference's own kernel (block online softmax of
+    scripts/sme/sme_attn.c:274-306) on all host threads, on a bounded sample of the workload: 32,768 positions of one
+    layer (8 KV heads, GQA 5, Q8_0), computed repeatedly for ~target_s seconds. Returns the cpu_baseline object."""
+    from oracle import oracle as orc
+    threads = os.cpu_count() or 1
+    nk = 32768
+    c = orc.gen_case(SEED, HD, NKV, GQA, nk, orc.Q8_0)
+    chunk = max(512, nk // (threads * 4) // 512 * 512)
+    orc.partial_f32_mt(c["shape"], c["Qs"], c["K"], c["V"], nk, threads, chunk)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        orc.partial_f32_mt(c["shape"], c["Qs"], c["K"], c["V"], nk, threads, chunk)
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= target_s:
+            break
+    b = layer_bytes(nk)["total"] * reps
+    return {"value": round(b / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} x (1 layer x {nk} Q8_0 positions x 8 KV heads x 5 rows (GQA 5), d128, "
+                      f"{layer_bytes(nk)['total'] / 1e6:.1f} MB) in {dt:.1f} s; oracle fp32 block-online port of "
+                      f"sme_attn_partial on {threads} threads"}
+
+
+def run_reference(args, rank: int, world: int):
+    """--impl reference: the CPU restatement of the reference path on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    import numpy as np
+    from oracle import oracle as orc
+    threads = os.cpu_count() or 1
+    nk = 8192       # each step: a bounded sample of one layer's positions
+    cases = [orc.gen_case(SEED + i, HD, NKV, GQA, nk, orc.Q8_0) for i in range(2)]
+    for i in range(args.warmup):
+        c = cases[i % 2]
+        orc.partial_f32_mt(c["shape"], c["Qs"], c["K"], c["V"], nk, threads, 512)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        c = cases[i % 2]
+        orc.partial_f32_mt(c["shape"], c["Qs"], c["K"], c["V"], nk, threads, 512)
+    dt = time.perf_counter() - t0
+    b = layer_bytes(nk)["total"] * args.steps
+    v = b / dt / 1e9
+    sample = (f"each step: 1 layer x {nk} Q8_0 positions x 8 KV heads x 5 rows, d128 ({layer_bytes(nk)['total'] / 1e6:.1f}"
+              f" MB); oracle fp32 block-online port of sme_attn_partial (the reference CPU kernel is ARM SME2-only)")
+    line = {
+        "impl": "reference", "metric": "decode KV-attn GB/s (config 1: 64 layers x 131072 Q8_0 keys, 40q/8kv, d128)",
+        "value": round(v, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "config 1 decode (bounded CPU sample per step)", "layers": LAYERS, "keys": KEYS,
+                   "nkv": NKV, "q_heads": Q_HEADS, "hd": HD, "quant": "q8_0"},
+        "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------------------------- GPU arm
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    import backburner_b200 as pa
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", rank=rank, world_size=world,
+                                timeout=__import__("datetime").timedelta(seconds=120), device_id=device)
+    if not pa.available():
+        raise RuntimeError("libpacuda.so did not load on this GPU (build it with python -m backburner_b200.build)")
+    ctx = pa.Context(local)
+    L = args.layers
+    shard = args.keys // world
+    k0 = rank * shard
+    nk = shard if rank < world - 1 else args.keys - k0
+    shape = pa.shape_for(HD, NKV, GQA, pa.Q8_0)
+    rows = L * NKV * GQA
+
+    # ---- resident inputs: this rank's positions of every layer
+    Kall = torch.empty((L, nk, shape.rs), dtype=torch.uint8, device=device)
+    Vall = torch.empty_like(Kall)
+    for layer in range(L):
+        k, v = make_layer(torch, pa, layer, k0, nk, device)
+        Kall[layer].copy_(k)
+        Vall[layer].copy_(v)
+        del k, v
+    torch.cuda.synchronize()
+    total_steps = args.warmup + args.steps
+    Qs = make_q(torch, total_steps, L, device)            # [steps][L][NKV][GQA][HD]
+    segs = [pa.Seg(Kall[i].data_ptr(), Vall[i].data_ptr(), nk, i) for i in range(L)]
+    plan = pa.Plan(ctx, shape, L, segs)
+    packed = torch.empty((rows * (HD + 2),), dtype=torch.float32, device=device)   # this rank's (O, m, l)
+    Op, mp, lp = pa.packed_views(packed, rows, HD)
+    gathered = torch.empty((world, rows * (HD + 2)), dtype=torch.float32, device=device) if world > 1 else None
+    Of = torch.empty((rows, HD), dtype=torch.float32, device=device)
+    mf = torch.empty((rows,), dtype=torch.float32, device=device)
+    lf = torch.empty_like(mf)
+    stream = torch.cuda.current_stream(device)
+
+    def step(i):
+        plan.run(Qs[i], Op, mp, lp, stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, packed)
+            pa.merge_gathered(ctx, HD, rows, gathered, world, out=(Of, mf, lf), stream=stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for i in range(args.warmup):
+        step(i)
+    ctx.status(stream)
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = ctx.launches
+    plan.profile(args.steps)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    launches = ctx.launches - launches0
+    ctx.status(stream)
+    ms = ev0.elapsed_time(ev1)
+    kern_ms, kern_runs = plan.kernel_ms()
+    plan.profile(0)
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    per_step_bytes = L * layer_bytes(args.keys)["total"]      # the whole job's algorithmic bytes per step
+    value = per_step_bytes * args.steps / (ms * 1e-3) / 1e9
+
+    # ---- roofline of the dominant kernel (the decode kernel; one launch = this rank's 64-layer shard)
+    peak, peak_kind = measured_peaks()
+    kb = layer_bytes(nk)
+    launch_bytes = L * kb["total"]
+    kern_avg_ms = kern_ms / max(1, kern_runs)
+    achieved = launch_bytes / (kern_avg_ms * 1e-3) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "decode_traffic.json")) as f:
+            tr = json.load(f)
+        traffic = round(tr["dram_bytes_per_key_position"] * nk * L)
+    except Exception:
+        pass
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                "kernel": "pa::dec::decode_kernel<128,1>", "kernel_ms": round(kern_avg_ms, 4),
+                "algorithmic_bytes_per_launch": launch_bytes}
+
+    # ---- end to end through the host-buffer path (pinned Q in, O/m/l out, copies inside the timed region)
+    e2e = None
+    if args.e2e_steps > 0:
+        qh = torch.empty((args.e2e_steps, L, NKV, GQA, HD), dtype=torch.float16).pin_memory()
+        qh.copy_(Qs[:args.e2e_steps].cpu())
+        Oh = torch.empty((rows, HD), dtype=torch.float32).pin_memory()
+        mh = torch.empty((rows,), dtype=torch.float32).pin_memory()
+        lh = torch.empty_like(mh).pin_memory()
+        qd = torch.empty((L, NKV, GQA, HD), dtype=torch.float16, device=device)
+
+        def e2e_step(i):
+            if world == 1:
+                plan.run_host(qh[i], Oh, mh, lh, stream)     # the C ABI host path: H2D, kernels, D2H, sync
+            else:
+                qd.copy_(qh[i], non_blocking=True)
+                plan.run(qd, Op, mp, lp, stream)
+                dist.all_gather_into_tensor(gathered, packed)
+                pa.merge_gathered(ctx, HD, rows, gathered, world, out=(Of, mf, lf), stream=stream)
+                Oh.copy_(Of, non_blocking=True)
+                mh.copy_(mf, non_blocking=True)
+                lh.copy_(lf, non_blocking=True)
+                stream.synchronize()
+
+        for i in range(min(3, args.e2e_steps)):
+            e2e_step(i)
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(args.e2e_steps):
+            e2e_step(i)
+        dt = time.perf_counter() - t0
+        tt = torch.tensor([dt], device=device)
+        if world > 1:
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dt = float(tt.item())
+        e2e = {"value": round(per_step_bytes * args.e2e_steps / dt / 1e9, 1), "unit": "GB/s",
+               "h2d_bytes_per_step": L * NKV * GQA * HD * 2, "d2h_bytes_per_step": rows * (HD + 2) * 4,
+               "ms_per_step": round(dt / args.e2e_steps * 1e3, 3)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline()
+
+    clocks = clk.summary()
+    if rank == 0:
+        line = {
+            "metric": "decode KV-attn GB/s (config 1: 64 layers x 131072 Q8_0 keys, 40q/8kv, d128)",
+            "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "config 1: decode, 1 token/step, fresh seeded Q per step", "layers": L,
+                       "keys": args.keys, "keys_per_gpu": shard, "nkv": NKV, "q_heads": Q_HEADS, "hd": HD,
+                       "quant": "q8_0", "parallelism": f"sequence shards x{world}, 1 NCCL all-gather of (O,m,l)/step",
+                       "l2": "inputs larger than L2 (18.3 GB of KV per step), no flush",
+                       "bytes_per_step": per_step_bytes},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    plan.close()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

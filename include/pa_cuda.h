@@ -10,6 +10,7 @@
  *                          + the engine's page batching   phone-attn/pa-metal.mm:627-714
  *   pa_cuda_merge          pa_merge / pa_merge_big        phone-attn/pa-metal.mm:137-159, 490-524
  *                          merge_partial                  phone-attn/phone-attn.h:231-239
+ *   pa_cuda_merge_gathered the multi-phone merge           docs/TWO-PHONES.md:14-18 (host loop in the absent llama.cpp)
  *   pa_cuda_normalize      attn_core's O/l, lse           phone-attn/phone-attn.h:651-655
  *   pa_cuda_scale_q        f16(q * scale)                 phone-attn/phone-attn.h:595-599, scripts/sme/sme_attn.c:276-280
  *   pa_cuda_alloc_page,
@@ -106,6 +107,11 @@ uint32_t pa_cuda_plan_launches(const pa_cuda_plan *plan);
  * Asynchronous. */
 int pa_cuda_plan_run(pa_cuda_plan *plan, const uint16_t *Qs, float *O, float *m, float *l, void *stream);
 void pa_cuda_plan_destroy(pa_cuda_plan *plan);
+/* Kernel timing (as the reference engine reads GPUStartTime/GPUEndTime, phone-attn/pa-metal.mm:938-945): with
+ * max_runs > 0, each of the next max_runs runs records CUDA events around its decode kernel on the run's stream;
+ * pa_cuda_plan_kernel_ms waits for them, returns their summed duration and count, and rearms. 0 turns it off. */
+int pa_cuda_plan_profile(pa_cuda_plan *plan, uint32_t max_runs);
+int pa_cuda_plan_kernel_ms(pa_cuda_plan *plan, double *total_ms, uint32_t *n_runs);
 
 /* One-shot: plan, run, free (allocates; synchronises the stream before freeing the plan). */
 int pa_cuda_attn(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, const uint16_t *Qs, uint32_t n_sets,
@@ -126,6 +132,12 @@ int pa_cuda_plan_run_host(pa_cuda_plan *plan, const uint16_t *Qs_host, float *O_
  * fold = 1: (O, m, l) already hold a partial, folded in as one more part (merge_partial / pa_merge_big fold). */
 int pa_cuda_merge(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, uint32_t n_parts, const float *Op, const float *mp,
                   const float *lp, float *O, float *m, float *l, int fold, void *stream);
+/* The same merge over partials packed back to back as one all-gather of each part's (O, m, l) delivers them:
+ * part c = packed + c * rows*(hd+2): O [rows][hd], then m [rows], then l [rows]. This folds the N position shards of
+ * a multi-GPU call (one process per GPU, the partials exchanged with a single NCCL all-gather), generalising the
+ * Mac + phone and two-phone split (docs/TWO-PHONES.md:14-18). */
+int pa_cuda_merge_gathered(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, uint32_t n_parts, const float *packed,
+                           float *O, float *m, float *l, int fold, void *stream);
 /* O/l -> f16 Oh, lse = m + log l (device) */
 int pa_cuda_normalize(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, const float *O, const float *m, const float *l,
                       uint16_t *Oh, float *lse, void *stream);

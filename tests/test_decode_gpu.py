@@ -38,14 +38,14 @@ def _run(ctx, c, nk=None, segs_split=None):
     return O[0].cpu().numpy(), m[0].cpu().numpy(), l[0].cpu().numpy()
 
 
-def _check(c, O, m, l, nk):
+def _check(c, O, m, l, nk, tol_f64=TOL_F64):
     sh = c["shape"]
     Of, mf, lf = orc.partial_f64(sh, c["Qs"], c["K"], c["V"], nk)
     O3, m3, l3 = orc.partial_f32(sh, c["Qs"], c["K"], c["V"], nk)
     e64 = orc.rel_err(O, m, l, Of, mf, lf)
     e32 = orc.rel_err(O, m, l, O3.astype(np.float64), m3.astype(np.float64), l3.astype(np.float64))
     assert e32[0] <= TOL_REF and e32[1] <= TOL_REF, ("vs reference arithmetic", e32)
-    assert e64[0] <= TOL_F64 and e64[1] <= TOL_F64, ("vs fp64", e64)
+    assert e64[0] <= tol_f64 and e64[1] <= tol_f64, ("vs fp64", e64)
     if nk == 0:
         assert np.all(l == 0) and np.all(np.isneginf(m)) and np.all(O == 0)
     return e32, e64
@@ -85,9 +85,12 @@ def test_student_t_values_and_large_scores(ctx):
     c = orc.gen_case(4, 128, 8, 5, 3000, orc.Q8_0, student_t=True)
     O, m, l = _run(ctx, c)
     _check(c, O, m, l, 3000)
+    # scale 0.5 instead of 1/sqrt(128): scores reach ~40, and the reference's f16 rounding of K alone moves them by
+    # up to |s| * 2^-11 (~0.02): against exact fp64 the gate scales with the score range; against the reference's
+    # own arithmetic it stays 2e-3
     c = orc.gen_case(5, 128, 8, 5, 3000, orc.Q8_0, scale=0.5)
     O, m, l = _run(ctx, c)
-    _check(c, O, m, l, 3000)
+    _check(c, O, m, l, 3000, tol_f64=2e-2)
 
 
 def test_segments_fold_like_one_run(ctx):
