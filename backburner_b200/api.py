@@ -144,11 +144,14 @@ def _ptr(t) -> int:
     return 0 if t is None else int(t.data_ptr())
 
 
-def _stream_ptr(stream) -> int | None:
+def _stream_ptr(stream) -> int:
+    """cudaStream_t handle for a torch stream (None: torch's current stream). torch's default stream has handle 0,
+    which the C ABI reads as "the context's own stream", so it is passed as cudaStreamLegacy (1) instead."""
     if stream is None:
         import torch
-        return int(torch.cuda.current_stream().cuda_stream)
-    return int(getattr(stream, "cuda_stream", stream))
+        stream = torch.cuda.current_stream()
+    h = int(getattr(stream, "cuda_stream", stream))
+    return h if h != 0 else 1
 
 
 class Context:

@@ -120,7 +120,7 @@ int plan_decode_shape(pa_cuda_ctx *ctx, pa_cuda_plan *p) {
     if ((str / 16) % 2 == 0) str += 16;
     p->str = str;
     p->smem = (size_t) pa::dec::NSTAGE * 2 * pa::dec::STAGE_KEYS * str + pa::dec::SMEM_SLACK +
-              (2 * pa::dec::NSTAGE + 3) * 8 + 16;
+              (pa::dec::NSTAGE + 3) * 8 + 2 * pa::dec::NSTAGE * 4 + 16;
     if (p->smem > (size_t) kMaxSmem) return fail(ctx, PA_CUDA_EUNSUPPORTED, "rows of this head group do not fit shared memory");
     return PA_CUDA_OK;
 }
@@ -131,7 +131,7 @@ cudaError_t launch_decode(const pa_cuda_plan *p, const pa::dec::Params &prm, cud
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) p->smem);
     if (e != cudaSuccess) return e;
     dim3 grid(p->n_jobs, p->grid_y);
-    kern<<<grid, 32 * (p->n_consumers + 1), p->smem, st>>>(prm);
+    kern<<<grid, 32 * p->n_consumers, p->smem, st>>>(prm);
     return cudaGetLastError();
 }
 

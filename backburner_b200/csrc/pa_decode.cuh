@@ -7,9 +7,10 @@
 // (pa-metal.mm:452-464). Output per chunk of keys: the unnormalised partial (O, m, l); pa_merge.cuh folds chunks.
 //
 // B200 design (one CTA = one key chunk x a group of heads x a group of query rows):
-//   * a producer warp streams each 32-key stage of K and V rows from HBM into shared memory with 1-D bulk copies
-//     (TMA engine), one copy per key row, into rows padded to an odd number of 16-byte units so the consumers'
-//     32-bit reads hit at most 2 lanes per bank; full/empty mbarriers ring NSTAGE stages;
+//   * each 32-key stage of K and V rows is streamed from HBM into shared memory with 1-D bulk copies (TMA engine), one
+//     copy per key row, into rows padded to an odd number of 16-byte units so the warps' 32-bit reads hit at most 2
+//     lanes per bank; NSTAGE stages ring on "full" mbarriers; the last warp to finish with a stage (a shared counter)
+//     refills it, so there is no producer warp and every warp of the CTA computes (16 warps: 128 registers each);
 //   * each consumer warp owns one (head, 8-row group) and, when there are few such groups, every other 16-key tile;
 //   * the raw int8/int4 bytes go straight from shared memory into registers and are dequantised there into the
 //     operand fragments of mma.m16n8k16 (f16 in, fp32 accumulate), keys on the M side ("swap AB"):
@@ -24,7 +25,7 @@
 namespace pa {
 namespace dec {
 
-constexpr int STAGE_KEYS = 32;   // keys per pipeline stage (= lanes of the producer warp)
+constexpr int STAGE_KEYS = 32;   // keys per pipeline stage (= lanes of the warp that issues its copies)
 constexpr int TILE_KEYS = 16;    // keys per MMA tile
 constexpr int NSTAGE = 3;
 constexpr int SMEM_SLACK = 64;   // readable bytes past the last row (a lane may load one unused word there)
@@ -50,7 +51,7 @@ struct Params {
     uint32_t n_rg;        // 8-row groups in total = ceil(rows / 8)
     uint32_t str;         // shared-memory row stride (bytes, multiple of 16, odd number of 16-byte units)
     uint32_t pw;          // consumer warps per (head, row group): 1 or 2 (they split the 16-key tiles)
-    uint32_t n_consumers; // consumer warps per CTA (launch shape)
+    uint32_t n_consumers; // warps per CTA (launch shape)
     uint64_t timeout_ns;
     int stall;            // test hook: consumers first wait on a barrier that nothing completes (bounded)
 };
@@ -115,7 +116,7 @@ __device__ __forceinline__ void q4_word(uint32_t w, uint32_t s2, uint32_t &l02, 
 
 // ---------------------------------------------------------------- the kernel
 template <int HD, int QUANT>
-__global__ void __launch_bounds__(32 * (HD == 128 ? 17 : 13), 1) decode_kernel(const Params p) {
+__global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(const Params p) {
     constexpr int NMT = HD / 16;   // k-steps of QK^T = m-tiles of P.V
     constexpr int GB = q_group_bytes(QUANT);
     constexpr int PAIR = 2 * GB;   // bytes of an aligned pair of quant blocks
@@ -124,11 +125,12 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 17 : 13), 1) decode_kernel(c
     const uint32_t str = p.str;
     const uint32_t stage_bytes = 2u * STAGE_KEYS * str;   // K rows then V rows
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + NSTAGE * stage_bytes + SMEM_SLACK);
-    uint64_t *empty = full + NSTAGE;
-    uint64_t *done = empty + NSTAGE;   // every active consumer is past the pipeline (stage memory is free)
+    uint64_t *done = full + NSTAGE;    // every active warp is past the pipeline (stage memory is free)
     uint64_t *xchg = done + 1;         // the second warp of each (head, row group) pair has published its partial
     uint64_t *never = xchg + 1;        // completed by nobody: the stall test hook waits on it
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(never + 1);
+    uint32_t *released = reinterpret_cast<uint32_t *>(never + 1);   // per buffer: warps done with it, ever
+    uint32_t *issued = released + NSTAGE;                            // per buffer: the last stage issued into it
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(issued + NSTAGE);
 
     const Job job = p.jobs[blockIdx.x];
     const uint32_t n_hgroups = p.nkv / p.hg;
@@ -137,13 +139,15 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 17 : 13), 1) decode_kernel(c
     const uint32_t rg0 = rbi * p.rgc;
     const uint32_t nrg = min(p.rgc, p.n_rg - rg0);
     const uint32_t S = p.hg * nrg;                // (head, row group) streams in this CTA
-    const uint32_t n_active = S * p.pw;           // consumer warps with work
+    const uint32_t n_active = S * p.pw;           // warps with work
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const uint32_t n_stages = (job.nk + STAGE_KEYS - 1) / STAGE_KEYS;
     const uint32_t copy_bytes = (uint32_t) (p.hg * p.hb);
+    const uint8_t *kb = job.k + (uint64_t) job.key0 * p.rs + h0 * p.hb;
+    const uint8_t *vb = job.v + (uint64_t) job.key0 * p.rs + h0 * p.hb;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < NSTAGE; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], n_active); }
+        for (int s = 0; s < NSTAGE; s++) { mbar_init(&full[s], 1); released[s] = 0; issued[s] = 0; }
         mbar_init(done, n_active);
         mbar_init(xchg, S);
         mbar_init(never, 1);
@@ -151,47 +155,41 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 17 : 13), 1) decode_kernel(c
         fence_mbar_init();
     }
     __syncthreads();
-
-    if (warp == p.n_consumers) {
-        // ------------------------------------------------ producer warp
-        const uint8_t *kb = job.k + (uint64_t) job.key0 * p.rs + h0 * p.hb;
-        const uint8_t *vb = job.v + (uint64_t) job.key0 * p.rs + h0 * p.hb;
-        uint32_t issued = 0;
-        bool ok = true;
-        for (uint32_t it = 0; it < n_stages; it++) {
-            const uint32_t s = it % NSTAGE;
-            if (it >= NSTAGE) {
-                bool w = true;
-                if (lane == 0) w = mbar_wait_bounded(&empty[s], ((it / NSTAGE) & 1) ^ 1, p.timeout_ns, abort_flag);
-                w = __shfl_sync(0xffffffffu, w, 0);
-                if (!w) { ok = false; break; }
-            }
-            const uint32_t valid = min((uint32_t) STAGE_KEYS, job.nk - it * STAGE_KEYS);
-            if (lane == 0) mbar_arrive_expect_tx(&full[s], 2u * valid * copy_bytes);
-            __syncwarp();
-            if (lane < valid) {
-                const uint64_t off = (uint64_t) (it * STAGE_KEYS + lane) * p.rs;
-                uint8_t *dst = smem + s * stage_bytes + lane * str;
-                bulk_g2s(dst, kb + off, copy_bytes, &full[s]);
-                bulk_g2s(dst + STAGE_KEYS * str, vb + off, copy_bytes, &full[s]);
-            }
-            issued = it + 1;
-        }
-        if (!ok) {
-            // consumers gave up: let the copies already issued land before the CTA exits
-            if (lane == 0) {
-                *abort_flag = 1;
-                atomicCAS(p.status, ST_OK, ST_TIMEOUT_EMPTY);
-                const uint32_t first = issued > NSTAGE ? issued - NSTAGE : 0;
-                const uint64_t drain_ns = p.timeout_ns > DRAIN_NS ? p.timeout_ns : DRAIN_NS;
-                for (uint32_t it = first; it < issued; it++)
-                    if (!mbar_wait_bounded(&full[it % NSTAGE], (it / NSTAGE) & 1, drain_ns, nullptr))
-                        atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
-            }
-        }
-        return;
-    }
     if (warp >= n_active) return;
+
+    // stage `it` into buffer it % NSTAGE: K rows then V rows, one bulk copy per key row (warp-collective)
+    auto issue = [&](uint32_t it) {
+        const uint32_t s = it % NSTAGE;
+        const uint32_t valid = min((uint32_t) STAGE_KEYS, job.nk - it * STAGE_KEYS);
+        if (lane == 0) {
+            issued[s] = it;
+            mbar_arrive_expect_tx(&full[s], 2u * valid * copy_bytes);
+        }
+        __syncwarp();
+        if (lane < valid) {
+            const uint64_t off = (uint64_t) (it * STAGE_KEYS + lane) * p.rs;
+            uint8_t *dst = smem + s * stage_bytes + lane * str;
+            bulk_g2s(dst, kb + off, copy_bytes, &full[s]);
+            bulk_g2s(dst + STAGE_KEYS * str, vb + off, copy_bytes, &full[s]);
+        }
+    };
+    // after a wait gave up: every copy issued so far lands before the CTA exits (warp 0 waits for them, bounded)
+    auto abort_and_drain = [&]() {
+        if (lane == 0) {
+            *abort_flag = 1;
+            atomicCAS(p.status, ST_OK, ST_TIMEOUT_FULL);
+        }
+        if (warp == 0 && lane == 0) {
+            const uint64_t drain_ns = p.timeout_ns > DRAIN_NS ? p.timeout_ns : DRAIN_NS;
+            for (int s = 0; s < NSTAGE && s < (int) n_stages; s++) {
+                const uint32_t it = ((volatile uint32_t *) issued)[s];
+                if (!mbar_wait_bounded(&full[s], (it / NSTAGE) & 1, drain_ns, nullptr))
+                    atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
+            }
+        }
+    };
+    if (warp == 0)
+        for (uint32_t it = 0; it < NSTAGE && it < n_stages; it++) issue(it);
 
     // ------------------------------------------------ consumer warps
     const uint32_t stream = warp % S, par = warp / S;
@@ -368,11 +366,22 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 17 : 13), 1) decode_kernel(c
                 }
             }
         }
+        // release the buffer; the last warp to do so refills it with stage it + NSTAGE
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        uint32_t last = 0;
+        if (lane == 0) {
+            __threadfence_block();   // this warp's reads of the buffer are ordered before its count
+            last = (atomicAdd(&released[s], 1u) + 1u) % n_active == 0;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last && it + NSTAGE < n_stages) {
+            __threadfence_block();
+            fence_proxy_async();     // ... and before the bulk copies (async proxy) that overwrite it
+            issue(it + NSTAGE);
+        }
     }
     if (!ok) {
-        if (lane == 0) { *abort_flag = 1; atomicCAS(p.status, ST_OK, ST_TIMEOUT_FULL); }
+        abort_and_drain();
         return;
     }
 
@@ -392,7 +401,7 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 17 : 13), 1) decode_kernel(c
             bool w = true;
             if (lane == 0) w = mbar_wait_bounded(done, 0, p.timeout_ns, abort_flag);
             if (!__shfl_sync(0xffffffffu, w, 0)) {
-                if (lane == 0) { *abort_flag = 1; atomicCAS(p.status, ST_OK, ST_TIMEOUT_FULL); }
+                abort_and_drain();
                 return;
             }
 #pragma unroll
@@ -410,7 +419,7 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 17 : 13), 1) decode_kernel(c
         bool w = true;
         if (lane == 0) w = mbar_wait_bounded(xchg, 0, p.timeout_ns, abort_flag);
         if (!__shfl_sync(0xffffffffu, w, 0)) {
-            if (lane == 0) { *abort_flag = 1; atomicCAS(p.status, ST_OK, ST_TIMEOUT_FULL); }
+            abort_and_drain();
             return;
         }
         const float pm0 = xb[(NMT * 4 + 0) * 32 + lane], pm1 = xb[(NMT * 4 + 1) * 32 + lane];

@@ -1,0 +1,47 @@
+"""The drop-in surface end to end: the reference's own pa::server (phone-attn/phone-attn.h, unmodified) with
+pa::cuda_engine as its GPU engine (oracle/_ref/pa-serve-cuda), driven over loopback TCP by the reference's own
+`pa-tool test` client, which checks layer 0 against its fp64 reference and prints PASS/FAIL at its 5e-3 gate
+(phone-attn/pa-tool.cpp:150-173), plus its ATTN_BIG-vs-ATTN consistency check (phone-attn/pa-tool.cpp:230-238).
+Both binaries are built from the reference sources by oracle/Makefile."""
+import os
+import socket
+import subprocess
+import time
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REF = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle", "_ref")
+SERVE, TOOL = os.path.join(REF, "pa-serve-cuda"), os.path.join(REF, "pa-tool")
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.mark.skipif(not (os.path.exists(SERVE) and os.path.exists(TOOL)),
+                    reason="oracle/_ref binaries not built (they need the reference tree at build time)")
+@pytest.mark.parametrize("env,nkeys", [({}, 16384), ({"PA_Q4": "1"}, 16384), ({"PA_NTOK": "1"}, 16384),
+                                       ({"PA_NTOK": "3"}, 8192), ({"PA_BIG_TOK": "64"}, 8192),
+                                       ({"PA_Q4": "1", "PA_BIG_TOK": "24"}, 4096)])
+def test_reference_pa_tool_against_cuda_engine(env, nkeys):
+    port = _free_port()
+    srv = subprocess.Popen([SERVE, str(port), "2"], stdout=subprocess.DEVNULL, stderr=subprocess.PIPE, text=True)
+    try:
+        time.sleep(1.0)
+        assert srv.poll() is None, srv.stderr.read()
+        out = subprocess.run([TOOL, "test", "127.0.0.1", str(port), str(nkeys), "4", "4"], env=dict(os.environ, **env),
+                             capture_output=True, text=True, timeout=300)
+        text = out.stdout + out.stderr
+        assert out.returncode == 0, text
+        assert "-> PASS" in text and "FAIL" not in text, text
+        assert "engine=pa-cuda" in text, text
+        print(text)
+    finally:
+        srv.kill()
+        srv.wait()
