@@ -51,6 +51,7 @@ _SIGS = {
     "pa_cuda_set_timeout_ns": (None, [_P, ctypes.c_uint64]),
     "pa_cuda_launch_count": (ctypes.c_uint64, [_P]),
     "pa_cuda_set_stall_test": (None, [_P, ctypes.c_int]),
+    "pa_cuda_set_kernel": (None, [_P, ctypes.c_int]),
     "pa_cuda_plan_create": (ctypes.c_int, [_P, ctypes.POINTER(_Shape), ctypes.c_uint32, ctypes.POINTER(_Seg),
                                            ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(_P)]),
     "pa_cuda_plan_scratch_bytes": (ctypes.c_size_t, [_P]),
@@ -179,6 +180,10 @@ class Context:
 
     def set_timeout_ns(self, ns: int):
         lib().pa_cuda_set_timeout_ns(self._h, int(ns))
+
+    def set_kernel(self, which: int):
+        """0: by shape; 1: split-K mma.sync kernel; 2: tcgen05 kernel (hd 128) — for plans created afterwards."""
+        lib().pa_cuda_set_kernel(self._h, int(which))
 
     def set_stall_test(self, on: bool):
         """Failure-detection hook: the next decode kernels wait on a barrier nothing completes (bounded)."""

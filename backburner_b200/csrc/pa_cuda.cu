@@ -3,7 +3,9 @@
 // device status word that bounded in-kernel waits report into.
 #include "pa_cuda.h"
 
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <chrono>
@@ -14,10 +16,12 @@
 
 #include "pa_decode.cuh"
 #include "pa_merge.cuh"
+#include "pa_prefill.cuh"
 
 namespace {
 
 constexpr int kMaxSmem = 227 * 1024;
+constexpr uint32_t kPrefillMinRows = 64;   // query rows per KV head from which the tcgen05 kernel is used
 
 struct Plan;
 
@@ -31,6 +35,7 @@ struct pa_cuda_ctx {
     uint64_t timeout_ns = 2000000000ull;
     uint64_t launches = 0;
     int stall_test = 0;
+    int kernel_choice = 0;   // 0 auto, 1 split-K mma.sync kernel, 2 tcgen05 kernel
     std::string err;
     // pa::engine state (begin/end)
     pa_cuda_plan *eng_plan = nullptr;
@@ -57,8 +62,13 @@ struct pa_cuda_plan {
     float *d_op = nullptr, *d_mp = nullptr, *d_lp = nullptr;
     size_t scratch = 0;
     // decode launch shape
-    uint32_t hg = 1, rgc = 1, n_rg = 1, pw = 1, n_consumers = 1, str = 0, grid_y = 1;
+    uint32_t hg = 1, rgc = 1, n_rg = 1, pw = 1, n_consumers = 1, row = 0, gs = 0, grid_y = 1;
     size_t smem = 0;
+    // tcgen05 path (many query rows per KV head, hd 128): tiles of NT x 128 rows, tensor maps of the K/V segments
+    bool prefill = false;
+    int nt = 1;
+    uint32_t n_rt = 0;
+    CUtensorMap *d_maps = nullptr;
     // profiling: event pairs around the decode kernel of each run (a ring, summed by pa_cuda_plan_kernel_ms)
     bool profile = false;
     std::vector<cudaEvent_t> ev;
@@ -116,13 +126,62 @@ int plan_decode_shape(pa_cuda_ctx *ctx, pa_cuda_plan *p) {
     p->pw = 2 * S <= maxw ? 2 : 1;
     p->n_consumers = S * p->pw;
     p->grid_y = (sh.nkv / hg) * ((p->n_rg + p->rgc - 1) / p->rgc);
-    uint32_t str = (uint32_t) ((hg * sh.hb + 15) / 16 * 16);
-    if ((str / 16) % 2 == 0) str += 16;
-    p->str = str;
-    p->smem = (size_t) pa::dec::NSTAGE * 2 * pa::dec::STAGE_KEYS * str + pa::dec::SMEM_SLACK +
+    p->row = (uint32_t) (hg * sh.hb);                  // a multiple of 16 by the choice of hg
+    uint32_t gs = 2 * p->row;
+    if ((gs / 16) % 2 == 0) gs += 16;                 // odd number of 16-byte units per pair
+    p->gs = gs;
+    p->smem = (size_t) pa::dec::NSTAGE * pa::dec::STAGE_KEYS * gs + pa::dec::SMEM_SLACK +
               (pa::dec::NSTAGE + 3) * 8 + 2 * pa::dec::NSTAGE * 4 + 16;
     if (p->smem > (size_t) kMaxSmem) return fail(ctx, PA_CUDA_EUNSUPPORTED, "rows of this head group do not fit shared memory");
     return PA_CUDA_OK;
+}
+
+// ------------------------------------------------------------------ tensor maps (driver entry point, no -lcuda)
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return (PFN_cuTensorMapEncodeTiled_v12000) f;
+    }();
+    return fn;
+}
+// quantised rows of one segment as a 2-D u8 tensor {rs bytes, nk keys}; a box is one head's 16-byte-aligned window
+bool map_rows(CUtensorMap *m, const void *base, uint64_t rs, uint32_t nk, uint32_t raw_bytes) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {rs, nk};
+    const cuuint64_t strides[1] = {rs};
+    const cuuint32_t box[2] = {raw_bytes, (cuuint32_t) pa::pre::BN};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// Qs [all rows][128] f16 with the 128-byte swizzle of the UMMA operand layout; a box is 64 dims x 128 rows
+bool map_q(CUtensorMap *m, const void *Qs, uint64_t n_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {128, n_rows};
+    const cuuint64_t strides[1] = {256};
+    const cuuint32_t box[2] = {64, (cuuint32_t) pa::pre::BM};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(Qs), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int Q, int NT>
+cudaError_t launch_prefill(const pa_cuda_plan *p, const CUtensorMap &tq, const pa::pre::Params &prm, cudaStream_t st) {
+    auto kern = pa::pre::prefill_kernel<Q, NT>;
+    constexpr int smem = pa::pre::Smem<Q, NT>::TOTAL + 1024;   // + alignment slack for the 1024-byte operand tiles
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid(p->n_jobs, p->sh.nkv * p->n_rt);
+    kern<<<grid, 32 * (6 + 4 * NT), smem, st>>>(tq, prm);
+    return cudaGetLastError();
 }
 
 template <int HD, int Q>
@@ -146,7 +205,35 @@ cudaError_t launch_merge(const pa::mrg::Params &mp, cudaStream_t st) {
 int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, cudaStream_t st) {
     pa_cuda_ctx *ctx = p->ctx;
     const pa_cuda_shape &sh = p->sh;
-    if (p->n_jobs > 0) {
+    if (p->n_jobs > 0 && p->prefill) {
+        CUtensorMap tq;
+        if (!map_q(&tq, Qs, (uint64_t) p->n_sets * sh.nkv * sh.rows))
+            return fail(ctx, PA_CUDA_ECUDA, "cuTensorMapEncodeTiled (Q) failed");
+        pa::pre::Params prm{};
+        prm.jobs = p->d_jobs;
+        prm.kv_maps = p->d_maps;
+        prm.Op = p->d_op;
+        prm.Mp = p->d_mp;
+        prm.Lp = p->d_lp;
+        prm.status = ctx->d_status;
+        prm.rs = sh.rs;
+        prm.hb = sh.hb;
+        prm.nkv = sh.nkv;
+        prm.rows = sh.rows;
+        prm.n_rt = p->n_rt;
+        prm.timeout_ns = ctx->timeout_ns;
+        const bool prof = p->profile && p->ev_used + 2 <= p->ev.size();
+        if (prof) cudaEventRecord(p->ev[p->ev_used], st);
+        cudaError_t e;
+        if (sh.quant == PA_CUDA_Q8_0) e = p->nt == 2 ? launch_prefill<1, 2>(p, tq, prm, st) : launch_prefill<1, 1>(p, tq, prm, st);
+        else e = p->nt == 2 ? launch_prefill<2, 2>(p, tq, prm, st) : launch_prefill<2, 1>(p, tq, prm, st);
+        if (e != cudaSuccess) return cuda_fail(ctx, e, "prefill kernel launch");
+        if (prof) {
+            cudaEventRecord(p->ev[p->ev_used + 1], st);
+            p->ev_used += 2;
+        }
+        ctx->launches++;
+    } else if (p->n_jobs > 0) {
         pa::dec::Params prm{};
         prm.jobs = p->d_jobs;
         prm.Qs = Qs;
@@ -161,7 +248,8 @@ int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, 
         prm.hg = p->hg;
         prm.rgc = p->rgc;
         prm.n_rg = p->n_rg;
-        prm.str = p->str;
+        prm.row = p->row;
+        prm.gs = p->gs;
         prm.pw = p->pw;
         prm.n_consumers = p->n_consumers;
         prm.timeout_ns = ctx->timeout_ns;
@@ -290,6 +378,10 @@ void pa_cuda_set_timeout_ns(pa_cuda_ctx *ctx, uint64_t ns) {
 
 uint64_t pa_cuda_launch_count(const pa_cuda_ctx *ctx) { return ctx ? ctx->launches : 0; }
 
+void pa_cuda_set_kernel(pa_cuda_ctx *ctx, int which) {
+    if (ctx) ctx->kernel_choice = which;
+}
+
 void pa_cuda_set_stall_test(pa_cuda_ctx *ctx, int on) {
     if (ctx) ctx->stall_test = on ? 1 : 0;
 }
@@ -320,6 +412,16 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
     p->sh = *shape;
     p->n_sets = n_sets;
     if ((rc = plan_decode_shape(ctx, p))) { delete p; return rc; }
+    // the tcgen05 kernel takes calls with many query rows per KV head (prefill, ATTN_BIG, long verify batches), the
+    // split-K kernel the decode-sized ones (as the reference engine switches kernels by rows, pa-metal.mm:818-835)
+    const bool tc_ok = shape->hd == 128 && encode_fn() != nullptr;
+    p->prefill = tc_ok && (ctx->kernel_choice == 2 || (ctx->kernel_choice == 0 && shape->rows >= kPrefillMinRows));
+    if (ctx->kernel_choice == 2 && !tc_ok) { delete p; return fail(ctx, PA_CUDA_EUNSUPPORTED, "tcgen05 kernel needs hd 128"); }
+    if (p->prefill) {
+        p->nt = shape->rows > (uint32_t) pa::pre::BM ? 2 : 1;
+        p->n_rt = (shape->rows + pa::pre::BM * p->nt - 1) / (pa::pre::BM * p->nt);
+        p->grid_y = shape->nkv * p->n_rt;
+    }
 
     uint64_t total = 0;
     for (uint32_t i = 0; i < n_segs; i++) {
@@ -331,12 +433,16 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
         total += segs[i].nk;
     }
     uint32_t chunk = chunk_keys;
-    if (chunk == 0) {
+    if (chunk == 0 && p->prefill) {
+        // at least ~4 CTAs per SM in total, >= 1024 keys per job
+        const uint64_t jobs_wanted = std::max<uint64_t>(1, ((uint64_t) ctx->n_sm * 4 + p->grid_y - 1) / p->grid_y);
+        chunk = (uint32_t) std::max<uint64_t>(1024, (total + jobs_wanted - 1) / jobs_wanted);
+    } else if (chunk == 0) {
         // about 16 waves of CTAs over the SMs (one CTA per SM), 128..16384 keys per job
         const uint64_t per_y = std::max<uint64_t>(1, (uint64_t) ctx->n_sm * 16 / std::max<uint32_t>(1, p->grid_y));
         chunk = (uint32_t) std::min<uint64_t>(16384, std::max<uint64_t>(128, (total + per_y - 1) / per_y));
     }
-    chunk = (chunk + 31) / 32 * 32;
+    chunk = (chunk + 63) / 64 * 64;
 
     // jobs grouped by set, so that the slots of a set are contiguous
     std::vector<pa::dec::Job> jobs;
@@ -347,7 +453,7 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
             if (segs[i].set != s || segs[i].nk == 0) continue;
             const uint32_t nk = segs[i].nk;
             const uint32_t nj = (nk + chunk - 1) / chunk;
-            const uint32_t cj = ((nk + nj - 1) / nj + 31) / 32 * 32;   // equal chunks of whole stages
+            const uint32_t cj = ((nk + nj - 1) / nj + 63) / 64 * 64;   // equal chunks of whole stages / blocks
             for (uint32_t k0 = 0; k0 < nk; k0 += cj) {
                 pa::dec::Job j;
                 j.k = segs[i].k;
@@ -356,6 +462,8 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
                 j.nk = std::min(cj, nk - k0);
                 j.set = s;
                 j.slot = (uint32_t) jobs.size();
+                j.seg = i;
+                j.pad_ = 0;
                 jobs.push_back(j);
             }
         }
@@ -377,6 +485,20 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
     }
     if (e == cudaSuccess && (e = cudaMalloc((void **) &p->d_crange, crange.size() * 4)) == cudaSuccess)
         e = cudaMemcpy(p->d_crange, crange.data(), crange.size() * 4, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && p->prefill && n_segs) {
+        std::vector<CUtensorMap> maps(2 * (size_t) n_segs);
+        const uint32_t rawb = (uint32_t) pa::pre::raw_row_bytes((int) shape->quant);
+        for (uint32_t i = 0; i < n_segs; i++) {
+            if (!segs[i].nk) continue;
+            if (!map_rows(&maps[2 * i], segs[i].k, shape->rs, segs[i].nk, rawb) ||
+                !map_rows(&maps[2 * i + 1], segs[i].v, shape->rs, segs[i].nk, rawb)) {
+                pa_cuda_plan_destroy(p);
+                return fail(ctx, PA_CUDA_ECUDA, "cuTensorMapEncodeTiled (K/V rows) failed");
+            }
+        }
+        if ((e = cudaMalloc((void **) &p->d_maps, maps.size() * sizeof(CUtensorMap))) == cudaSuccess)
+            e = cudaMemcpy(p->d_maps, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice);
+    }
     if (e != cudaSuccess) {
         pa_cuda_plan_destroy(p);
         return fail(ctx, PA_CUDA_ENOMEM, std::string("plan allocation: ") + cudaGetErrorString(e));
@@ -435,6 +557,7 @@ void pa_cuda_plan_destroy(pa_cuda_plan *p) {
     for (auto e : p->ev) cudaEventDestroy(e);
     if (p->d_jobs) cudaFree(p->d_jobs);
     if (p->d_crange) cudaFree(p->d_crange);
+    if (p->d_maps) cudaFree(p->d_maps);
     if (p->d_op) cudaFree(p->d_op);
     if (p->d_mp) cudaFree(p->d_mp);
     if (p->d_lp) cudaFree(p->d_lp);

@@ -8,9 +8,12 @@
 //
 // B200 design (one CTA = one key chunk x a group of heads x a group of query rows):
 //   * each 32-key stage of K and V rows is streamed from HBM into shared memory with 1-D bulk copies (TMA engine), one
-//     copy per key row, into rows padded to an odd number of 16-byte units so the warps' 32-bit reads hit at most 2
-//     lanes per bank; NSTAGE stages ring on "full" mbarriers; the last warp to finish with a stage (a shared counter)
-//     refills it, so there is no producer warp and every warp of the CTA computes (16 warps: 128 registers each);
+//     copy per PAIR of key rows (requests of one 1 KB row cap a B200 at ~5.4 TB/s, two rows reach ~7.4 TB/s), pairs
+//     padded to an odd number of 16-byte units; NSTAGE stages ring on "full" mbarriers; the last warp to finish with a
+//     stage (a shared counter) refills it, so there is no producer warp and every warp of the CTA computes (16 warps:
+//     128 registers each);
+//   * the MMA's 16 key rows are ordered even keys first (row g = key 2g, row g+8 = key 2g+1): with the pair layout
+//     every 32-bit shared-memory read of K and V hits at most 2 lanes per bank;
 //   * each consumer warp owns one (head, 8-row group) and, when there are few such groups, every other 16-key tile;
 //   * the raw int8/int4 bytes go straight from shared memory into registers and are dequantised there into the
 //     operand fragments of mma.m16n8k16 (f16 in, fp32 accumulate), keys on the M side ("swap AB"):
@@ -36,6 +39,7 @@ struct Job {
     const uint8_t *k, *v;   // segment base (key 0 of the segment)
     uint32_t key0, nk;      // keys [key0, key0 + nk) of the segment
     uint32_t set, slot;     // output set (selects Q) and partial slot
+    uint32_t seg, pad_;     // segment index (selects the tensor maps of the tcgen05 kernel)
 };
 
 struct Params {
@@ -49,7 +53,8 @@ struct Params {
     uint32_t hg;          // heads per CTA
     uint32_t rgc;         // 8-row groups per CTA
     uint32_t n_rg;        // 8-row groups in total = ceil(rows / 8)
-    uint32_t str;         // shared-memory row stride (bytes, multiple of 16, odd number of 16-byte units)
+    uint32_t row;         // bytes of one key row in shared memory (= hg * hb, a multiple of 16)
+    uint32_t gs;          // shared-memory stride of a pair of key rows (multiple of 16, odd number of 16-byte units)
     uint32_t pw;          // consumer warps per (head, row group): 1 or 2 (they split the 16-key tiles)
     uint32_t n_consumers; // warps per CTA (launch shape)
     uint64_t timeout_ns;
@@ -122,8 +127,11 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
     constexpr int PAIR = 2 * GB;   // bytes of an aligned pair of quant blocks
 
     extern __shared__ __align__(128) uint8_t smem[];
-    const uint32_t str = p.str;
-    const uint32_t stage_bytes = 2u * STAGE_KEYS * str;   // K rows then V rows
+    const uint32_t row = p.row, gs = p.gs;
+    const uint32_t half_stage = (STAGE_KEYS / 2) * gs;    // K pairs, then V pairs
+    const uint32_t stage_bytes = 2u * half_stage;
+    // shared-memory offset of key k of a stage (keys in pairs)
+    auto kofs = [&](uint32_t k) -> uint32_t { return (k / 2) * gs + (k % 2) * row; };
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + NSTAGE * stage_bytes + SMEM_SLACK);
     uint64_t *done = full + NSTAGE;    // every active warp is past the pipeline (stage memory is free)
     uint64_t *xchg = done + 1;         // the second warp of each (head, row group) pair has published its partial
@@ -151,11 +159,12 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
         mbar_init(done, n_active);
         mbar_init(xchg, S);
         mbar_init(never, 1);
-        *abort_flag = 0;
+        // a CTA started after another one gave up a wait does no work (a systematic failure ends in one timeout)
+        *abort_flag = *(volatile int *) p.status != ST_OK;
         fence_mbar_init();
     }
     __syncthreads();
-    if (warp >= n_active) return;
+    if (*abort_flag || warp >= n_active) return;
 
     // stage `it` into buffer it % NSTAGE: K rows then V rows, one bulk copy per key row (warp-collective)
     auto issue = [&](uint32_t it) {
@@ -166,11 +175,12 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
             mbar_arrive_expect_tx(&full[s], 2u * valid * copy_bytes);
         }
         __syncwarp();
-        if (lane < valid) {
-            const uint64_t off = (uint64_t) (it * STAGE_KEYS + lane) * p.rs;
-            uint8_t *dst = smem + s * stage_bytes + lane * str;
-            bulk_g2s(dst, kb + off, copy_bytes, &full[s]);
-            bulk_g2s(dst + STAGE_KEYS * str, vb + off, copy_bytes, &full[s]);
+        if (2 * lane < valid) {   // lane copies keys 2*lane, 2*lane+1 (one row if the stage ends there)
+            const uint64_t off = (uint64_t) (it * STAGE_KEYS + 2 * lane) * p.rs;
+            const uint32_t bytes = (2 * lane + 1 < valid ? 2u : 1u) * copy_bytes;
+            uint8_t *dst = smem + s * stage_bytes + lane * gs;
+            bulk_g2s(dst, kb + off, bytes, &full[s]);
+            bulk_g2s(dst + half_stage, vb + off, bytes, &full[s]);
         }
     };
     // after a wait gave up: every copy issued so far lands before the CTA exits (warp 0 waits for them, bounded)
@@ -225,12 +235,12 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
         if (!mbar_wait_bounded(&full[s], (it / NSTAGE) & 1, p.timeout_ns, abort_flag)) { ok = false; break; }
         const uint32_t valid = min((uint32_t) STAGE_KEYS, job.nk - it * STAGE_KEYS);
         const uint32_t kbase = smem_u32(smem + s * stage_bytes) + hoff;
-        const uint32_t vbase = kbase + STAGE_KEYS * str;
+        const uint32_t vbase = kbase + half_stage;
         for (uint32_t tt = par; tt < STAGE_KEYS / TILE_KEYS; tt += p.pw) {
             const int tvalid = (int) valid - (int) tt * TILE_KEYS;
             if (tvalid <= 0) break;
-            const uint32_t tk = kbase + tt * TILE_KEYS * str;
-            const uint32_t tv = vbase + tt * TILE_KEYS * str;
+            const uint32_t tk = kbase + tt * (TILE_KEYS / 2) * gs;   // the tile's 8 pairs
+            const uint32_t tv = vbase + tt * (TILE_KEYS / 2) * gs;
 
             // ---- S^T = K . Qs^T  (lane: keys g, g+8; its quant block(s) t (+4))
             float c[4] = {0.f, 0.f, 0.f, 0.f};
@@ -243,7 +253,7 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
                 uint32_t w[2][NWK], s2[2];
 #pragma unroll
                 for (int kk = 0; kk < 2; kk++) {
-                    const uint32_t rb = tk + (g + 8 * kk) * str + pb + 4 * (odd ? NWK - 1 : 0);
+                    const uint32_t rb = tk + kofs(2 * g + kk) + pb + 4 * (odd ? NWK - 1 : 0);   // MMA rows g, g+8
 #pragma unroll
                     for (int i = 0; i < NWK; i++) w[kk][i] = lds32(rb + 4 * i);
                     // scale: even block -> first word bytes 0-1; odd block -> first word (shared with the even block) bytes 2-3
@@ -280,8 +290,8 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
 
             // ---- online softmax over this tile (rows 2t, 2t+1; keys g, g+8)
             if (tvalid < TILE_KEYS) {
-                if ((int) g >= tvalid) c[0] = c[1] = -INFINITY;
-                if ((int) g + 8 >= tvalid) c[2] = c[3] = -INFINITY;
+                if ((int) (2 * g) >= tvalid) c[0] = c[1] = -INFINITY;       // row g = key 2g
+                if ((int) (2 * g + 1) >= tvalid) c[2] = c[3] = -INFINITY;   // row g+8 = key 2g+1
             }
             float mx0 = fmaxf(c[0], c[2]), mx1 = fmaxf(c[1], c[3]);
 #pragma unroll
@@ -307,7 +317,8 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
 
             // ---- O^T += V^T . P^T  (lane: keys 2t,2t+1,2t+8,2t+9; head-dim rows dV(mt, g, 0/1))
             {
-                const uint32_t key[4] = {2 * t, 2 * t + 1, 2 * t + 8, 2 * t + 9};
+                // k indices 2t, 2t+1, 2t+8, 2t+9 are MMA rows of S^T, i.e. keys 4t, 4t+2, 4t+1, 4t+3
+                const uint32_t key[4] = {4 * t, 4 * t + 2, 4 * t + 1, 4 * t + 3};
                 // the lane's data bytes start 2 bytes into a word for even quant blocks: load the covering words and
                 // shift them into alignment (funnel shift by 8*sig bits; sig is 0 or 2), so every later index is static
                 constexpr int NB = QUANT == 1 ? (HD == 128 ? 16 : 32) : (HD == 128 ? 8 : 16);   // bytes per lane per key
@@ -322,7 +333,7 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
                 uint32_t W[4][NW];
 #pragma unroll
                 for (int kk = 0; kk < 4; kk++) {
-                    const uint32_t rb = tv + key[kk] * str;
+                    const uint32_t rb = tv + kofs(key[kk]);
                     sc[kk] = lds16(rb + soff);
                     uint32_t raw[NW + 1];
 #pragma unroll

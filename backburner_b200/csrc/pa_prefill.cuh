@@ -1,0 +1,480 @@
+// pa_prefill.cuh - partial attention for many query rows per KV head (prefill / ATTN_BIG calls, long verify
+// batches) on the 5th-generation tensor cores: tcgen05.mma with accumulators in tensor memory (TMEM).
+//
+// Reference semantics: pa_attn_big (phone-attn/pa-metal.mm:379-487), the dense-row kernel the reference runs for
+// prefill: rows of all groups of one KV head packed back to back, K/V blocks dequantised to f16, S = Qs.K^T and
+// O += P.V on the matrix units with fp32 accumulation, online softmax over the valid keys (pa-metal.mm:452-464),
+// one unnormalised (O, m, l) per chunk of keys. Head dim 128.
+//
+// One CTA = one chunk of keys of one segment x one KV head x NT tiles of 128 query rows. Warp roles:
+//   warp 0             TMA: the Q tiles once (128-byte swizzle, the UMMA operand layout), then per 64-key block the
+//                      raw quantised rows of this head (a 16-byte-aligned window of each key row, one 2-D tensor copy
+//                      for K and one for V; keys past the end read as zeros)
+//   warp 1             allocates TMEM; one thread issues the MMAs: S_t = Q_t K^T (M=128, N=64) into a double-buffered
+//                      S in TMEM, then O_t += P_t V (M=128, N=128, B = V read MN-major) into O_t in TMEM
+//   warps 2 .. 2+4NT   one warpgroup per Q tile: thread = query row = TMEM lane. Reads its row of S (64 keys), masks
+//                      tail keys, online softmax in the log2 domain with lazy rescaling (the running max moves only
+//                      when a block's max exceeds it by more than 8, so O in TMEM is rescaled rarely), writes P as f16
+//                      into shared memory in the swizzled operand layout
+//   last 4 warps       dequantise each raw K and V block into f16 operand tiles (f16(d * q), 128-byte swizzle)
+// All waits are bounded; a wait that runs out records a status, and every role still reaches the final barrier so
+// TMEM is released.
+#pragma once
+#include <cuda.h>
+
+#include "pa_common.cuh"
+#include "pa_decode.cuh"
+
+namespace pa {
+namespace pre {
+
+constexpr int HD = 128;
+constexpr int BM = 128;   // query rows per tile = TMEM lanes
+constexpr int BN = 64;    // keys per block
+constexpr int NS = 3;     // raw stages
+
+__host__ __device__ constexpr int raw_row_bytes(int quant) { return quant == 1 ? 144 : 80; }   // 16-aligned window
+
+struct Params {
+    const dec::Job *jobs;
+    const CUtensorMap *kv_maps;   // [2*seg] K rows, [2*seg+1] V rows: u8 {rs, nk}, box {raw_row_bytes, BN}
+    float *Op, *Mp, *Lp;          // slot partials [slot][nkv][rows][HD], [slot][nkv][rows]
+    int *status;
+    uint64_t rs, hb;
+    uint32_t nkv, rows, n_rt;     // n_rt: groups of NT*BM rows per head
+    uint64_t timeout_ns;
+};
+
+// ---------------------------------------------------------------- tcgen05 / TMA helpers
+__device__ __forceinline__ void tma_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes: thread i gets lane (quarter*32 + i)
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+__device__ __forceinline__ void lds128(uint32_t addr, uint32_t &a, uint32_t &b, uint32_t &c, uint32_t &d) {
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(a), "=r"(b), "=r"(c), "=r"(d) : "r"(addr));
+}
+
+// UMMA shared-memory descriptor, 128-byte swizzle (sm100 layout: start>>4 [0,14), LBO>>4 [16,30), SBO>>4 [32,46),
+// version 1 at bit 46, layout type 2 = SWIZZLE_128B at bits [61,64))
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t) ((saddr >> 4) & 0x3FFFu) | ((uint64_t) ((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t) ((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+// instruction descriptor, kind::f16: D f32 (bits 4-5 = 1), A/B f16 (0), A K-major, B K- or MN-major (bit 16),
+// N>>3 at bits 17-22, M>>4 at bits 24-28
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int b_mn_major) {
+    return (1u << 4) | ((uint32_t) b_mn_major << 16) | ((uint32_t) (N >> 3) << 17) | ((uint32_t) (M >> 4) << 24);
+}
+
+// shared-memory map (all operand tiles 1024-aligned)
+template <int QUANT, int NT>
+struct Smem {
+    static constexpr int RAWB = raw_row_bytes(QUANT);
+    static constexpr int Q = 0;                                   // NT x [2 atom cols][128 rows][128 B]
+    static constexpr int K = Q + NT * BM * HD * 2;                 // 2 x [2 atom cols][64 keys][128 B]
+    static constexpr int V = K + 2 * BN * HD * 2;                  // 2 x same (read MN-major)
+    static constexpr int P = V + 2 * BN * HD * 2;                  // NT x [128 rows][64 keys] f16
+    static constexpr int RAW = P + NT * BM * BN * 2;               // NS x (K rows, V rows) x [64][RAWB]
+    static constexpr int RAW_STAGE = (2 * BN * RAWB + 1023) / 1024 * 1024;
+    static constexpr int BAR = RAW + NS * RAW_STAGE;
+    static constexpr int N_BAR = 1 + 2 * NS + 8 + 4 * NT + 2 * NT + 1;
+    static constexpr int TOTAL = BAR + N_BAR * 8 + 32;
+};
+
+template <int QUANT, int NT>
+__global__ void __launch_bounds__(32 * (6 + 4 * NT), 1) prefill_kernel(const __grid_constant__ CUtensorMap tq,
+                                                                       const Params p) {
+    using L = Smem<QUANT, NT>;
+    constexpr int RAWB = L::RAWB;
+    constexpr int GB = dec::q_group_bytes(QUANT);
+    constexpr uint32_t IDESC_S = idesc_f16(BM, BN, 0);
+    constexpr uint32_t IDESC_PV = idesc_f16(BM, HD, 1);
+    constexpr int SM0 = 2, DQ0 = 2 + 4 * NT;   // first softmax warp, first dequant warp
+
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // operand tiles need 1024-byte alignment (128-byte swizzle atoms): align the dynamic base explicitly
+    uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+    const uint32_t sbase = smem_u32(smem);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::BAR);
+    uint64_t *q_full = bar;
+    uint64_t *raw_full = bar + 1, *raw_empty = raw_full + NS;
+    uint64_t *k_full = raw_empty + NS, *k_free = k_full + 2, *v_full = k_free + 2, *v_free = v_full + 2;
+    uint64_t *s_full = v_free + 2;             // [NT][2]
+    uint64_t *s_empty = s_full + 2 * NT;       // [NT][2]
+    uint64_t *p_full = s_empty + 2 * NT;       // [NT]
+    uint64_t *pv_done = p_full + NT;           // [NT]
+    uint64_t *mma_done = pv_done + NT;         // every MMA this CTA issued has completed (before TMEM is freed)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + L::N_BAR);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const dec::Job job = p.jobs[blockIdx.x];
+    const uint32_t h = blockIdx.y % p.nkv, rt = blockIdx.y / p.nkv;
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t nblk = (job.nk + BN - 1) / BN;
+    const uint32_t hbyte = h * (uint32_t) p.hb;
+    const int hx = (int) (hbyte & ~15u);          // window start (16-byte aligned) of this head in a key row
+    const uint32_t hoff = hbyte & 15u;            // head start inside the window
+    const uint32_t row0 = rt * NT * BM;           // first query row of this CTA (within the head)
+    const uint64_t tmo = p.timeout_ns;
+    bool ok = true;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < NS; s++) { mbar_init(&raw_full[s], 1); mbar_init(&raw_empty[s], 4); }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&k_full[b], 4); mbar_init(&k_free[b], 1); mbar_init(&v_full[b], 4); mbar_init(&v_free[b], 1);
+        }
+        for (int t = 0; t < NT; t++) {
+            for (int b = 0; b < 2; b++) { mbar_init(&s_full[2 * t + b], 1); mbar_init(&s_empty[2 * t + b], 4); }
+            mbar_init(&p_full[t], 4);
+            mbar_init(&pv_done[t], 1);
+        }
+        mbar_init(mma_done, 1);
+        // a CTA started after another one gave up a wait does no work (a systematic failure ends in one timeout)
+        *abort_flag = *(volatile int *) p.status != ST_OK;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (*abort_flag) return;   // uniform: before TMEM is allocated
+    if (warp == 1) {   // TMEM: per tile S x2 (64 columns each) + O (128 columns)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(256 * NT)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    auto wait = [&](uint64_t *b, uint32_t parity) -> bool {
+        if (!ok) return false;
+        if (!mbar_wait_bounded(b, parity, tmo, abort_flag)) {
+            ok = false;
+            *abort_flag = 1;
+            atomicCAS(p.status, ST_OK, ST_TIMEOUT_FULL);
+        }
+        return ok;
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            const int qrow = (int) (((uint64_t) job.set * p.nkv + h) * p.rows + row0);
+            mbar_arrive_expect_tx(q_full, NT * BM * HD * 2);
+            for (int t = 0; t < NT; t++)
+                for (int c = 0; c < 2; c++)
+                    tma_2d(smem + L::Q + t * BM * HD * 2 + c * BM * 128, &tq, c * 64, qrow + t * BM, q_full);
+            const CUtensorMap *km = p.kv_maps + 2 * job.seg, *vm = km + 1;
+            uint32_t issued = 0;
+            for (uint32_t j = 0; j < nblk; j++) {
+                const uint32_t st = j % NS;
+                if (j >= NS && !wait(&raw_empty[st], ((j / NS) - 1) & 1)) break;
+                mbar_arrive_expect_tx(&raw_full[st], 2 * BN * RAWB);
+                uint8_t *dst = smem + L::RAW + st * L::RAW_STAGE;
+                tma_2d(dst, km, hx, (int) (job.key0 + j * BN), &raw_full[st]);
+                tma_2d(dst + BN * RAWB, vm, hx, (int) (job.key0 + j * BN), &raw_full[st]);
+                issued = j + 1;
+            }
+            // on an abort, every issued copy lands before the CTA exits
+            if (!ok) {
+                const uint64_t drain = tmo > dec::DRAIN_NS ? tmo : dec::DRAIN_NS;
+                if (!mbar_wait_bounded(q_full, 0, drain, nullptr)) atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
+                const uint32_t first = issued > NS ? issued - NS : 0;
+                for (uint32_t j = first; j < issued; j++)
+                    if (!mbar_wait_bounded(&raw_full[j % NS], (j / NS) & 1, drain, nullptr))
+                        atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            uint32_t issued_pv = 0;
+            auto issue_pv = [&](uint32_t jj) {
+                const uint32_t b = jj & 1;
+                if (!wait(&v_full[b], (jj >> 1) & 1)) return;
+                for (int t = 0; t < NT; t++) {
+                    if (!wait(&p_full[t], jj & 1)) return;
+                    tc_fence_after();
+                    const uint32_t d = tmem + t * 256 + 128;
+                    const uint32_t pa = sbase + L::P + t * BM * BN * 2, va = sbase + L::V + b * BN * HD * 2;
+#pragma unroll
+                    for (int ks = 0; ks < BN / 16; ks++)
+                        tc_mma(d, sdesc(pa + ks * 32, 16, 1024), sdesc(va + ks * 2048, BN * 128, 1024), IDESC_PV,
+                               (jj > 0 || ks > 0) ? 1u : 0u);
+                    tc_commit(&pv_done[t]);
+                }
+                tc_commit(&v_free[b]);
+                issued_pv = jj + 1;
+            };
+            if (wait(q_full, 0)) {
+                for (uint32_t j = 0; j < nblk && ok; j++) {
+                    const uint32_t b = j & 1;
+                    if (!wait(&k_full[b], (j >> 1) & 1)) break;
+                    for (int t = 0; t < NT && ok; t++) {
+                        if (j >= 2 && !wait(&s_empty[2 * t + b], ((j - 2) >> 1) & 1)) break;
+                        tc_fence_after();
+                        const uint32_t d = tmem + t * 256 + b * BN;
+                        const uint32_t qa = sbase + L::Q + t * BM * HD * 2, ka = sbase + L::K + b * BN * HD * 2;
+#pragma unroll
+                        for (int kk = 0; kk < HD / 16; kk++)
+                            tc_mma(d, sdesc(qa + (kk / 4) * BM * 128 + (kk % 4) * 32, 16, 1024),
+                                   sdesc(ka + (kk / 4) * BN * 128 + (kk % 4) * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+                        tc_commit(&s_full[2 * t + b]);
+                    }
+                    if (!ok) break;
+                    tc_commit(&k_free[b]);
+                    if (j >= 1) issue_pv(j - 1);
+                }
+                if (ok && nblk > 0) issue_pv(nblk - 1);
+            }
+            (void) issued_pv;
+            // TMEM must not be released under MMAs still running (they complete on their own; bounded wait)
+            tc_commit(mma_done);
+            const uint64_t drain = tmo > dec::DRAIN_NS ? tmo : dec::DRAIN_NS;
+            if (!mbar_wait_bounded(mma_done, 0, drain, nullptr)) atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
+        }
+    } else if (warp < (uint32_t) DQ0) {
+        // ------------------------------------------------ softmax warpgroup of tile t
+        const int t = (int) (warp - SM0) / 4;
+        const uint32_t wq = warp % 4;                      // TMEM lane quarter of this warp
+        const uint32_t r = wq * 32 + lane;                 // row of the tile = TMEM lane
+        const uint32_t tl = tmem + ((wq * 32) << 16) + t * 256;
+        const uint32_t prow = sbase + L::P + t * BM * BN * 2 + (r / 8) * 1024 + (r % 8) * 128;
+        float m_used = -INFINITY, l = 0.f;
+        for (uint32_t j = 0; j < nblk; j++) {
+            const uint32_t b = j & 1;
+            if (!wait(&s_full[2 * t + b], (j >> 1) & 1)) break;
+            tc_fence_after();
+            float s[64];
+            {
+                float a[32], c[32];
+                tmem_ld32(tl + b * BN, a);
+                tmem_ld32(tl + b * BN + 32, c);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i++) { s[i] = a[i]; s[32 + i] = c[i]; }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_empty[2 * t + b]);
+            const int nvalid = (int) (job.nk - j * BN);
+            if (nvalid < BN) {
+#pragma unroll
+                for (int i = 0; i < BN; i++)
+                    if (i >= nvalid) s[i] = -INFINITY;
+            }
+            float mx = s[0];
+#pragma unroll
+            for (int i = 1; i < BN; i++) mx = fmaxf(mx, s[i]);
+            mx *= LOG2E;
+            float alpha = 1.f;
+            bool rescale = false;
+            if (j == 0) m_used = mx;
+            else if (mx > m_used + 8.f) {
+                alpha = ex2(m_used - mx);
+                m_used = mx;
+                rescale = true;
+            }
+            float sum = 0.f;
+            uint32_t ph[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const float p0 = ex2(fmaf(s[2 * i], LOG2E, -m_used)), p1 = ex2(fmaf(s[2 * i + 1], LOG2E, -m_used));
+                sum += p0 + p1;
+                ph[i] = pack_h2(p0, p1);
+            }
+            l = fmaf(l, alpha, sum);
+            // P buffer and O are free once the previous block's P.V has completed
+            if (j >= 1 && !wait(&pv_done[t], (j - 1) & 1)) break;
+            if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
+                tc_fence_after();
+#pragma unroll
+                for (int q = 0; q < HD / 32; q++) {
+                    float o[32];
+                    tmem_ld32(tl + 128 + q * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] *= alpha;
+                    tmem_st32(tl + 128 + q * 32, o);
+                }
+                tmem_wait_st();
+            }
+#pragma unroll
+            for (int c = 0; c < BN / 8; c++)
+                sts128(prow + ((c ^ (r % 8)) * 16), ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
+            fence_proxy_async();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[t]);
+        }
+        // final: O (unnormalised, relative to m_used) from TMEM to the slot partial
+        if (ok && nblk > 0 && wait(&pv_done[t], (nblk - 1) & 1)) {
+            tc_fence_after();
+            const uint32_t row = row0 + t * BM + r;
+            const uint64_t orow = ((uint64_t) job.slot * p.nkv + h) * p.rows + row;
+#pragma unroll
+            for (int q = 0; q < HD / 32; q++) {
+                float o[32];
+                tmem_ld32(tl + 128 + q * 32, o);
+                tmem_wait_ld();
+                if (row < p.rows) {
+                    float4 *dst = reinterpret_cast<float4 *>(p.Op + orow * HD + q * 32);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                }
+            }
+            if (row < p.rows) {
+                p.Mp[orow] = l > 0.f ? m_used * (1.0f / LOG2E) : -INFINITY;
+                p.Lp[orow] = l;
+            }
+        }
+    } else {
+        // ------------------------------------------------ dequantisers: warp dw owns quant block dw of every key
+        const uint32_t dw = warp - DQ0;
+        const uint32_t bo = hoff + GB * dw;                 // block start inside the raw window row
+        const uint32_t w16 = bo & ~15u;                     // 16-byte aligned start of the words covering it
+        const uint32_t ds = bo + 2;                         // first data byte
+        const uint32_t w0 = (ds - w16) / 4, shift = 8 * (ds % 4);
+        const uint32_t colb = (QUANT == 1 ? (dw / 2) : (dw / 2)) * BN * 128;   // atom column of this block's d's
+        for (uint32_t j = 0; j < nblk; j++) {
+            const uint32_t st = j % NS, b = j & 1;
+            if (!wait(&raw_full[st], (j / NS) & 1)) break;
+            const uint32_t raw = sbase + L::RAW + st * L::RAW_STAGE;
+#pragma unroll
+            for (int kv = 0; kv < 2; kv++) {
+                if (j >= 2 && !wait(kv == 0 ? &k_free[b] : &v_free[b], ((j - 2) >> 1) & 1)) break;
+                const uint32_t src = raw + kv * BN * RAWB;
+                const uint32_t dst = sbase + (kv == 0 ? L::K : L::V) + b * BN * HD * 2 + colb;
+#pragma unroll
+                for (int pass = 0; pass < 2; pass++) {
+                    const uint32_t key = pass * 32 + lane;
+                    const uint32_t rb = src + key * RAWB;
+                    const uint32_t s2 = lds16(rb + bo);
+                    const uint32_t sc2 = s2 | (s2 << 16);
+                    uint32_t W[12];
+                    // q8_0: the block's 34 bytes lie within 3 aligned 16-byte chunks; q4_0: 18 bytes within 2
+#pragma unroll
+                    for (int i = 0; i < (QUANT == 1 ? 3 : 2); i++)
+                        lds128(rb + w16 + 16 * i, W[4 * i], W[4 * i + 1], W[4 * i + 2], W[4 * i + 3]);
+                    if (QUANT != 1) W[8] = W[9] = W[10] = W[11] = 0u;
+                    const uint32_t kbase = dst + (key / 8) * 1024 + (key % 8) * 128;
+                    if (QUANT == 1) {
+                        uint32_t A[8];
+                        switch (w0) {   // uniform across the warp
+#define PA_ALIGN8(W0)                                                                        \
+    case W0:                                                                                 \
+        _Pragma("unroll") for (int i = 0; i < 8; i++) A[i] = __funnelshift_r(W[W0 + i], W[(W0 + i + 1 < 12) ? W0 + i + 1 : 11], shift); \
+        break;
+                            PA_ALIGN8(0) PA_ALIGN8(1) PA_ALIGN8(2) PA_ALIGN8(3) default: PA_ALIGN8(4)
+#undef PA_ALIGN8
+                        }
+#pragma unroll
+                        for (int cc = 0; cc < 4; cc++) {
+                            uint32_t h0, h1, h2, h3;
+                            dec::q8_word(A[2 * cc], sc2, h0, h1);
+                            dec::q8_word(A[2 * cc + 1], sc2, h2, h3);
+                            const uint32_t c = 4 * (dw % 2) + cc;
+                            sts128(kbase + ((c ^ (key % 8)) * 16), h0, h1, h2, h3);
+                        }
+                    } else {
+                        uint32_t D[4];
+                        switch (w0) {
+#define PA_ALIGN4(W0)                                                                        \
+    case W0:                                                                                 \
+        _Pragma("unroll") for (int i = 0; i < 4; i++) D[i] = __funnelshift_r(W[W0 + i], W[W0 + i + 1], shift); \
+        break;
+                            PA_ALIGN4(0) PA_ALIGN4(1) PA_ALIGN4(2) PA_ALIGN4(3) default: PA_ALIGN4(4)
+#undef PA_ALIGN4
+                        }
+                        // byte i: element i (low nibble), element i + 16 (high nibble)
+                        uint32_t lo[8], hi[8];   // f16x2 of elements (2i, 2i+1) and (16+2i, 17+2i)
+                        const uint32_t m = 0x000F000Fu, magic = 0x64006400u, off8 = 0x64086408u;
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const uint32_t y = prmt(D[i], D[i], 0x3120u);   // bytes (x0, x2, x1, x3)
+                            lo[2 * i] = hmul2(hsub2(and_or(y, m, magic), off8), sc2);
+                            lo[2 * i + 1] = hmul2(hsub2(and_or(y >> 8, m, magic), off8), sc2);
+                            hi[2 * i] = hmul2(hsub2(and_or(y >> 4, m, magic), off8), sc2);
+                            hi[2 * i + 1] = hmul2(hsub2(and_or(y >> 12, m, magic), off8), sc2);
+                        }
+                        const uint32_t c0 = 4 * (dw % 2);
+                        sts128(kbase + (((c0 + 0) ^ (key % 8)) * 16), lo[0], lo[1], lo[2], lo[3]);
+                        sts128(kbase + (((c0 + 1) ^ (key % 8)) * 16), lo[4], lo[5], lo[6], lo[7]);
+                        sts128(kbase + (((c0 + 2) ^ (key % 8)) * 16), hi[0], hi[1], hi[2], hi[3]);
+                        sts128(kbase + (((c0 + 3) ^ (key % 8)) * 16), hi[4], hi[5], hi[6], hi[7]);
+                    }
+                }
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(kv == 0 ? &k_full[b] : &v_full[b]);
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_empty[st]);
+        }
+    }
+
+    // every role ends here (no return after the TMEM allocation); the MMA thread has waited for its MMAs
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256 * NT) : "memory");
+    }
+}
+
+}  // namespace pre
+}  // namespace pa

@@ -40,13 +40,15 @@ GEN_CHUNK = 16384   # keys per generator draw (the data does not depend on the n
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--keys", type=int, default=KEYS)
     ap.add_argument("--e2e-steps", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill-steps", type=int, default=3)
+    ap.add_argument("--prefill-layers", type=int, default=LAYERS)
     return ap.parse_args()
 
 
@@ -67,6 +69,15 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
+def measured_tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
 
@@ -84,7 +95,7 @@ class ClockSampler:
         os.close(fd)
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
@@ -209,6 +220,59 @@ def run_reference(args, rank: int, world: int):
         "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------------------------- config 2
+PF_TOKENS, PF_KEYS = 512, 65536
+
+
+def bench_prefill(torch, pa, ctx, device, stream, layers: int, steps: int):
+    """Config 2: a 512-token query batch (40 q / 8 KV heads, d128) against 65,536 older Q8_0 positions per layer, no
+    mask, all `layers` layers per step in one plan (the tcgen05 kernel: 2,560 rows per KV head). Device-timed."""
+    rows = PF_TOKENS * GQA
+    shape = pa.shape_for(HD, NKV, rows, pa.Q8_0)
+    K = torch.empty((layers, PF_KEYS, shape.rs), dtype=torch.uint8, device=device)
+    V = torch.empty_like(K)
+    for layer in range(layers):
+        k, v = make_layer(torch, pa, 1000 + layer, 0, PF_KEYS, device)
+        K[layer].copy_(k)
+        V[layer].copy_(v)
+        del k, v
+    g = torch.Generator(device=device)
+    g.manual_seed(SEED + 11)
+    Qs = (torch.randn((layers, NKV, rows, HD), generator=g, device=device) / HD ** 0.5).to(torch.float16)
+    segs = [pa.Seg(K[i].data_ptr(), V[i].data_ptr(), PF_KEYS, i) for i in range(layers)]
+    plan = pa.Plan(ctx, shape, layers, segs)
+    O = torch.empty((layers, NKV, rows, HD), dtype=torch.float32, device=device)
+    m = torch.empty((layers, NKV, rows), dtype=torch.float32, device=device)
+    l = torch.empty_like(m)
+    for _ in range(2):
+        plan.run(Qs, O, m, l, stream)
+    ctx.status(stream)
+    torch.cuda.synchronize()
+    plan.profile(steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        plan.run(Qs, O, m, l, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ctx.status(stream)
+    ms = e0.elapsed_time(e1) / steps
+    kms, kn = plan.kernel_ms()
+    kms /= max(1, kn)
+    flops = 4.0 * PF_TOKENS * Q_HEADS * HD * PF_KEYS * layers
+    peak, kind = measured_tensor_peak()
+    plan.close()
+    del K, V, Qs, O
+    torch.cuda.empty_cache()
+    return {"metric": "prefill attn TFLOP/s (config 2: 512 tokens x 65536 Q8_0 keys, 40q/8kv, d128)",
+            "value": round(flops / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "ms_per_step": round(ms, 3),
+            "layers": layers, "steps": steps,
+            "roofline": {"bound": "tensor", "achieved": round(flops / (kms * 1e-3) / 1e12, 1), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(flops / (kms * 1e-3) / 1e12 / peak, 4), "peak_kind": kind,
+                         "kernel": "pa::pre::prefill_kernel<1,2>", "kernel_ms": round(kms, 3),
+                         "algorithmic_flops_per_launch": flops}}
 
 
 # --------------------------------------------------------------------------------------------- GPU arm
@@ -356,6 +420,13 @@ def main():
                "h2d_bytes_per_step": L * NKV * GQA * HD * 2, "d2h_bytes_per_step": rows * (HD + 2) * 4,
                "ms_per_step": round(dt / args.e2e_steps * 1e3, 3)}
 
+    # ---- config 2 (prefill): 512 tokens x 40 q heads against 65,536 Q8_0 positions per layer, all layers per step
+    prefill = None
+    if world == 1 and args.prefill_steps > 0:
+        del Kall, Vall
+        torch.cuda.empty_cache()
+        prefill = bench_prefill(torch, pa, ctx, device, stream, args.prefill_layers, args.prefill_steps)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline()
@@ -373,6 +444,7 @@ def main():
                        "l2": "inputs larger than L2 (18.3 GB of KV per step), no flush",
                        "bytes_per_step": per_step_bytes},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     plan.close()

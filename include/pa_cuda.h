@@ -87,6 +87,10 @@ const char *pa_cuda_last_error(const pa_cuda_ctx *ctx);
 int pa_cuda_status(pa_cuda_ctx *ctx, void *stream);
 /* Bound on every in-kernel wait (default 2 s). */
 void pa_cuda_set_timeout_ns(pa_cuda_ctx *ctx, uint64_t ns);
+/* Kernel selection for plans created afterwards (as the reference engine's PA_BIG_KERNEL / PA_BIG_MIN_NG switches,
+ * phone-attn/pa-metal.mm:818-821): 0 = by shape (default: the tcgen05 kernel for hd 128 and >= 64 query rows per KV
+ * head, the split-K mma.sync kernel otherwise), 1 = always the split-K kernel, 2 = the tcgen05 kernel (hd 128 only). */
+void pa_cuda_set_kernel(pa_cuda_ctx *ctx, int which);
 /* Failure-detection test hook: while on, the decode kernel's consumer warps first wait on a barrier that nothing
  * completes, so their bounded wait runs out after the timeout; the kernel records PA_CUDA_ETIMEOUT and returns
  * without trapping, and the context stays usable. Off by default. */

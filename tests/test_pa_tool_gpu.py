@@ -33,8 +33,17 @@ def test_reference_pa_tool_against_cuda_engine(env, nkeys):
     port = _free_port()
     srv = subprocess.Popen([SERVE, str(port), "2"], stdout=subprocess.DEVNULL, stderr=subprocess.PIPE, text=True)
     try:
-        time.sleep(1.0)
-        assert srv.poll() is None, srv.stderr.read()
+        # the server initialises CUDA before it listens: wait until the port accepts a connection
+        deadline = time.time() + 60
+        while True:
+            assert srv.poll() is None, srv.stderr.read()
+            try:
+                with socket.create_connection(("127.0.0.1", port), timeout=1.0):
+                    break
+            except OSError:
+                if time.time() > deadline:
+                    raise
+                time.sleep(0.2)
         out = subprocess.run([TOOL, "test", "127.0.0.1", str(port), str(nkeys), "4", "4"], env=dict(os.environ, **env),
                              capture_output=True, text=True, timeout=300)
         text = out.stdout + out.stderr

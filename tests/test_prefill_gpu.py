@@ -1,0 +1,79 @@
+"""Parity of the tcgen05/TMEM kernel (many query rows per KV head: prefill, ATTN_BIG, long verify batches) with the
+oracle on identical seeded inputs, and with the split-K mma.sync kernel on the same call. Tolerances as in
+test_decode_gpu.py: 2e-3 against the reference-arithmetic oracle, 5e-3 (pa-tool's gate) against exact fp64."""
+import numpy as np
+import pytest
+
+import backburner_b200 as pa
+from oracle import oracle as orc
+
+from test_decode_gpu import TOL_F64, TOL_REF, _check, _dev
+
+pytestmark = pytest.mark.gpu
+
+
+def _run_kernel(ctx, c, which, n_sets=1, cases=None):
+    import torch
+    ctx.set_kernel(which)
+    try:
+        sh = c["shape"]
+        shape = pa.shape_for(sh.hd, sh.nkv, sh.rows, sh.quant)
+        K, V = _dev(c["K"]), _dev(c["V"])
+        Qs = _dev(c["Qs"].view(np.int16)).view(torch.float16)
+        nk = c["K"].shape[0]
+        O, m, l = pa.attn(ctx, shape, Qs, [pa.Seg(K.data_ptr(), V.data_ptr(), nk, 0)], 1)
+        ctx.status()
+        return O[0].cpu().numpy(), m[0].cpu().numpy(), l[0].cpu().numpy()
+    finally:
+        ctx.set_kernel(0)
+
+
+@pytest.mark.parametrize("rows,nk,quant", [
+    (64, 1024, orc.Q8_0), (80, 2048, orc.Q4_0), (80, 1000, orc.Q8_0), (128, 4096, orc.Q8_0), (129, 700, orc.Q8_0),
+    (256, 2048, orc.Q8_0), (300, 1500, orc.Q4_0), (640, 4096, orc.Q8_0), (5, 333, orc.Q8_0), (48, 64, orc.Q8_0),
+    (256, 1, orc.Q8_0), (200, 63, orc.Q4_0), (257, 65, orc.Q8_0)])
+def test_tcgen05_kernel_parity(ctx, rows, nk, quant):
+    c = orc.gen_case(3000 + rows + nk + quant, 128, 8, rows, nk, quant)
+    O, m, l = _run_kernel(ctx, c, 2)
+    _check(c, O, m, l, nk)
+
+
+@pytest.mark.parametrize("rows,nk", [(80, 3000), (256, 2000)])
+def test_tcgen05_matches_split_k_kernel(ctx, rows, nk):
+    c = orc.gen_case(77 + rows, 128, 8, rows, nk, orc.Q8_0)
+    O2, m2, l2 = _run_kernel(ctx, c, 2)
+    O1, m1, l1 = _run_kernel(ctx, c, 1)
+    e = orc.rel_err(O2, m2, l2, O1.astype(np.float64), m1.astype(np.float64), l1.astype(np.float64))
+    assert e[0] <= 1e-3 and e[1] <= 1e-3, e
+
+
+def test_tcgen05_many_sets_and_split_keys(ctx):
+    """Several layers (output sets) in one plan, each split into several key chunks (jobs), run twice."""
+    import torch
+    hd, nkv, rows = 128, 8, 160
+    ctx.set_kernel(2)
+    try:
+        shape = pa.shape_for(hd, nkv, rows, pa.Q8_0)
+        cases = [orc.gen_case(900 + i, hd, nkv, rows, nk, orc.Q8_0) for i, nk in enumerate([5000, 64, 2100])]
+        Ks = [_dev(c["K"]) for c in cases]
+        Vs = [_dev(c["V"]) for c in cases]
+        Qs = _dev(np.stack([c["Qs"] for c in cases]).view(np.int16)).view(torch.float16)
+        segs = [pa.Seg(Ks[i].data_ptr(), Vs[i].data_ptr(), c["K"].shape[0], i) for i, c in enumerate(cases)]
+        plan = pa.Plan(ctx, shape, len(cases), segs, chunk_keys=1024)
+        O = torch.empty((len(cases), nkv, rows, hd), device="cuda")
+        m = torch.empty((len(cases), nkv, rows), device="cuda")
+        l = torch.empty_like(m)
+        for _ in range(2):
+            plan.run(Qs, O, m, l)
+            ctx.status()
+            for i, c in enumerate(cases):
+                _check(c, O[i].cpu().numpy(), m[i].cpu().numpy(), l[i].cpu().numpy(), c["K"].shape[0])
+        plan.close()
+    finally:
+        ctx.set_kernel(0)
+
+
+def test_tcgen05_student_t_values(ctx):
+    c = orc.gen_case(44, 128, 8, 256, 3000, orc.Q8_0, student_t=True)
+    O, m, l = _run_kernel(ctx, c, 2)
+    _check(c, O, m, l, 3000)
