@@ -78,6 +78,8 @@ _SIGS = {
                                      ctypes.POINTER(_Shape), ctypes.c_int, ctypes.c_int]),
     "pa_cuda_end": (ctypes.c_double, [_P, _P, _P, _P]),
     "pa_cuda_exec_ms": (ctypes.c_double, [_P]),
+    "pa_cuda_attn_noalloc": (ctypes.c_int, [ctypes.POINTER(_Shape), _P, _P, _P, ctypes.c_uint32, _P, _P, _P, _P,
+                                            ctypes.POINTER(ctypes.c_char_p)]),
 }
 
 _lib = None

@@ -9,6 +9,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <mutex>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -841,3 +842,155 @@ double pa_cuda_end(pa_cuda_ctx *ctx, float *O, float *m, float *l) {
 double pa_cuda_exec_ms(const pa_cuda_ctx *ctx) { return ctx ? ctx->last_exec_ms : 0; }
 
 }  // extern "C"
+
+// ====================================================================================================== no allocation
+// pa_cuda_attn_noalloc: the split-K kernel with its scratch (the chunk partials, the job list, the status word) in a
+// fixed device array, for callers that cannot allocate device memory (see include/pa_cuda.h).
+namespace {
+
+constexpr size_t kNaBytes = 16u << 20;   // per GPU; held by every GPU that loads the library until the process exits
+constexpr uint32_t kNaMaxJobs = 2048;
+constexpr size_t kNaStatus = 0;          // int: bounded-wait status of the call
+constexpr size_t kNaRange = 256;         // uint32_t[2]: the merge's part range [0, n_jobs)
+constexpr size_t kNaJobs = 512;          // pa::dec::Job[kNaMaxJobs]
+constexpr size_t kNaParts = (kNaJobs + kNaMaxJobs * sizeof(pa::dec::Job) + 255) / 256 * 256;   // partials
+
+static __device__ __align__(256) uint8_t g_na_scratch[kNaBytes];
+
+// the device address of g_na_scratch per device (set up by the first call on that device; a host-side name of a
+// __device__ array is not a device address)
+std::mutex g_na_mu;
+uint8_t *g_na_ptr[128] = {};
+
+// writes this call's job list, part range and a zero status into the scratch (the array keeps the previous call's
+// contents otherwise)
+__global__ void noalloc_setup_kernel(uint8_t *base, const uint8_t *K, const uint8_t *V, uint32_t nk, uint32_t chunk,
+                                     uint32_t n_jobs) {
+    pa::dec::Job *jobs = reinterpret_cast<pa::dec::Job *>(base + kNaJobs);
+    for (uint32_t i = threadIdx.x; i < n_jobs; i += blockDim.x) {
+        pa::dec::Job j;
+        j.k = K;
+        j.v = V;
+        j.key0 = i * chunk;
+        j.nk = min(chunk, nk - i * chunk);
+        j.set = 0;
+        j.slot = i;
+        j.seg = 0;
+        j.pad_ = 0;
+        jobs[i] = j;
+    }
+    if (threadIdx.x == 0) {
+        *reinterpret_cast<int *>(base + kNaStatus) = pa::ST_OK;
+        uint32_t *range = reinterpret_cast<uint32_t *>(base + kNaRange);
+        range[0] = 0;
+        range[1] = n_jobs;
+    }
+}
+
+int na_fail(const char **why, int code, const char *msg) {
+    if (why) *why = msg;
+    return code;
+}
+
+}  // namespace
+
+extern "C" int pa_cuda_attn_noalloc(const pa_cuda_shape *shape, const uint16_t *Qs, const uint8_t *K, const uint8_t *V,
+                                    uint32_t nk, float *O, float *m, float *l, void *stream, const char **why) {
+    if (why) *why = "";
+    if (!shape || !O || !m || !l || (nk && (!Qs || !K || !V))) return na_fail(why, PA_CUDA_EINVAL, "null argument");
+    if (check_shape(nullptr, shape) != PA_CUDA_OK)
+        return na_fail(why, PA_CUDA_EUNSUPPORTED, "shape: hd 128/256, Q8_0 or Q4_0, hb of the format, rs >= nkv*hb and "
+                                                  "a multiple of 16");
+    if (nk && (((uintptr_t) K | (uintptr_t) V) & 15)) return na_fail(why, PA_CUDA_EINVAL, "K/V not 16-byte aligned");
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return na_fail(why, PA_CUDA_ECUDA, "cudaGetDevice");
+    uint8_t *base;
+    {
+        std::lock_guard<std::mutex> lk(g_na_mu);
+        if (!g_na_ptr[dev]) {
+            void *ptr = nullptr;
+            if (cudaGetSymbolAddress(&ptr, g_na_scratch) != cudaSuccess || !ptr)
+                return na_fail(why, PA_CUDA_ECUDA, "cudaGetSymbolAddress of the fixed scratch failed");
+            g_na_ptr[dev] = (uint8_t *) ptr;
+        }
+        base = g_na_ptr[dev];
+    }
+    const uint64_t rows_all = (uint64_t) shape->nkv * shape->rows;
+    const uint64_t slot_bytes = rows_all * (shape->hd + 2) * 4;
+    const uint64_t max_slots = std::min<uint64_t>(kNaMaxJobs, (kNaBytes - kNaParts) / slot_bytes);
+    if (max_slots == 0)
+        return na_fail(why, PA_CUDA_EUNSUPPORTED,
+                       "nkv * rows * (hd + 2) * 4 bytes (one chunk partial) exceed the 16 MiB fixed scratch");
+    pa_cuda_plan p;   // launch shape only: no allocation
+    p.ctx = nullptr;
+    p.sh = *shape;
+    p.n_sets = 1;
+    if (plan_decode_shape(nullptr, &p) != PA_CUDA_OK)
+        return na_fail(why, PA_CUDA_EUNSUPPORTED, "no head grouping of this shape fits the split-K kernel");
+    int n_sm = 148;
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    uint32_t chunk = 0, n_jobs = 0;
+    if (nk) {
+        const uint64_t per_y = std::max<uint64_t>(1, (uint64_t) n_sm * 16 / std::max<uint32_t>(1, p.grid_y));
+        chunk = (uint32_t) std::min<uint64_t>(16384, std::max<uint64_t>(128, (nk + per_y - 1) / per_y));
+        chunk = (chunk + 63) / 64 * 64;
+        if ((nk + chunk - 1) / chunk > max_slots) chunk = (uint32_t) (((nk + max_slots - 1) / max_slots + 63) / 64 * 64);
+        n_jobs = (nk + chunk - 1) / chunk;
+    }
+    p.n_jobs = p.n_slots = n_jobs;
+    cudaStream_t st = (cudaStream_t) stream;
+    noalloc_setup_kernel<<<1, 256, 0, st>>>(base, K, V, nk, chunk, n_jobs);
+    if (cudaGetLastError() != cudaSuccess) return na_fail(why, PA_CUDA_ECUDA, "setup kernel launch failed");
+    float *Op = reinterpret_cast<float *>(base + kNaParts);
+    float *Mp = Op + (uint64_t) n_jobs * rows_all * shape->hd, *Lp = Mp + (uint64_t) n_jobs * rows_all;
+    int *status = reinterpret_cast<int *>(base + kNaStatus);
+    if (n_jobs) {
+        pa::dec::Params prm{};
+        prm.jobs = reinterpret_cast<const pa::dec::Job *>(base + kNaJobs);
+        prm.Qs = Qs;
+        prm.Op = Op;
+        prm.Mp = Mp;
+        prm.Lp = Lp;
+        prm.status = status;
+        prm.rs = shape->rs;
+        prm.hb = shape->hb;
+        prm.nkv = shape->nkv;
+        prm.rows = shape->rows;
+        prm.hg = p.hg;
+        prm.rgc = p.rgc;
+        prm.n_rg = p.n_rg;
+        prm.row = p.row;
+        prm.gs = p.gs;
+        prm.pw = p.pw;
+        prm.n_consumers = p.n_consumers;
+        prm.timeout_ns = 2000000000ull;
+        prm.stall = 0;
+        cudaError_t e;
+        if (shape->hd == 128) e = shape->quant == PA_CUDA_Q8_0 ? launch_decode<128, 1>(&p, prm, st) : launch_decode<128, 2>(&p, prm, st);
+        else e = shape->quant == PA_CUDA_Q8_0 ? launch_decode<256, 1>(&p, prm, st) : launch_decode<256, 2>(&p, prm, st);
+        if (e != cudaSuccess) return na_fail(why, PA_CUDA_ECUDA, "split-K kernel launch failed");
+    }
+    pa::mrg::Params mp{};
+    mp.Op = Op;
+    mp.Mp = Mp;
+    mp.Lp = Lp;
+    mp.c_range = reinterpret_cast<const uint32_t *>(base + kNaRange);
+    mp.n_parts = n_jobs;
+    mp.op_stride = rows_all * shape->hd;
+    mp.ml_stride = rows_all;
+    mp.set_rows = 0;
+    mp.O = O;
+    mp.M = m;
+    mp.L = l;
+    mp.rows_per_set = rows_all;
+    mp.n_sets = 1;
+    mp.fold = 0;
+    if ((shape->hd == 128 ? launch_merge<128>(mp, st) : launch_merge<256>(mp, st)) != cudaSuccess)
+        return na_fail(why, PA_CUDA_ECUDA, "merge kernel launch failed");
+    if (cudaStreamSynchronize(st) != cudaSuccess) return na_fail(why, PA_CUDA_ECUDA, "stream synchronize failed");
+    int h = 0;
+    if (cudaMemcpy(&h, status, sizeof h, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return na_fail(why, PA_CUDA_ECUDA, "status read failed");
+    if (h != pa::ST_OK) return na_fail(why, PA_CUDA_ETIMEOUT, "a kernel gave up a bounded wait");
+    return PA_CUDA_OK;
+}

@@ -163,6 +163,25 @@ double pa_cuda_end(pa_cuda_ctx *ctx, float *O, float *m, float *l);
 /* GPU execution time of the last completed begin/end call (CUDA events), ms */
 double pa_cuda_exec_ms(const pa_cuda_ctx *ctx);
 
+/* ---- allocation-free call (no counterpart in the reference: an addition of this library)
+ * For callers that cannot allocate device memory: a host runtime that owns every device allocation itself (a fixed
+ * memory pool, an inference server that reserves the GPU's memory up front), or code running where cudaMalloc is not
+ * allowed, cannot create a context (pa_cuda_create allocates) or a plan (plans own scratch). This entry point runs the
+ * split-K kernel and the merge for one segment (as pa_cuda_attn with one set and one segment) using a fixed 16 MiB
+ * device array compiled into the library instead of allocated scratch; it calls no cudaMalloc, cudaFree or other
+ * allocating routine. The caller still passes Qs (f16(q*scale) [nkv][rows][hd]), K, V (device) and O, m, l.
+ *   Limit: one chunk partial, nkv * rows * (hd + 2) * 4 bytes, must fit the 16 MiB array (up to 2048 chunks are used);
+ *   a larger shape returns PA_CUDA_EUNSUPPORTED with the reason in *why (a static string; why may be null).
+ *   Set-up: the first call on a device looks the array's device address up (cudaGetSymbolAddress, with that device
+ *   current); make that first call before any stream capture. Every GPU that loads the library holds the array until
+ *   the process exits.
+ *   Sharing: all calls on a device share the one array and it keeps the last call's contents (each call rewrites what
+ *   it reads); calls that overlap on the GPU (other streams, other host threads) race and must be serialised.
+ *   The call returns after the stream has synchronised: PA_CUDA_OK, or PA_CUDA_ETIMEOUT if a bounded wait ran out.
+ *   stream: a cudaStream_t (NULL: the default stream). */
+int pa_cuda_attn_noalloc(const pa_cuda_shape *shape, const uint16_t *Qs, const uint8_t *K, const uint8_t *V, uint32_t nk,
+                         float *O, float *m, float *l, void *stream, const char **why);
+
 #ifdef __cplusplus
 }
 #endif
