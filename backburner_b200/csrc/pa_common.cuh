@@ -71,6 +71,13 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
     asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
     return v;
 }
+// the same with a compile-time byte offset folded into the instruction (no separate address add)
+template <int OFF>
+__device__ __forceinline__ uint32_t lds32o(uint32_t base) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1+%2];" : "=r"(v) : "r"(base), "n"(OFF));
+    return v;
+}
 __device__ __forceinline__ uint32_t lds16(uint32_t addr) {
     uint16_t v;
     asm volatile("ld.shared.b16 %0, [%1];" : "=h"(v) : "r"(addr));

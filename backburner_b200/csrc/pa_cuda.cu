@@ -11,6 +11,7 @@
 #include <chrono>
 #include <mutex>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -181,7 +182,7 @@ cudaError_t launch_prefill(const pa_cuda_plan *p, const CUtensorMap &tq, const p
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid(p->n_jobs, p->sh.nkv * p->n_rt);
-    kern<<<grid, 32 * (6 + 4 * NT), smem, st>>>(tq, prm);
+    kern<<<grid, 32 * (8 + 4 * NT), smem, st>>>(tq, prm);
     return cudaGetLastError();
 }
 
@@ -419,7 +420,9 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
     p->prefill = tc_ok && (ctx->kernel_choice == 2 || (ctx->kernel_choice == 0 && shape->rows >= kPrefillMinRows));
     if (ctx->kernel_choice == 2 && !tc_ok) { delete p; return fail(ctx, PA_CUDA_EUNSUPPORTED, "tcgen05 kernel needs hd 128"); }
     if (p->prefill) {
-        p->nt = shape->rows > (uint32_t) pa::pre::BM ? 2 : 1;
+        // PA_CUDA_TC_TILES=1|2: Q tiles of 128 rows per CTA (default: 2 when there are more than 128 rows)
+        static const int tiles_env = getenv("PA_CUDA_TC_TILES") ? atoi(getenv("PA_CUDA_TC_TILES")) : 0;
+        p->nt = (tiles_env == 1 || tiles_env == 2) ? tiles_env : (shape->rows > (uint32_t) pa::pre::BM ? 2 : 1);
         p->n_rt = (shape->rows + pa::pre::BM * p->nt - 1) / (pa::pre::BM * p->nt);
         p->grid_y = shape->nkv * p->n_rt;
     }

@@ -254,8 +254,17 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
 #pragma unroll
                 for (int kk = 0; kk < 2; kk++) {
                     const uint32_t rb = tk + kofs(2 * g + kk) + pb + 4 * (odd ? NWK - 1 : 0);   // MMA rows g, g+8
-#pragma unroll
-                    for (int i = 0; i < NWK; i++) w[kk][i] = lds32(rb + 4 * i);
+                    w[kk][0] = lds32o<0>(rb);
+                    w[kk][1] = lds32o<4>(rb);
+                    w[kk][2] = lds32o<8>(rb);
+                    w[kk][3] = lds32o<12>(rb);
+                    w[kk][4] = lds32o<16>(rb);
+                    if (NWK > 5) {
+                        w[kk][5 % NWK] = lds32o<20>(rb);
+                        w[kk][6 % NWK] = lds32o<24>(rb);
+                        w[kk][7 % NWK] = lds32o<28>(rb);
+                        w[kk][8 % NWK] = lds32o<32>(rb);
+                    }
                     // scale: even block -> first word bytes 0-1; odd block -> first word (shared with the even block) bytes 2-3
                     s2[kk] = prmt(w[kk][0], w[kk][0], odd ? 0x3232u : 0x1010u);
                 }
@@ -336,9 +345,15 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
                     const uint32_t rb = tv + kofs(key[kk]);
                     sc[kk] = lds16(rb + soff);
                     uint32_t raw[NW + 1];
-#pragma unroll
-                    for (int i = 0; i < NW; i++) raw[i] = lds32(rb + wa + 4 * i);
-                    raw[NW] = sig ? lds32(rb + wa + 4 * NW) : 0u;
+                    const uint32_t ra = rb + wa;
+                    raw[0] = lds32o<0>(ra);
+                    raw[1] = lds32o<4>(ra);
+                    if (NW > 2) { raw[2 % (NW + 1)] = lds32o<8>(ra); raw[3 % (NW + 1)] = lds32o<12>(ra); }
+                    if (NW > 4) {
+                        raw[4 % (NW + 1)] = lds32o<16>(ra); raw[5 % (NW + 1)] = lds32o<20>(ra);
+                        raw[6 % (NW + 1)] = lds32o<24>(ra); raw[7 % (NW + 1)] = lds32o<28>(ra);
+                    }
+                    raw[NW] = sig ? lds32(ra + 4 * NW) : 0u;
 #pragma unroll
                     for (int i = 0; i < NW; i++) W[kk][i] = __funnelshift_r(raw[i], raw[i + 1], shift);
                 }

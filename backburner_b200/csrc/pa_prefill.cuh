@@ -99,6 +99,31 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// fp32 pairs (sm_100 .f32x2 arithmetic) and the three-input max
+__device__ __forceinline__ uint64_t pack_f2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void unpack_f2(uint64_t x, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(x));
+}
+__device__ __forceinline__ uint64_t fma_f2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t add_f2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -134,14 +159,15 @@ struct Smem {
 };
 
 template <int QUANT, int NT>
-__global__ void __launch_bounds__(32 * (6 + 4 * NT), 1) prefill_kernel(const __grid_constant__ CUtensorMap tq,
+__global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __grid_constant__ CUtensorMap tq,
                                                                        const Params p) {
     using L = Smem<QUANT, NT>;
     constexpr int RAWB = L::RAWB;
     constexpr int GB = dec::q_group_bytes(QUANT);
     constexpr uint32_t IDESC_S = idesc_f16(BM, BN, 0);
     constexpr uint32_t IDESC_PV = idesc_f16(BM, HD, 1);
-    constexpr int SM0 = 2, DQ0 = 2 + 4 * NT;   // first softmax warp, first dequant warp
+    // warpgroups: 0 = TMA (warp 0) + MMA (warp 1) + 2 idle warps, 1..NT = softmax of tile t, last = dequant
+    constexpr int SM0 = 4, DQ0 = 4 + 4 * NT;   // first softmax warp, first dequant warp
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // operand tiles need 1024-byte alignment (128-byte swizzle atoms): align the dynamic base explicitly
@@ -198,6 +224,8 @@ __global__ void __launch_bounds__(32 * (6 + 4 * NT), 1) prefill_kernel(const __g
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // NT == 2: 16 warps launched with 128 registers each; every warpgroup's branch starts by resizing its share:
+    // control 56, softmax 2 x 168, dequant 120 (128 x (56 + 168 + 168 + 120) = 65,536 = the launched total)
 
     auto wait = [&](uint64_t *b, uint32_t parity) -> bool {
         if (!ok) return false;
@@ -209,7 +237,9 @@ __global__ void __launch_bounds__(32 * (6 + 4 * NT), 1) prefill_kernel(const __g
         return ok;
     };
 
-    if (warp == 0) {
+    if (warp < 4) {
+      if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+      if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
             const int qrow = (int) (((uint64_t) job.set * p.nkv + h) * p.rows + row0);
@@ -238,7 +268,7 @@ __global__ void __launch_bounds__(32 * (6 + 4 * NT), 1) prefill_kernel(const __g
                         atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
             }
         }
-    } else if (warp == 1) {
+      } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
             uint32_t issued_pv = 0;
@@ -286,8 +316,10 @@ __global__ void __launch_bounds__(32 * (6 + 4 * NT), 1) prefill_kernel(const __g
             const uint64_t drain = tmo > dec::DRAIN_NS ? tmo : dec::DRAIN_NS;
             if (!mbar_wait_bounded(mma_done, 0, drain, nullptr)) atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
         }
+      }   // warps 2 and 3: idle
     } else if (warp < (uint32_t) DQ0) {
         // ------------------------------------------------ softmax warpgroup of tile t
+        if (NT == 2) asm volatile("setmaxnreg.inc.sync.aligned.u32 168;");
         const int t = (int) (warp - SM0) / 4;
         const uint32_t wq = warp % 4;                      // TMEM lane quarter of this warp
         const uint32_t r = wq * 32 + lane;                 // row of the tile = TMEM lane
@@ -318,7 +350,8 @@ __global__ void __launch_bounds__(32 * (6 + 4 * NT), 1) prefill_kernel(const __g
             }
             float mx = s[0];
 #pragma unroll
-            for (int i = 1; i < BN; i++) mx = fmaxf(mx, s[i]);
+            for (int i = 1; i + 1 < BN; i += 2) mx = max3(mx, s[i], s[i + 1]);
+            mx = fmaxf(mx, s[BN - 1]);
             mx *= LOG2E;
             float alpha = 1.f;
             bool rescale = false;
@@ -328,14 +361,22 @@ __global__ void __launch_bounds__(32 * (6 + 4 * NT), 1) prefill_kernel(const __g
                 m_used = mx;
                 rescale = true;
             }
-            float sum = 0.f;
+            // p = 2^(s*log2e - m): scale-and-shift and the row sum on fp32 pairs (fma/add .f32x2)
+            const uint64_t l2e2 = pack_f2(LOG2E, LOG2E), nm2 = pack_f2(-m_used, -m_used);
+            uint64_t acc = pack_f2(0.f, 0.f);
             uint32_t ph[32];
 #pragma unroll
             for (int i = 0; i < 32; i++) {
-                const float p0 = ex2(fmaf(s[2 * i], LOG2E, -m_used)), p1 = ex2(fmaf(s[2 * i + 1], LOG2E, -m_used));
-                sum += p0 + p1;
+                float t0, t1;
+                unpack_f2(fma_f2(pack_f2(s[2 * i], s[2 * i + 1]), l2e2, nm2), t0, t1);
+                const float p0 = ex2(t0), p1 = ex2(t1);
+                const uint64_t pp = pack_f2(p0, p1);
+                acc = add_f2(acc, pp);
                 ph[i] = pack_h2(p0, p1);
             }
+            float sa, sb;
+            unpack_f2(acc, sa, sb);
+            const float sum = sa + sb;
             l = fmaf(l, alpha, sum);
             // P buffer and O are free once the previous block's P.V has completed
             if (j >= 1 && !wait(&pv_done[t], (j - 1) & 1)) break;
@@ -383,6 +424,7 @@ __global__ void __launch_bounds__(32 * (6 + 4 * NT), 1) prefill_kernel(const __g
         }
     } else {
         // ------------------------------------------------ dequantisers: warp dw owns quant block dw of every key
+        if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 120;");
         const uint32_t dw = warp - DQ0;
         const uint32_t bo = hoff + GB * dw;                 // block start inside the raw window row
         const uint32_t w16 = bo & ~15u;                     // 16-byte aligned start of the words covering it

@@ -373,7 +373,8 @@ def main():
     try:
         with open(os.path.join(ROOT, "profiles", "decode_traffic.json")) as f:
             tr = json.load(f)
-        traffic = round(tr["dram_bytes_per_key_position"] * nk * L)
+        # ncu DRAM bytes of a smaller capture, scaled to this launch: reads by key positions, writes by jobs (slots)
+        traffic = round(tr["dram_read_bytes_per_key_position"] * nk * L + tr["dram_write_bytes_per_job"] * plan.jobs)
     except Exception:
         pass
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
