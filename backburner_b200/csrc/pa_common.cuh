@@ -66,22 +66,19 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
+// Shared-memory loads by 32-bit shared address. They are plain C++ loads (not volatile asm), so the compiler may
+// schedule them early, e.g. a tile's V words under the softmax of its scores; the mbarrier waits and fences above
+// carry "memory" clobbers, so no load moves across a wait for the data it reads.
 __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
+    return *reinterpret_cast<const uint32_t *>(__cvta_shared_to_generic(addr));
 }
-// the same with a compile-time byte offset folded into the instruction (no separate address add)
+// the same at a compile-time byte offset from base
 template <int OFF>
 __device__ __forceinline__ uint32_t lds32o(uint32_t base) {
-    uint32_t v;
-    asm volatile("ld.shared.b32 %0, [%1+%2];" : "=r"(v) : "r"(base), "n"(OFF));
-    return v;
+    return *reinterpret_cast<const uint32_t *>(__cvta_shared_to_generic(base + OFF));
 }
 __device__ __forceinline__ uint32_t lds16(uint32_t addr) {
-    uint16_t v;
-    asm volatile("ld.shared.b16 %0, [%1];" : "=h"(v) : "r"(addr));
-    return v;
+    return *reinterpret_cast<const uint16_t *>(__cvta_shared_to_generic(addr));
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {

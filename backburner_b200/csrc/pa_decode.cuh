@@ -22,6 +22,9 @@
 //     own quant block (Q's fragments use the same permutation), so one scale per lane and no unpacking shuffles.
 //     V needs keys in pairs along k: two rows' words are byte-interleaved with one PRMT. P's accumulator fragment
 //     becomes P^T's operand fragment with movmatrix (8x8 transpose).
+//   * P is taken against a lazily raised reference max (one warp vote per tile; the cross-lane max and the O rescale
+//     run only when a score passes the reference by 2^8), and the exact row max is restored once per job; a tile's V
+//     words are loaded before its softmax so their shared-memory latency overlaps the softmax.
 #pragma once
 #include "pa_common.cuh"
 
@@ -227,6 +230,13 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
 #pragma unroll
     for (int mt = 0; mt < NMT; mt++) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
     float m0 = M_EMPTY, m1 = M_EMPTY, l0 = 0.f, l1 = 0.f;   // rows 2t, 2t+1 of the 8-row group
+    // Lazy running max: P is taken against a reference max mb (log2 units) that moves only when a score exceeds it by
+    // more than LAZY_T (P <= 2^LAZY_T, well inside f16), so most tiles skip the cross-lane max and the O rescale. The
+    // exact maximum (ml, lane-local then reduced) is restored at the end: O and l are rescaled to it once.
+    constexpr float LAZY_T = 8.f;
+    float mb0 = M_EMPTY * LOG2E, mb1 = M_EMPTY * LOG2E;
+    float th0 = M_EMPTY, th1 = M_EMPTY;        // scores (natural units) above these move mb
+    float ml0 = -INFINITY, ml1 = -INFINITY;    // lane-local maxima of the scores
     bool ok = true;
     if (p.stall && !mbar_wait_bounded(never, 0, p.timeout_ns, abort_flag)) ok = false;
 
@@ -249,35 +259,37 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
                 const int blk = t + 4 * rep;
                 const uint32_t odd = blk % 2;
                 const uint32_t pb = (uint32_t) (PAIR * (blk / 2));
-                constexpr int NWK = QUANT == 1 ? 9 : 5;   // aligned words covering the lane's block (+ its scale)
-                uint32_t w[2][NWK], s2[2];
+                // the lane's words: NWK-1 "slots" of its values, then the pair's shared word (even block: its last
+                // values; odd block: its scale). Even block: slots = pair words 0..NWK-2; odd block: the NWK-1 aligned
+                // words after the shared one. One lane-dependent PRMT selector then serves both parities.
+                constexpr int NWK = QUANT == 1 ? 9 : 5;
+                const uint32_t ssel = odd ? 0x7676u : 0x1010u;   // scale: odd -> shared word bytes 2-3, even -> slot 0 bytes 0-1
+                const uint32_t gsel = odd ? 0x3210u : 0x5432u;   // group 0: odd -> slot 0, even -> (v0, v1 | v30, v31)
+                uint32_t w[2][NWK], s2[2], g0[2];
 #pragma unroll
                 for (int kk = 0; kk < 2; kk++) {
-                    const uint32_t rb = tk + kofs(2 * g + kk) + pb + 4 * (odd ? NWK - 1 : 0);   // MMA rows g, g+8
+                    const uint32_t rk = tk + kofs(2 * g + kk) + pb;   // MMA rows g, g+8
+                    const uint32_t rb = rk + (odd ? 4u * NWK : 0u);
                     w[kk][0] = lds32o<0>(rb);
                     w[kk][1] = lds32o<4>(rb);
                     w[kk][2] = lds32o<8>(rb);
                     w[kk][3] = lds32o<12>(rb);
-                    w[kk][4] = lds32o<16>(rb);
                     if (NWK > 5) {
+                        w[kk][4 % NWK] = lds32o<16>(rb);
                         w[kk][5 % NWK] = lds32o<20>(rb);
                         w[kk][6 % NWK] = lds32o<24>(rb);
                         w[kk][7 % NWK] = lds32o<28>(rb);
-                        w[kk][8 % NWK] = lds32o<32>(rb);
                     }
-                    // scale: even block -> first word bytes 0-1; odd block -> first word (shared with the even block) bytes 2-3
-                    s2[kk] = prmt(w[kk][0], w[kk][0], odd ? 0x3232u : 0x1010u);
+                    w[kk][NWK - 1] = lds32o<4 * (NWK - 1)>(rk);
+                    s2[kk] = prmt(w[kk][0], w[kk][NWK - 1], ssel);
+                    g0[kk] = prmt(w[kk][0], w[kk][NWK - 1], gsel);
                 }
                 if (QUANT == 1) {
 #pragma unroll
                     for (int ss = 0; ss < 8; ss++) {
                         uint32_t lo[2], hi[2];
 #pragma unroll
-                        for (int kk = 0; kk < 2; kk++) {
-                            // odd block: words 1..8 are its 32 values; even block: (q0,q1 | q30,q31), then words 1..7
-                            const uint32_t grp = odd ? w[kk][1 + ss] : (ss == 0 ? prmt(w[kk][0], w[kk][8], 0x5432u) : w[kk][ss]);
-                            q8_word(grp, s2[kk], lo[kk], hi[kk]);
-                        }
+                        for (int kk = 0; kk < 2; kk++) q8_word(ss == 0 ? g0[kk] : w[kk][ss], s2[kk], lo[kk], hi[kk]);
                         const int sidx = 8 * rep + ss;
                         mma16816(c, lo[0], lo[1], hi[0], hi[1], qf[sidx][0], qf[sidx][1]);
                     }
@@ -287,8 +299,7 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
                         uint32_t l02[2], l13[2], h02[2], h13[2];
 #pragma unroll
                         for (int kk = 0; kk < 2; kk++) {
-                            const uint32_t grp = odd ? w[kk][1 + gi] : (gi == 0 ? prmt(w[kk][0], w[kk][4], 0x5432u) : w[kk][gi]);
-                            q4_word(grp, s2[kk], l02[kk], l13[kk], h02[kk], h13[kk]);
+                            q4_word(gi == 0 ? g0[kk] : w[kk][gi], s2[kk], l02[kk], l13[kk], h02[kk], h13[kk]);
                         }
                         const int sidx = 8 * rep + 2 * gi;
                         mma16816(c, l02[0], l02[1], l13[0], l13[1], qf[sidx][0], qf[sidx][1]);
@@ -297,75 +308,82 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
                 }
             }
 
-            // ---- online softmax over this tile (rows 2t, 2t+1; keys g, g+8)
+            // ---- V words of the tile, loaded before the softmax so that their latency hides under it
+            // k indices 2t, 2t+1, 2t+8, 2t+9 are MMA rows of S^T, i.e. keys 4t, 4t+2, 4t+1, 4t+3
+            const uint32_t key[4] = {4 * t, 4 * t + 2, 4 * t + 1, 4 * t + 3};
+            // the lane's data bytes start 2 bytes into a word for even quant blocks: load the covering words and
+            // shift them into alignment (funnel shift by 8*sig bits; sig is 0 or 2), so every later index is static
+            constexpr int NB = QUANT == 1 ? (HD == 128 ? 16 : 32) : (HD == 128 ? 8 : 16);   // bytes per lane per key
+            constexpr int NW = NB / 4;
+            const int b = HD == 128 ? (int) g / 2 : (int) g;
+            const int hh = HD == 128 ? (int) g % 2 : 0;
+            const uint32_t pb = (uint32_t) (PAIR * (b / 2));
+            const uint32_t start = QUANT == 1 ? pb + ((b % 2) ? 36u : 2u) + 16u * hh : pb + ((b % 2) ? 20u : 2u) + 8u * hh;
+            const uint32_t sig = start % 4, wa = start - sig, shift = 8 * sig;
+            const uint32_t soff = pb + ((b % 2) ? (uint32_t) GB : 0u);
+            uint32_t sc[4];
+            uint32_t W[4][NW];
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                const uint32_t rb = tv + kofs(key[kk]);
+                sc[kk] = lds16(rb + soff);
+                uint32_t raw[NW + 1];
+                const uint32_t ra = rb + wa;
+                raw[0] = lds32o<0>(ra);
+                raw[1] = lds32o<4>(ra);
+                if (NW > 2) { raw[2 % (NW + 1)] = lds32o<8>(ra); raw[3 % (NW + 1)] = lds32o<12>(ra); }
+                if (NW > 4) {
+                    raw[4 % (NW + 1)] = lds32o<16>(ra); raw[5 % (NW + 1)] = lds32o<20>(ra);
+                    raw[6 % (NW + 1)] = lds32o<24>(ra); raw[7 % (NW + 1)] = lds32o<28>(ra);
+                }
+                raw[NW] = sig ? lds32(ra + 4 * NW) : 0u;
+#pragma unroll
+                for (int i = 0; i < NW; i++) W[kk][i] = __funnelshift_r(raw[i], raw[i + 1], shift);
+            }
+            // keys past the stage's valid count hold whatever the buffer held before (possibly never written):
+            // a zero scale makes their V exactly 0, so P = 0 times it cannot produce NaN
+            if (tvalid < TILE_KEYS) {
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++)
+                    if ((int) key[kk] >= tvalid) sc[kk] = 0u;
+            }
+            // key pairs: (key0,key1) -> a0/a1, (key2,key3) -> a2/a3
+            const uint32_t s01 = sc[0] | (sc[1] << 16), s23 = sc[2] | (sc[3] << 16);
+
+            // ---- online softmax over this tile (rows 2t, 2t+1; keys g, g+8) against the lazy reference max
             if (tvalid < TILE_KEYS) {
                 if ((int) (2 * g) >= tvalid) c[0] = c[1] = -INFINITY;       // row g = key 2g
                 if ((int) (2 * g + 1) >= tvalid) c[2] = c[3] = -INFINITY;   // row g+8 = key 2g+1
             }
             float mx0 = fmaxf(c[0], c[2]), mx1 = fmaxf(c[1], c[3]);
+            ml0 = fmaxf(ml0, mx0);
+            ml1 = fmaxf(ml1, mx1);
+            if (__any_sync(0xffffffffu, mx0 > th0 || mx1 > th1)) {
 #pragma unroll
-            for (int x = 4; x < 32; x <<= 1) {
-                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, x));
-                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, x));
-            }
-            const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-            const float al0 = ex2((m0 - mn0) * LOG2E), al1 = ex2((m1 - mn1) * LOG2E);
-            const float b0 = -mn0 * LOG2E, b1 = -mn1 * LOG2E;
-            const float p0 = ex2(fmaf(c[0], LOG2E, b0)), p1 = ex2(fmaf(c[1], LOG2E, b1));
-            const float p2 = ex2(fmaf(c[2], LOG2E, b0)), p3 = ex2(fmaf(c[3], LOG2E, b1));
-            l0 = fmaf(l0, al0, p0 + p2);
-            l1 = fmaf(l1, al1, p1 + p3);
-            m0 = mn0;
-            m1 = mn1;
-            if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
+                for (int x = 4; x < 32; x <<= 1) {
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, x));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, x));
+                }
+                const float nb0 = fmaxf(mb0, mx0 * LOG2E), nb1 = fmaxf(mb1, mx1 * LOG2E);
+                const float al0 = ex2(mb0 - nb0), al1 = ex2(mb1 - nb1);
+                l0 *= al0;
+                l1 *= al1;
 #pragma unroll
                 for (int mt = 0; mt < NMT; mt++) { o[mt][0] *= al0; o[mt][1] *= al1; o[mt][2] *= al0; o[mt][3] *= al1; }
+                mb0 = nb0;
+                mb1 = nb1;
+                th0 = (mb0 + LAZY_T) * (1.f / LOG2E);
+                th1 = (mb1 + LAZY_T) * (1.f / LOG2E);
             }
+            const float p0 = ex2(fmaf(c[0], LOG2E, -mb0)), p1 = ex2(fmaf(c[1], LOG2E, -mb1));
+            const float p2 = ex2(fmaf(c[2], LOG2E, -mb0)), p3 = ex2(fmaf(c[3], LOG2E, -mb1));
+            l0 += p0 + p2;
+            l1 += p1 + p3;
             const uint32_t pb0 = movtrans(pack_h2(p0, p1));   // P^T keys 2t,2t+1 for row g
             const uint32_t pb1 = movtrans(pack_h2(p2, p3));   // keys 2t+8, 2t+9
 
             // ---- O^T += V^T . P^T  (lane: keys 2t,2t+1,2t+8,2t+9; head-dim rows dV(mt, g, 0/1))
             {
-                // k indices 2t, 2t+1, 2t+8, 2t+9 are MMA rows of S^T, i.e. keys 4t, 4t+2, 4t+1, 4t+3
-                const uint32_t key[4] = {4 * t, 4 * t + 2, 4 * t + 1, 4 * t + 3};
-                // the lane's data bytes start 2 bytes into a word for even quant blocks: load the covering words and
-                // shift them into alignment (funnel shift by 8*sig bits; sig is 0 or 2), so every later index is static
-                constexpr int NB = QUANT == 1 ? (HD == 128 ? 16 : 32) : (HD == 128 ? 8 : 16);   // bytes per lane per key
-                constexpr int NW = NB / 4;
-                const int b = HD == 128 ? (int) g / 2 : (int) g;
-                const int hh = HD == 128 ? (int) g % 2 : 0;
-                const uint32_t pb = (uint32_t) (PAIR * (b / 2));
-                const uint32_t start = QUANT == 1 ? pb + ((b % 2) ? 36u : 2u) + 16u * hh : pb + ((b % 2) ? 20u : 2u) + 8u * hh;
-                const uint32_t sig = start % 4, wa = start - sig, shift = 8 * sig;
-                const uint32_t soff = pb + ((b % 2) ? (uint32_t) GB : 0u);
-                uint32_t sc[4];
-                uint32_t W[4][NW];
-#pragma unroll
-                for (int kk = 0; kk < 4; kk++) {
-                    const uint32_t rb = tv + kofs(key[kk]);
-                    sc[kk] = lds16(rb + soff);
-                    uint32_t raw[NW + 1];
-                    const uint32_t ra = rb + wa;
-                    raw[0] = lds32o<0>(ra);
-                    raw[1] = lds32o<4>(ra);
-                    if (NW > 2) { raw[2 % (NW + 1)] = lds32o<8>(ra); raw[3 % (NW + 1)] = lds32o<12>(ra); }
-                    if (NW > 4) {
-                        raw[4 % (NW + 1)] = lds32o<16>(ra); raw[5 % (NW + 1)] = lds32o<20>(ra);
-                        raw[6 % (NW + 1)] = lds32o<24>(ra); raw[7 % (NW + 1)] = lds32o<28>(ra);
-                    }
-                    raw[NW] = sig ? lds32(ra + 4 * NW) : 0u;
-#pragma unroll
-                    for (int i = 0; i < NW; i++) W[kk][i] = __funnelshift_r(raw[i], raw[i + 1], shift);
-                }
-                // keys past the stage's valid count hold whatever the buffer held before (possibly never written):
-                // a zero scale makes their V exactly 0, so P = 0 times it cannot produce NaN
-                if (tvalid < TILE_KEYS) {
-#pragma unroll
-                    for (int kk = 0; kk < 4; kk++)
-                        if ((int) key[kk] >= tvalid) sc[kk] = 0u;
-                }
-                // key pairs: (key0,key1) -> a0/a1, (key2,key3) -> a2/a3
-                const uint32_t s01 = sc[0] | (sc[1] << 16), s23 = sc[2] | (sc[3] << 16);
                 if (QUANT == 1) {
 #pragma unroll
                     for (int mt = 0; mt < NMT; mt++) {
@@ -409,6 +427,24 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
     if (!ok) {
         abort_and_drain();
         return;
+    }
+
+    // ---- report the exact maximum of each row: rescale O and l from the lazy reference max to it (an empty row keeps
+    // m = M_EMPTY, l = 0)
+#pragma unroll
+    for (int x = 4; x < 32; x <<= 1) {
+        ml0 = fmaxf(ml0, __shfl_xor_sync(0xffffffffu, ml0, x));
+        ml1 = fmaxf(ml1, __shfl_xor_sync(0xffffffffu, ml1, x));
+    }
+    {
+        const float f0 = ml0 > -INFINITY ? ex2(mb0 - ml0 * LOG2E) : 1.f;
+        const float f1 = ml1 > -INFINITY ? ex2(mb1 - ml1 * LOG2E) : 1.f;
+        l0 *= f0;
+        l1 *= f1;
+#pragma unroll
+        for (int mt = 0; mt < NMT; mt++) { o[mt][0] *= f0; o[mt][1] *= f1; o[mt][2] *= f0; o[mt][3] *= f1; }
+        m0 = ml0 > -INFINITY ? ml0 : M_EMPTY;
+        m1 = ml1 > -INFINITY ? ml1 : M_EMPTY;
     }
 
     // ---- finish: l summed over the lanes of a row (keys g), then the partner warp (if any) folded in
