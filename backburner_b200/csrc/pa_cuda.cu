@@ -94,13 +94,15 @@ int cuda_fail(pa_cuda_ctx *ctx, cudaError_t e, const char *what) {
 
 cudaStream_t pick(pa_cuda_ctx *ctx, void *stream) { return stream ? (cudaStream_t) stream : ctx->stream; }
 
-size_t head_bytes(uint32_t quant, uint32_t hd) { return quant == PA_CUDA_Q8_0 ? hd / 32 * 34 : hd / 32 * 18; }
+size_t head_bytes(uint32_t quant, uint32_t hd) {
+    return quant == PA_CUDA_Q8_0 ? hd / 32 * 34 : quant == PA_CUDA_Q4_0 ? hd / 32 * 18 : hd * 2;
+}
 
 int check_shape(pa_cuda_ctx *ctx, const pa_cuda_shape *sh) {
     if (!sh) return fail(ctx, PA_CUDA_EINVAL, "shape is null");
     if (sh->hd != 128 && sh->hd != 256) return fail(ctx, PA_CUDA_EUNSUPPORTED, "hd must be 128 or 256");
-    if (sh->quant != PA_CUDA_Q8_0 && sh->quant != PA_CUDA_Q4_0)
-        return fail(ctx, PA_CUDA_EUNSUPPORTED, "quant must be Q8_0 (1) or Q4_0 (2)");
+    if (sh->quant != PA_CUDA_F16 && sh->quant != PA_CUDA_Q8_0 && sh->quant != PA_CUDA_Q4_0)
+        return fail(ctx, PA_CUDA_EUNSUPPORTED, "quant must be F16 (0), Q8_0 (1) or Q4_0 (2)");
     if (sh->nkv < 1 || sh->nkv > 64) return fail(ctx, PA_CUDA_EINVAL, "nkv out of range");
     if (sh->rows < 1) return fail(ctx, PA_CUDA_EINVAL, "rows must be >= 1");
     if (sh->hb != head_bytes(sh->quant, sh->hd)) return fail(ctx, PA_CUDA_EINVAL, "hb does not match quant/hd");
@@ -114,14 +116,26 @@ int plan_decode_shape(pa_cuda_ctx *ctx, pa_cuda_plan *p) {
     const pa_cuda_shape &sh = p->sh;
     const uint32_t maxw = sh.hd == 128 ? 16 : 12;
     p->n_rg = (sh.rows + 7) / 8;
+    // shared memory of NSTAGE stages of key pairs for head-group rows of `row` bytes (pairs padded to an odd number of
+    // 16-byte units)
+    auto pair_stride = [](uint32_t row) { uint32_t gs = 2 * row; return (gs / 16) % 2 == 0 ? gs + 16 : gs; };
+    auto smem_for = [](uint32_t gs) {
+        return (size_t) pa::dec::NSTAGE * pa::dec::STAGE_KEYS * gs + pa::dec::SMEM_SLACK + (pa::dec::NSTAGE + 3) * 8 +
+               2 * pa::dec::NSTAGE * 4 + 16;
+    };
+    // the largest head group that divides nkv, gives 16-byte aligned rows and fits shared memory
     uint32_t hg = 0;
+    bool aligned = false;
     for (uint32_t c = std::min(sh.nkv, maxw); c >= 1; c--) {
         if (sh.nkv % c) continue;
         if ((c * sh.hb) % 16) continue;
+        aligned = true;
+        if (smem_for(pair_stride((uint32_t) (c * sh.hb))) > (size_t) kMaxSmem) continue;
         hg = c;
         break;
     }
-    if (!hg) return fail(ctx, PA_CUDA_EUNSUPPORTED, "no head grouping gives 16-byte aligned rows (nkv * hb)");
+    if (!hg && !aligned) return fail(ctx, PA_CUDA_EUNSUPPORTED, "no head grouping gives 16-byte aligned rows (nkv * hb)");
+    if (!hg) return fail(ctx, PA_CUDA_EUNSUPPORTED, "rows of this head group do not fit shared memory");
     p->hg = hg;
     p->rgc = std::min(p->n_rg, maxw / hg);
     const uint32_t S = hg * p->rgc;
@@ -129,12 +143,8 @@ int plan_decode_shape(pa_cuda_ctx *ctx, pa_cuda_plan *p) {
     p->n_consumers = S * p->pw;
     p->grid_y = (sh.nkv / hg) * ((p->n_rg + p->rgc - 1) / p->rgc);
     p->row = (uint32_t) (hg * sh.hb);                  // a multiple of 16 by the choice of hg
-    uint32_t gs = 2 * p->row;
-    if ((gs / 16) % 2 == 0) gs += 16;                 // odd number of 16-byte units per pair
-    p->gs = gs;
-    p->smem = (size_t) pa::dec::NSTAGE * pa::dec::STAGE_KEYS * gs + pa::dec::SMEM_SLACK +
-              (pa::dec::NSTAGE + 3) * 8 + 2 * pa::dec::NSTAGE * 4 + 16;
-    if (p->smem > (size_t) kMaxSmem) return fail(ctx, PA_CUDA_EUNSUPPORTED, "rows of this head group do not fit shared memory");
+    p->gs = pair_stride(p->row);
+    p->smem = smem_for(p->gs);
     return PA_CUDA_OK;
 }
 
@@ -194,6 +204,15 @@ cudaError_t launch_decode(const pa_cuda_plan *p, const pa::dec::Params &prm, cud
     dim3 grid(p->n_jobs, p->grid_y);
     kern<<<grid, 32 * p->n_consumers, p->smem, st>>>(prm);
     return cudaGetLastError();
+}
+// the decode-kernel instance of a geometry (hd 128 / 256; f16, Q8_0 or Q4_0 rows)
+cudaError_t launch_decode_any(const pa_cuda_plan *p, const pa::dec::Params &prm, cudaStream_t st, uint32_t hd,
+                              uint32_t quant) {
+    if (hd == 128)
+        return quant == PA_CUDA_Q8_0 ? launch_decode<128, 1>(p, prm, st)
+             : quant == PA_CUDA_Q4_0 ? launch_decode<128, 2>(p, prm, st) : launch_decode<128, 0>(p, prm, st);
+    return quant == PA_CUDA_Q8_0 ? launch_decode<256, 1>(p, prm, st)
+         : quant == PA_CUDA_Q4_0 ? launch_decode<256, 2>(p, prm, st) : launch_decode<256, 0>(p, prm, st);
 }
 
 template <int HD>
@@ -259,8 +278,7 @@ int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, 
         const bool prof = p->profile && p->ev_used + 2 <= p->ev.size();
         if (prof) cudaEventRecord(p->ev[p->ev_used], st);
         cudaError_t e;
-        if (sh.hd == 128) e = sh.quant == PA_CUDA_Q8_0 ? launch_decode<128, 1>(p, prm, st) : launch_decode<128, 2>(p, prm, st);
-        else e = sh.quant == PA_CUDA_Q8_0 ? launch_decode<256, 1>(p, prm, st) : launch_decode<256, 2>(p, prm, st);
+        e = launch_decode_any(p, prm, st, sh.hd, sh.quant);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "decode kernel launch");
         if (prof) {
             cudaEventRecord(p->ev[p->ev_used + 1], st);
@@ -416,9 +434,12 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
     if ((rc = plan_decode_shape(ctx, p))) { delete p; return rc; }
     // the tcgen05 kernel takes calls with many query rows per KV head (prefill, ATTN_BIG, long verify batches), the
     // split-K kernel the decode-sized ones (as the reference engine switches kernels by rows, pa-metal.mm:818-835)
-    const bool tc_ok = shape->hd == 128 && encode_fn() != nullptr;
+    const bool tc_ok = shape->hd == 128 && shape->quant != PA_CUDA_F16 && encode_fn() != nullptr;
     p->prefill = tc_ok && (ctx->kernel_choice == 2 || (ctx->kernel_choice == 0 && shape->rows >= kPrefillMinRows));
-    if (ctx->kernel_choice == 2 && !tc_ok) { delete p; return fail(ctx, PA_CUDA_EUNSUPPORTED, "tcgen05 kernel needs hd 128"); }
+    if (ctx->kernel_choice == 2 && !tc_ok) {
+        delete p;
+        return fail(ctx, PA_CUDA_EUNSUPPORTED, "tcgen05 kernel needs hd 128 and quantised (Q8_0 / Q4_0) rows");
+    }
     if (p->prefill) {
         // PA_CUDA_TC_TILES=1|2: Q tiles of 128 rows per CTA (default: 2 when there are more than 128 rows)
         static const int tiles_env = getenv("PA_CUDA_TC_TILES") ? atoi(getenv("PA_CUDA_TC_TILES")) : 0;
@@ -969,8 +990,7 @@ extern "C" int pa_cuda_attn_noalloc(const pa_cuda_shape *shape, const uint16_t *
         prm.timeout_ns = 2000000000ull;
         prm.stall = 0;
         cudaError_t e;
-        if (shape->hd == 128) e = shape->quant == PA_CUDA_Q8_0 ? launch_decode<128, 1>(&p, prm, st) : launch_decode<128, 2>(&p, prm, st);
-        else e = shape->quant == PA_CUDA_Q8_0 ? launch_decode<256, 1>(&p, prm, st) : launch_decode<256, 2>(&p, prm, st);
+        e = launch_decode_any(&p, prm, st, shape->hd, shape->quant);
         if (e != cudaSuccess) return na_fail(why, PA_CUDA_ECUDA, "split-K kernel launch failed");
     }
     pa::mrg::Params mp{};

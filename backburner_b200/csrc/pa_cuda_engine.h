@@ -17,8 +17,9 @@
 //                          ntok_hint real tokens' rows (phone-attn/pa-metal.mm:627-646).
 //   end                  : waits; unnormalised O [ng][nkv*48][256], m, l; -1 and m = -inf, l = 0 on failure
 //                          (phone-attn/pa-metal.mm:928-937).
-// Not covered: f16 page storage (config_req.store_f16 / is_q8 == 0): begin() fails with an error, the server answers
-// ERR.
+//   page formats         : whatever the server's store_cfg() says (phone-attn/phone-attn.h:298-302): Q8_0 and Q4_0
+//                          rows as received, or f16 rows (is_q8 == 0, store_f16), all on the split-K kernel; the
+//                          tcgen05 kernel takes quantised rows with hd 128 only.
 #pragma once
 #include <string>
 #include <vector>

@@ -64,12 +64,14 @@ struct Params {
     int stall;            // test hook: consumers first wait on a barrier that nothing completes (bounded)
 };
 
-__host__ __device__ constexpr int q_group_bytes(int quant) { return quant == 1 ? 34 : 18; }
+__host__ __device__ constexpr int q_group_bytes(int quant) { return quant == 1 ? 34 : quant == 2 ? 18 : 64; }
 
 // ---------------------------------------------------------------- d permutations (host + device)
 // QK^T: lane t of a quad feeds k = {2t, 2t+1, 2t+8, 2t+9} of each k-step s. Those 4 values are one 4-byte group of the
 // lane's own quant block. dK(s, t, i) is the head-dim index of the i-th of them (i: 0,1 -> k = 2t,2t+1; 2,3 -> 2t+8,2t+9).
 __host__ __device__ inline int dK(int quant, int s, int t, int i) {
+    // f16 rows: natural order (ldmatrix fragments): k = 2t, 2t+1 -> d 16s + 2t + i; k = 2t+8, 2t+9 -> d 16s + 8 + 2t + i-2
+    if (quant == 0) return 16 * s + 2 * t + (i < 2 ? i : 6 + i);
     const int blk = t + 4 * (s / 8), ss = s % 8;
     if (quant == 1) {
         // a pair of q8_0 blocks = 68 bytes = 17 aligned words; even block: (d,q0,q1)(q2..q5)...(q30,q31,d'), odd: d' then
@@ -94,6 +96,7 @@ __host__ __device__ inline int dK(int quant, int s, int t, int i) {
 // P.V: lane g of the A fragment (V^T) holds two head-dim rows per m-tile mt: dV(mt, g, 0) (row g) and dV(mt, g, 1)
 // (row g + 8). Lane g owns a contiguous byte range of one quant block.
 __host__ __device__ inline int dV(int quant, int hd, int mt, int g, int half) {
+    if (quant == 0) return 16 * mt + g + 8 * half;   // f16 rows: ldmatrix.trans fragments, natural order
     if (quant == 1) {
         const int base = hd == 128 ? 16 * g : 32 * g;
         return base + 2 * mt + half;
@@ -180,10 +183,20 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
         __syncwarp();
         if (2 * lane < valid) {   // lane copies keys 2*lane, 2*lane+1 (one row if the stage ends there)
             const uint64_t off = (uint64_t) (it * STAGE_KEYS + 2 * lane) * p.rs;
-            const uint32_t bytes = (2 * lane + 1 < valid ? 2u : 1u) * copy_bytes;
+            const bool two = 2 * lane + 1 < valid;
             uint8_t *dst = smem + s * stage_bytes + lane * gs;
-            bulk_g2s(dst, kb + off, bytes, &full[s]);
-            bulk_g2s(dst + half_stage, vb + off, bytes, &full[s]);
+            if (p.rs == copy_bytes) {   // the head group is the whole position: the pair is one contiguous range
+                const uint32_t bytes = (two ? 2u : 1u) * copy_bytes;
+                bulk_g2s(dst, kb + off, bytes, &full[s]);
+                bulk_g2s(dst + half_stage, vb + off, bytes, &full[s]);
+            } else {                    // a head group of a wider (or padded) position: one copy per row
+                bulk_g2s(dst, kb + off, copy_bytes, &full[s]);
+                bulk_g2s(dst + half_stage, vb + off, copy_bytes, &full[s]);
+                if (two) {
+                    bulk_g2s(dst + row, kb + off + p.rs, copy_bytes, &full[s]);
+                    bulk_g2s(dst + half_stage + row, vb + off + p.rs, copy_bytes, &full[s]);
+                }
+            }
         }
     };
     // after a wait gave up: every copy issued so far lands before the CTA exits (warp 0 waits for them, bounded)
@@ -254,6 +267,17 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
 
             // ---- S^T = K . Qs^T  (lane: keys g, g+8; its quant block(s) t (+4))
             float c[4] = {0.f, 0.f, 0.f, 0.f};
+            if constexpr (QUANT == 0) {
+                // f16 rows: ldmatrix.x4 gives each k-step's A fragment (matrices: keys 2r | 2r+1 x d +0 | +8)
+                const uint32_t r = lane % 8, mi = lane / 8;
+                const uint32_t ka = tk + kofs(2 * r + (mi & 1)) + (mi >> 1) * 16;
+#pragma unroll
+                for (int ks = 0; ks < NMT; ks++) {
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4(ka + 32 * ks, a0, a1, a2, a3);
+                    mma16816(c, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+                }
+            } else {
 #pragma unroll
             for (int rep = 0; rep < HD / 128; rep++) {
                 const int blk = t + 4 * rep;
@@ -307,14 +331,19 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
                     }
                 }
             }
+            }
 
             // ---- V words of the tile, loaded before the softmax so that their latency hides under it
             // k indices 2t, 2t+1, 2t+8, 2t+9 are MMA rows of S^T, i.e. keys 4t, 4t+2, 4t+1, 4t+3
             const uint32_t key[4] = {4 * t, 4 * t + 2, 4 * t + 1, 4 * t + 3};
             // the lane's data bytes start 2 bytes into a word for even quant blocks: load the covering words and
             // shift them into alignment (funnel shift by 8*sig bits; sig is 0 or 2), so every later index is static
-            constexpr int NB = QUANT == 1 ? (HD == 128 ? 16 : 32) : (HD == 128 ? 8 : 16);   // bytes per lane per key
+            // (f16 rows: the P.V fragments come from ldmatrix.trans in the P.V loop instead)
+            constexpr int NB = QUANT == 1 ? (HD == 128 ? 16 : 32) : QUANT == 2 ? (HD == 128 ? 8 : 16) : 4;   // bytes per lane per key
             constexpr int NW = NB / 4;
+            uint32_t W[4][NW];
+            uint32_t s01 = 0, s23 = 0;
+            if constexpr (QUANT != 0) {
             const int b = HD == 128 ? (int) g / 2 : (int) g;
             const int hh = HD == 128 ? (int) g % 2 : 0;
             const uint32_t pb = (uint32_t) (PAIR * (b / 2));
@@ -322,7 +351,6 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
             const uint32_t sig = start % 4, wa = start - sig, shift = 8 * sig;
             const uint32_t soff = pb + ((b % 2) ? (uint32_t) GB : 0u);
             uint32_t sc[4];
-            uint32_t W[4][NW];
 #pragma unroll
             for (int kk = 0; kk < 4; kk++) {
                 const uint32_t rb = tv + kofs(key[kk]);
@@ -348,7 +376,9 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
                     if ((int) key[kk] >= tvalid) sc[kk] = 0u;
             }
             // key pairs: (key0,key1) -> a0/a1, (key2,key3) -> a2/a3
-            const uint32_t s01 = sc[0] | (sc[1] << 16), s23 = sc[2] | (sc[3] << 16);
+            s01 = sc[0] | (sc[1] << 16);
+            s23 = sc[2] | (sc[3] << 16);
+            }
 
             // ---- online softmax over this tile (rows 2t, 2t+1; keys g, g+8) against the lazy reference max
             if (tvalid < TILE_KEYS) {
@@ -384,7 +414,24 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(c
 
             // ---- O^T += V^T . P^T  (lane: keys 2t,2t+1,2t+8,2t+9; head-dim rows dV(mt, g, 0/1))
             {
-                if (QUANT == 1) {
+                if constexpr (QUANT == 0) {
+                    // f16 rows: ldmatrix.x4.trans gives each m-tile's A fragment (matrices: keys 2r | 2r+1 of the P^T
+                    // order x d +0 | +8); keys past the stage's valid count are zeroed in the fragment (their rows
+                    // may hold anything, and 0 * NaN would poison O)
+                    const uint32_t r = lane % 8, mi = lane / 8;
+                    const uint32_t va = tv + kofs(2 * r + (mi >> 1)) + (mi & 1) * 16;
+                    uint32_t m01 = 0xFFFFFFFFu, m23 = 0xFFFFFFFFu;
+                    if (tvalid < TILE_KEYS) {
+                        m01 = ((int) key[0] < tvalid ? 0x0000FFFFu : 0u) | ((int) key[1] < tvalid ? 0xFFFF0000u : 0u);
+                        m23 = ((int) key[2] < tvalid ? 0x0000FFFFu : 0u) | ((int) key[3] < tvalid ? 0xFFFF0000u : 0u);
+                    }
+#pragma unroll
+                    for (int mt = 0; mt < NMT; mt++) {
+                        uint32_t a0, a1, a2, a3;
+                        ldsm_x4_t(va + 32 * mt, a0, a1, a2, a3);
+                        mma16816(o[mt], a0 & m01, a1 & m01, a2 & m23, a3 & m23, pb0, pb1);
+                    }
+                } else if constexpr (QUANT == 1) {
 #pragma unroll
                     for (int mt = 0; mt < NMT; mt++) {
                         constexpr uint32_t SEL[2] = {0x5140u, 0x7362u};   // (a.e, b.e, a.e+1, b.e+1), e = 2mt

@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--keys", type=int, default=KEYS)
     ap.add_argument("--e2e-steps", type=int, default=16)
+    ap.add_argument("--chunk-keys", type=int, default=0,
+                    help="keys per decode job (0: the plan's own choice); lets a small capture keep the full run's job size")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-steps", type=int, default=3)
     ap.add_argument("--prefill-layers", type=int, default=LAYERS)
@@ -315,7 +317,7 @@ def main():
     total_steps = args.warmup + args.steps
     Qs = make_q(torch, total_steps, L, device)            # [steps][L][NKV][GQA][HD]
     segs = [pa.Seg(Kall[i].data_ptr(), Vall[i].data_ptr(), nk, i) for i in range(L)]
-    plan = pa.Plan(ctx, shape, L, segs)
+    plan = pa.Plan(ctx, shape, L, segs, chunk_keys=args.chunk_keys)
     packed = torch.empty((rows * (HD + 2),), dtype=torch.float32, device=device)   # this rank's (O, m, l)
     Op, mp, lp = pa.packed_views(packed, rows, HD)
     gathered = torch.empty((world, rows * (HD + 2)), dtype=torch.float32, device=device) if world > 1 else None

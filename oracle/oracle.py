@@ -117,6 +117,10 @@ def quant_q4_0(x: np.ndarray) -> np.ndarray:
 
 
 def quantize(x, quant):
+    """[..., hd] float32 -> stored rows: Q8_0 / Q4_0 blocks, or f16 values (the storage of f16 pages)."""
+    if quant == F16:
+        h = f2h(x)
+        return h.view(np.uint8).reshape(*h.shape[:-1], h.shape[-1] * 2)
     return quant_q8_0(x) if quant == Q8_0 else quant_q4_0(x)
 
 

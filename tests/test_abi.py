@@ -64,18 +64,20 @@ def test_shapes_and_head_bytes():
 
 def test_kernel_head_dim_maps_are_permutations(tmp_path):
     """dK / dV (pa_decode.cuh) decide which head dim each MMA fragment slot carries: compiled as host code they must
-    be permutations of 0..hd-1, dK must keep each lane inside its own quant block(s), and dV inside one block."""
+    be permutations of 0..hd-1, dK must keep each lane inside its own quant block(s), and dV inside one block (f16
+    rows: each k-step / m-tile inside its own 16 dims, the ldmatrix fragment order)."""
     src = tmp_path / "maps.cu"
     src.write_text(r'''
 #include <cstdio>
 #include "pa_decode.cuh"
 int main() {
-  for (int quant = 1; quant <= 2; quant++) for (int hd = 128; hd <= 256; hd += 128) {
+  for (int quant = 0; quant <= 2; quant++) for (int hd = 128; hd <= 256; hd += 128) {
     int seen[256] = {0};
     for (int s = 0; s < hd / 16; s++) for (int t = 0; t < 4; t++) for (int i = 0; i < 4; i++) {
       int d = pa::dec::dK(quant, s, t, i);
       if (d < 0 || d >= hd) { printf("dK out of range\n"); return 1; }
-      if (d / 32 != t + 4 * (s / 8)) { printf("dK leaves the lane's block\n"); return 1; }
+      if (quant && d / 32 != t + 4 * (s / 8)) { printf("dK leaves the lane's block\n"); return 1; }
+      if (!quant && d / 16 != s) { printf("dK (f16) leaves the k-step's 16 dims\n"); return 1; }
       seen[d]++;
     }
     for (int d = 0; d < hd; d++) if (seen[d] != 1) { printf("dK not a permutation q%d hd%d d%d\n", quant, hd, d); return 1; }
@@ -83,7 +85,8 @@ int main() {
     for (int mt = 0; mt < hd / 16; mt++) for (int g = 0; g < 8; g++) for (int h = 0; h < 2; h++) {
       int d = pa::dec::dV(quant, hd, mt, g, h);
       if (d < 0 || d >= hd) { printf("dV out of range\n"); return 1; }
-      if (d / 32 != (hd == 128 ? g / 2 : g)) { printf("dV leaves the lane's block\n"); return 1; }
+      if (quant && d / 32 != (hd == 128 ? g / 2 : g)) { printf("dV leaves the lane's block\n"); return 1; }
+      if (!quant && d / 16 != mt) { printf("dV (f16) leaves the m-tile's 16 dims\n"); return 1; }
       seen2[d]++;
     }
     for (int d = 0; d < hd; d++) if (seen2[d] != 1) { printf("dV not a permutation q%d hd%d d%d\n", quant, hd, d); return 1; }

@@ -27,7 +27,7 @@ def _run(ctx, c, nk=None, segs_split=None):
     import torch
     sh = c["shape"]
     nk = c["K"].shape[0] if nk is None else nk
-    shape = pa.shape_for(sh.hd, sh.nkv, sh.rows, sh.quant)
+    shape = pa.shape_for(sh.hd, sh.nkv, sh.rows, sh.quant, sh.rs)
     K, V = _dev(c["K"]), _dev(c["V"])
     Qs = _dev(c["Qs"].view(np.int16)).view(torch.float16)
     bounds = segs_split or [0, nk]
@@ -63,12 +63,45 @@ CASES = [
     (128, 2, 10, orc.Q8_0, 333),
     (128, 8, 40, orc.Q8_0, 700),
     (128, 8, 16, orc.Q8_0, 64),
+    (128, 8, 5, orc.F16, 4096),                  # f16 pages (store_f16 / is_q8 = 0), ldmatrix fragments
+    (128, 8, 80, orc.F16, 1000),                 # f16 pages with many rows stay on the split-K kernel
+    (256, 4, 48, orc.F16, 2000),                 # pa-tool's wire geometry with f16 pages
+    (128, 2, 10, orc.F16, 333),
+    (256, 4, 6, orc.F16, 77),
 ]
 
 
 @pytest.mark.parametrize("hd,nkv,rows,quant,nk", CASES)
 def test_decode_parity(ctx, hd, nkv, rows, quant, nk):
     c = orc.gen_case(1000 + hd + nkv + rows + nk + quant, hd, nkv, rows, nk, quant)
+    O, m, l = _run(ctx, c)
+    _check(c, O, m, l, nk)
+
+
+def _padded(c, pad):
+    """The same case with `pad` unused bytes after each position's heads (rs > nkv * hb)."""
+    sh = c["shape"]
+    out = dict(c)
+    for key in ("K", "V"):
+        x = c[key]
+        y = np.full((x.shape[0], x.shape[1] + pad), 0xEE, dtype=np.uint8)
+        y[:, :x.shape[1]] = x
+        out[key] = y
+    out["shape"] = orc.shape(sh.hd, sh.nkv, sh.rows, sh.quant, rs=sh.rs + pad)
+    return out
+
+
+@pytest.mark.parametrize("hd,nkv,rows,quant,nk,pad", [
+    (256, 16, 6, orc.Q8_0, 700, 0),      # 16 KV heads at hd 256: two head groups of 8 per position
+    (128, 8, 5, orc.Q8_0, 999, 48),      # padded positions: the head group is not the whole row
+    (128, 8, 5, orc.Q4_0, 300, 16),
+    (128, 8, 5, orc.F16, 517, 32),       # f16: head groups of 4 and a padded row
+])
+def test_head_groups_and_padded_rows(ctx, hd, nkv, rows, quant, nk, pad):
+    """Positions wider than one CTA's head group (or padded) are copied row by row instead of as contiguous pairs."""
+    c = orc.gen_case(2000 + hd + nkv + nk + pad, hd, nkv, rows, nk, quant)
+    if pad:
+        c = _padded(c, pad)
     O, m, l = _run(ctx, c)
     _check(c, O, m, l, nk)
 

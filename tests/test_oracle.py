@@ -81,7 +81,8 @@ def test_live_reference_shim_agrees():
 
 @pytest.mark.parametrize("hd,nkv,rows,quant,nk", [
     (128, 8, 5, orc.Q8_0, 1000), (128, 8, 5, orc.Q4_0, 777), (256, 4, 48, orc.Q8_0, 300),
-    (256, 4, 12, orc.Q4_0, 513), (128, 2, 80, orc.Q8_0, 64), (128, 8, 5, orc.Q8_0, 1)])
+    (256, 4, 12, orc.Q4_0, 513), (128, 2, 80, orc.Q8_0, 64), (128, 8, 5, orc.Q8_0, 1), (128, 8, 5, orc.F16, 600),
+    (256, 4, 48, orc.F16, 129)])
 def test_f32_block_online_matches_f64(hd, nkv, rows, quant, nk):
     c = orc.gen_case(hd * 7 + nk, hd, nkv, rows, nk, quant)
     sh = c["shape"]
@@ -159,10 +160,12 @@ def _free_port():
 
 @pytest.mark.skipif(not os.path.exists(os.path.join(orc.HERE, "_ref", "pa-serve-oracle")),
                     reason="oracle/_ref not built (needs the reference tree)")
-@pytest.mark.parametrize("env", [{}, {"PA_Q4": "1"}, {"PA_NTOK": "1"}, {"PA_BIG_TOK": "16"}])
-def test_reference_pa_tool_gate_passes_on_oracle(env):
+@pytest.mark.parametrize("env,extra", [({}, []), ({"PA_Q4": "1"}, []), ({"PA_NTOK": "1"}, []), ({"PA_BIG_TOK": "16"}, []),
+                                       ({}, ["1", "1", "0", "1024", "1"])])
+def test_reference_pa_tool_gate_passes_on_oracle(env, extra):
     """The reference's own `pa-tool test` (its fp64 check, 5e-3 gate) against the reference's pa::server with the
-    oracle's fp32 path as the engine."""
+    oracle's fp32 path as the engine; the last case has the server keep the rows as f16 pages (store_f16,
+    phone-attn/phone-attn.h:298-319)."""
     port = _free_port()
     srv = subprocess.Popen([os.path.join(orc.HERE, "_ref", "pa-serve-oracle"), str(port), "2"],
                            stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
@@ -170,7 +173,7 @@ def test_reference_pa_tool_gate_passes_on_oracle(env):
         time.sleep(0.3)
         e = dict(os.environ, **env)
         out = subprocess.run([os.path.join(orc.HERE, "_ref", "pa-tool"), "test", "127.0.0.1", str(port), "2048", "2",
-                              "2"], env=e, capture_output=True, text=True, timeout=120)
+                              "2", *extra], env=e, capture_output=True, text=True, timeout=120)
         text = out.stdout + out.stderr
         assert out.returncode == 0, text
         assert "-> PASS" in text and "FAIL" not in text, text

@@ -24,12 +24,18 @@ def _free_port():
     return p
 
 
+# pa-tool test's trailing arguments: SME workers, pack helpers, GPU share (permille), GPU chunk, f16 storage
+# (phone-attn/pa-tool.cpp:107-112); F16 asks the server to keep the q8_0 rows it receives as f16 pages (store_f16)
+F16 = ["1", "1", "0", "1024", "1"]
+
+
 @pytest.mark.skipif(not (os.path.exists(SERVE) and os.path.exists(TOOL)),
                     reason="oracle/_ref binaries not built (they need the reference tree at build time)")
-@pytest.mark.parametrize("env,nkeys", [({}, 16384), ({"PA_Q4": "1"}, 16384), ({"PA_NTOK": "1"}, 16384),
-                                       ({"PA_NTOK": "3"}, 8192), ({"PA_BIG_TOK": "64"}, 8192),
-                                       ({"PA_Q4": "1", "PA_BIG_TOK": "24"}, 4096)])
-def test_reference_pa_tool_against_cuda_engine(env, nkeys):
+@pytest.mark.parametrize("env,nkeys,extra", [({}, 16384, []), ({"PA_Q4": "1"}, 16384, []), ({"PA_NTOK": "1"}, 16384, []),
+                                             ({"PA_NTOK": "3"}, 8192, []), ({"PA_BIG_TOK": "64"}, 8192, []),
+                                             ({"PA_Q4": "1", "PA_BIG_TOK": "24"}, 4096, []), ({}, 8192, F16),
+                                             ({"PA_NTOK": "1", "PA_BIG_TOK": "24"}, 4096, F16)])
+def test_reference_pa_tool_against_cuda_engine(env, nkeys, extra):
     port = _free_port()
     srv = subprocess.Popen([SERVE, str(port), "2"], stdout=subprocess.DEVNULL, stderr=subprocess.PIPE, text=True)
     try:
@@ -44,7 +50,7 @@ def test_reference_pa_tool_against_cuda_engine(env, nkeys):
                 if time.time() > deadline:
                     raise
                 time.sleep(0.2)
-        out = subprocess.run([TOOL, "test", "127.0.0.1", str(port), str(nkeys), "4", "4"], env=dict(os.environ, **env),
+        out = subprocess.run([TOOL, "test", "127.0.0.1", str(port), str(nkeys), "4", "4", *extra], env=dict(os.environ, **env),
                              capture_output=True, text=True, timeout=300)
         text = out.stdout + out.stderr
         assert out.returncode == 0, text
