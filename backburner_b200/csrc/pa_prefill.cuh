@@ -10,12 +10,14 @@
 //   warp 0             TMA: the Q tiles once (128-byte swizzle, the UMMA operand layout), then per 64-key block the
 //                      raw quantised rows of this head (a 16-byte-aligned window of each key row, one 2-D tensor copy
 //                      for K and one for V; keys past the end read as zeros)
-//   warp 1             allocates TMEM; one thread issues the MMAs: S_t = Q_t K^T (M=128, N=64) into a double-buffered
-//                      S in TMEM, then O_t += P_t V (M=128, N=128, B = V read MN-major) into O_t in TMEM
-//   warps 2 .. 2+4NT   one warpgroup per Q tile: thread = query row = TMEM lane. Reads its row of S (64 keys), masks
-//                      tail keys, online softmax in the log2 domain with lazy rescaling (the running max moves only
-//                      when a block's max exceeds it by more than 8, so O in TMEM is rescaled rarely), writes P as f16
-//                      into shared memory in the swizzled operand layout
+//   warp 1             allocates TMEM (per tile: S 64 columns, two P buffers of 32, O 128); one thread issues the MMAs:
+//                      S_t = Q_t K^T (M=128, N=64) into S, then O_t += P_t V (M=128, N=128, A = P read from TMEM, B = V
+//                      read MN-major) into O
+//   warps 4 .. 4+4NT   one warpgroup per Q tile: thread = query row = TMEM lane. Reads its row of S (64 keys; S is
+//                      free again once read), masks tail keys, online softmax in the log2 domain with lazy rescaling (the
+//                      running max moves only when a block's max exceeds it by more than 8, so O in TMEM is rescaled
+//                      rarely), writes P as packed f16 into the block's P buffer: the softmax never waits for a P.V
+//                      except to rescale
 //   last 4 warps       dequantise each raw K and V block into f16 operand tiles (f16(d * q), 128-byte swizzle)
 // All waits are bounded; a wait that runs out records a status, and every role still reaches the final barrier so
 // TMEM is released.
@@ -59,12 +61,20 @@ __device__ __forceinline__ void tc_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
+// (volatile keeps it in order with the mbarrier waits, fences and commits around it, which all are volatile asm; no
+// "memory" clobber, so the compiler need not re-read spilled or cached values around each issue)
 __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc)
-        : "memory");
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(acc));
+}
+// the same with A (M=128 x K=16, 16-bit, two per 32-bit column, row = lane) read from tensor memory
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(acc));
 }
 // 32 consecutive fp32 columns of this warp's 32 TMEM lanes: thread i gets lane (quarter*32 + i)
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
@@ -97,6 +107,17 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 32 consecutive 32-bit columns of this warp's 32 TMEM lanes from packed words (f16x2)
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+        "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+        "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // fp32 pairs (sm_100 .f32x2 arithmetic) and the three-input max
@@ -150,11 +171,10 @@ struct Smem {
     static constexpr int Q = 0;                                   // NT x [2 atom cols][128 rows][128 B]
     static constexpr int K = Q + NT * BM * HD * 2;                 // 2 x [2 atom cols][64 keys][128 B]
     static constexpr int V = K + 2 * BN * HD * 2;                  // 2 x same (read MN-major)
-    static constexpr int P = V + 2 * BN * HD * 2;                  // NT x [128 rows][64 keys] f16
-    static constexpr int RAW = P + NT * BM * BN * 2;               // NS x (K rows, V rows) x [64][RAWB]
+    static constexpr int RAW = V + 2 * BN * HD * 2;                // NS x (K rows, V rows) x [64][RAWB]
     static constexpr int RAW_STAGE = (2 * BN * RAWB + 1023) / 1024 * 1024;
     static constexpr int BAR = RAW + NS * RAW_STAGE;
-    static constexpr int N_BAR = 1 + 2 * NS + 8 + 4 * NT + 2 * NT + 1;
+    static constexpr int N_BAR = 1 + 2 * NS + 8 + 7 * NT + 1;
     static constexpr int TOTAL = BAR + N_BAR * 8 + 32;
 };
 
@@ -177,11 +197,13 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
     uint64_t *q_full = bar;
     uint64_t *raw_full = bar + 1, *raw_empty = raw_full + NS;
     uint64_t *k_full = raw_empty + NS, *k_free = k_full + 2, *v_full = k_free + 2, *v_free = v_full + 2;
-    uint64_t *s_full = v_free + 2;             // [NT][2]
-    uint64_t *s_empty = s_full + 2 * NT;       // [NT][2]
-    uint64_t *p_full = s_empty + 2 * NT;       // [NT]
-    uint64_t *pv_done = p_full + NT;           // [NT]
-    uint64_t *mma_done = pv_done + NT;         // every MMA this CTA issued has completed (before TMEM is freed)
+    uint64_t *s_full = v_free + 2;             // [NT]: S of the block in TMEM
+    uint64_t *s_empty = s_full + NT;           // [NT]: the softmax has read S into registers
+    uint64_t *p_full = s_empty + NT;           // [NT][2]: P of the block in P buffer j & 1 (one barrier per buffer, so
+                                               // the softmax finishing block j+1 cannot complete block j's phase)
+    uint64_t *pv_free = p_full + 2 * NT;       // [NT][2]: P.V of a block with P buffer b completed
+    uint64_t *o_ready = pv_free + 2 * NT;      // [NT]: the last P.V completed (once)
+    uint64_t *mma_done = o_ready + NT;         // every MMA this CTA issued has completed (before TMEM is freed)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + L::N_BAR);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -203,11 +225,15 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
             mbar_init(&k_full[b], 4); mbar_init(&k_free[b], 1); mbar_init(&v_full[b], 4); mbar_init(&v_free[b], 1);
         }
         for (int t = 0; t < NT; t++) {
-            for (int b = 0; b < 2; b++) { mbar_init(&s_full[2 * t + b], 1); mbar_init(&s_empty[2 * t + b], 4); }
-            mbar_init(&p_full[t], 4);
-            mbar_init(&pv_done[t], 1);
+            mbar_init(&s_full[t], 1);
+            mbar_init(&s_empty[t], 4);
+            mbar_init(&p_full[2 * t], 4);
+            mbar_init(&p_full[2 * t + 1], 4);
+            mbar_init(&pv_free[2 * t], 1);
+            mbar_init(&pv_free[2 * t + 1], 1);
+            mbar_init(&o_ready[t], 1);
         }
-        mbar_init(mma_done, 1);
+        mbar_init(mma_done, 2);
         // a CTA started after another one gave up a wait does no work (a systematic failure ends in one timeout)
         *abort_flag = *(volatile int *) p.status != ST_OK;
         fence_mbar_init();
@@ -225,7 +251,8 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     // NT == 2: 16 warps launched with 128 registers each; every warpgroup's branch starts by resizing its share:
-    // control 56, softmax 2 x 168, dequant 120 (128 x (56 + 168 + 168 + 120) = 65,536 = the launched total)
+    // control 88 (the MMA issuer keeps its operand descriptors in registers), softmax 2 x 160, dequant 104
+    // (128 x (88 + 160 + 160 + 104) = 65,536 = the launched total)
 
     auto wait = [&](uint64_t *b, uint32_t parity) -> bool {
         if (!ok) return false;
@@ -238,7 +265,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
     };
 
     if (warp < 4) {
-      if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+      if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 88;");
       if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
@@ -268,80 +295,90 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
                         atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
             }
         }
-      } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            uint32_t issued_pv = 0;
-            auto issue_pv = [&](uint32_t jj) {
-                const uint32_t b = jj & 1;
-                if (!wait(&v_full[b], (jj >> 1) & 1)) return;
-                for (int t = 0; t < NT; t++) {
-                    if (!wait(&p_full[t], jj & 1)) return;
-                    tc_fence_after();
-                    const uint32_t d = tmem + t * 256 + 128;
-                    const uint32_t pa = sbase + L::P + t * BM * BN * 2, va = sbase + L::V + b * BN * HD * 2;
-#pragma unroll
-                    for (int ks = 0; ks < BN / 16; ks++)
-                        tc_mma(d, sdesc(pa + ks * 32, 16, 1024), sdesc(va + ks * 2048, BN * 128, 1024), IDESC_PV,
-                               (jj > 0 || ks > 0) ? 1u : 0u);
-                    tc_commit(&pv_done[t]);
-                }
-                tc_commit(&v_free[b]);
-                issued_pv = jj + 1;
-            };
+      } else if (warp == 1 || warp == 2) {
+        // ------------------------------------------------ MMA issuers: warp 1 the S = Q K^T MMAs, warp 2 the P.V ones.
+        // Two issuing threads (on two SM sub-partitions) keep the issue of one kind from waiting behind the other;
+        // each commit tracks its own thread's MMAs, and the softmax orders the two through s_full / p_full / pv_free.
+        // Operand descriptors are built once: their high word (LBO, SBO, version, swizzle) is fixed per operand and an
+        // operand's start address advances by adding (byte offset >> 4) to the 14-bit start field (every address
+        // stays below 256 KB, so the field cannot carry).
+        if (lane == 0 && warp == 1) {
+            const uint64_t dq0 = sdesc(sbase + L::Q, 16, 1024), dk0 = sdesc(sbase + L::K, 16, 1024);
             if (wait(q_full, 0)) {
                 for (uint32_t j = 0; j < nblk && ok; j++) {
                     const uint32_t b = j & 1;
                     if (!wait(&k_full[b], (j >> 1) & 1)) break;
-                    for (int t = 0; t < NT && ok; t++) {
-                        if (j >= 2 && !wait(&s_empty[2 * t + b], ((j - 2) >> 1) & 1)) break;
+                    const uint64_t dk = dk0 + b * (uint32_t) (BN * HD * 2 / 16);
+#pragma unroll
+                    for (int t = 0; t < NT; t++) {
+                        if (j >= 1 && !wait(&s_empty[t], (j - 1) & 1)) break;
                         tc_fence_after();
-                        const uint32_t d = tmem + t * 256 + b * BN;
-                        const uint32_t qa = sbase + L::Q + t * BM * HD * 2, ka = sbase + L::K + b * BN * HD * 2;
+                        const uint32_t d = tmem + t * 256;
+                        const uint64_t dq = dq0 + (uint32_t) (t * BM * HD * 2 / 16);
 #pragma unroll
                         for (int kk = 0; kk < HD / 16; kk++)
-                            tc_mma(d, sdesc(qa + (kk / 4) * BM * 128 + (kk % 4) * 32, 16, 1024),
-                                   sdesc(ka + (kk / 4) * BN * 128 + (kk % 4) * 32, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
-                        tc_commit(&s_full[2 * t + b]);
+                            tc_mma(d, dq + (uint32_t) (((kk / 4) * BM * 128 + (kk % 4) * 32) / 16),
+                                   dk + (uint32_t) (((kk / 4) * BN * 128 + (kk % 4) * 32) / 16), IDESC_S, kk > 0 ? 1u : 0u);
+                        tc_commit(&s_full[t]);
                     }
                     if (!ok) break;
                     tc_commit(&k_free[b]);
-                    if (j >= 1) issue_pv(j - 1);
                 }
-                if (ok && nblk > 0) issue_pv(nblk - 1);
             }
-            (void) issued_pv;
-            // TMEM must not be released under MMAs still running (they complete on their own; bounded wait)
+        } else if (lane == 0) {
+            const uint64_t dv0 = sdesc(sbase + L::V, BN * 128, 1024);
+            for (uint32_t jj = 0; jj < nblk && ok; jj++) {
+                const uint32_t b = jj & 1;
+                if (!wait(&v_full[b], (jj >> 1) & 1)) break;
+                const uint64_t dv = dv0 + b * (uint32_t) (BN * HD * 2 / 16);
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    if (!wait(&p_full[2 * t + b], (jj >> 1) & 1)) break;
+                    tc_fence_after();
+                    const uint32_t d = tmem + t * 256 + 128;
+                    const uint32_t pa = tmem + t * 256 + BN + b * (BN / 2);   // P buffer b (f16, two keys per column)
+#pragma unroll
+                    for (int ks = 0; ks < BN / 16; ks++)
+                        tc_mma_ts(d, pa + ks * 8, dv + (uint32_t) (ks * 2048 / 16), IDESC_PV, (jj > 0 || ks > 0) ? 1u : 0u);
+                    tc_commit(&pv_free[2 * t + b]);   // P buffer b and O (through this block) are settled
+                    if (jj + 1 == nblk) tc_commit(&o_ready[t]);
+                }
+                if (!ok) break;
+                tc_commit(&v_free[b]);
+            }
+        }
+        if (lane == 0) {
+            // TMEM must not be released under MMAs still running (they complete on their own; bounded wait): both
+            // issuers commit to mma_done (count 2) and wait for both
             tc_commit(mma_done);
             const uint64_t drain = tmo > dec::DRAIN_NS ? tmo : dec::DRAIN_NS;
             if (!mbar_wait_bounded(mma_done, 0, drain, nullptr)) atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
         }
-      }   // warps 2 and 3: idle
+      }   // warp 3: idle
     } else if (warp < (uint32_t) DQ0) {
         // ------------------------------------------------ softmax warpgroup of tile t
-        if (NT == 2) asm volatile("setmaxnreg.inc.sync.aligned.u32 168;");
+        if (NT == 2) asm volatile("setmaxnreg.inc.sync.aligned.u32 160;");
         const int t = (int) (warp - SM0) / 4;
         const uint32_t wq = warp % 4;                      // TMEM lane quarter of this warp
         const uint32_t r = wq * 32 + lane;                 // row of the tile = TMEM lane
         const uint32_t tl = tmem + ((wq * 32) << 16) + t * 256;
-        const uint32_t prow = sbase + L::P + t * BM * BN * 2 + (r / 8) * 1024 + (r % 8) * 128;
         float m_used = -INFINITY, l = 0.f;
         for (uint32_t j = 0; j < nblk; j++) {
             const uint32_t b = j & 1;
-            if (!wait(&s_full[2 * t + b], (j >> 1) & 1)) break;
+            if (!wait(&s_full[t], j & 1)) break;
             tc_fence_after();
             float s[64];
             {
                 float a[32], c[32];
-                tmem_ld32(tl + b * BN, a);
-                tmem_ld32(tl + b * BN + 32, c);
+                tmem_ld32(tl, a);
+                tmem_ld32(tl + 32, c);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; i++) { s[i] = a[i]; s[32 + i] = c[i]; }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[2 * t + b]);
+            if (lane == 0) mbar_arrive(&s_empty[t]);
             const int nvalid = (int) (job.nk - j * BN);
             if (nvalid < BN) {
 #pragma unroll
@@ -378,9 +415,11 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
             unpack_f2(acc, sa, sb);
             const float sum = sa + sb;
             l = fmaf(l, alpha, sum);
-            // P buffer and O are free once the previous block's P.V has completed
-            if (j >= 1 && !wait(&pv_done[t], (j - 1) & 1)) break;
+            // O is rescaled (rarely: the lazy max moved) once P.V of block j-1 has completed; P buffer b is free once
+            // P.V of block j-2 (its last reader) has. Each buffer's barrier completes once per P.V on that buffer, and
+            // P.V of block j cannot start before this P is written, so each wait names exactly one completion.
             if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
+                if (!wait(&pv_free[2 * t + (b ^ 1)], ((j - 1) >> 1) & 1)) break;
                 tc_fence_after();
 #pragma unroll
                 for (int q = 0; q < HD / 32; q++) {
@@ -393,16 +432,15 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
                 }
                 tmem_wait_st();
             }
-#pragma unroll
-            for (int c = 0; c < BN / 8; c++)
-                sts128(prow + ((c ^ (r % 8)) * 16), ph[4 * c], ph[4 * c + 1], ph[4 * c + 2], ph[4 * c + 3]);
-            fence_proxy_async();
+            if (j >= 2 && !wait(&pv_free[2 * t + b], ((j - 2) >> 1) & 1)) break;
+            tmem_st32u(tl + BN + b * (BN / 2), ph);   // P, two keys per column, into P buffer b
+            tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[t]);
+            if (lane == 0) mbar_arrive(&p_full[2 * t + b]);
         }
         // final: O (unnormalised, relative to m_used) from TMEM to the slot partial
-        if (ok && nblk > 0 && wait(&pv_done[t], (nblk - 1) & 1)) {
+        if (ok && nblk > 0 && wait(&o_ready[t], 0)) {
             tc_fence_after();
             const uint32_t row = row0 + t * BM + r;
             const uint64_t orow = ((uint64_t) job.slot * p.nkv + h) * p.rows + row;
@@ -424,7 +462,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
         }
     } else {
         // ------------------------------------------------ dequantisers: warp dw owns quant block dw of every key
-        if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 120;");
+        if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 104;");
         const uint32_t dw = warp - DQ0;
         const uint32_t bo = hoff + GB * dw;                 // block start inside the raw window row
         const uint32_t w16 = bo & ~15u;                     // 16-byte aligned start of the words covering it
