@@ -78,6 +78,9 @@ _SIGS = {
                                      ctypes.POINTER(_Shape), ctypes.c_int, ctypes.c_int]),
     "pa_cuda_end": (ctypes.c_double, [_P, _P, _P, _P]),
     "pa_cuda_exec_ms": (ctypes.c_double, [_P]),
+    "pa_cuda_arm": (ctypes.c_int, [_P, _P, ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, ctypes.POINTER(_Shape),
+                                   ctypes.c_int]),
+    "pa_cuda_graph_calls": (ctypes.c_uint64, [_P]),
     "pa_cuda_attn_noalloc": (ctypes.c_int, [ctypes.POINTER(_Shape), _P, _P, _P, ctypes.c_uint32, _P, _P, _P, _P,
                                             ctypes.POINTER(ctypes.c_char_p)]),
 }
@@ -388,6 +391,18 @@ class Engine:
             msg = lib().pa_cuda_last_error(self.ctx.handle).decode(errors="replace")
             raise PaCudaError(ETIMEOUT, f"end: {msg}")
         return ms
+
+    def arm(self, pages: Sequence[_Page], nkeys: Sequence[int], shape: Shape, ntok: int = 8):
+        """engine::arm: prepare the likely next one-group call (its plan and a CUDA graph of the whole call)."""
+        arr = (_Page * max(1, len(pages)))(*pages)
+        nk = (ctypes.c_uint32 * max(1, len(nkeys)))(*nkeys)
+        sh = shape.c()
+        self.ctx.check(lib().pa_cuda_arm(self.ctx.handle, arr, nk, len(pages), ctypes.byref(sh), ntok), "arm")
+
+    @property
+    def graph_calls(self) -> int:
+        """begin calls served by an armed graph"""
+        return int(lib().pa_cuda_graph_calls(self.ctx.handle))
 
     @property
     def exec_ms(self) -> float:

@@ -27,6 +27,18 @@ constexpr uint32_t kPrefillMinRows = 64;   // query rows per KV head from which 
 
 struct Plan;
 
+// pa::engine calls: plans are kept per call shape (a layer's pages, its key counts, the geometry), so the per-layer
+// calls of a decode step reuse their job lists and partial buffers instead of allocating them every call; a plan
+// armed for the next call (pa_cuda_arm) also holds a CUDA graph of the whole call.
+constexpr size_t kEngCache = 256;
+struct EngEntry {
+    std::vector<uint64_t> key;           // geometry, groups, packed tokens, then (k, v, nkeys) per page
+    pa_cuda_plan *plan = nullptr;
+    cudaGraphExec_t graph = nullptr;     // Q upload, kernels, result readback (captured by pa_cuda_arm)
+    uint64_t graph_launches = 0;         // kernel launches one replay makes
+    uint64_t used = 0;                   // LRU tick
+};
+
 }  // namespace
 
 struct pa_cuda_ctx {
@@ -40,7 +52,9 @@ struct pa_cuda_ctx {
     int kernel_choice = 0;   // 0 auto, 1 split-K mma.sync kernel, 2 tcgen05 kernel
     std::string err;
     // pa::engine state (begin/end)
-    pa_cuda_plan *eng_plan = nullptr;
+    pa_cuda_plan *eng_plan = nullptr;      // the current call's plan (owned by eng_cache)
+    std::vector<EngEntry> eng_cache;
+    uint64_t eng_tick = 0, eng_graph_calls = 0;
     std::vector<pa_cuda_seg> eng_segs;
     uint16_t *h_q = nullptr;      // pinned staging
     float *h_out = nullptr;       // pinned staging: O, then m, then l
@@ -378,7 +392,10 @@ void pa_cuda_destroy(pa_cuda_ctx *ctx) {
     if (!ctx) return;
     cudaSetDevice(ctx->device);
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
-    if (ctx->eng_plan) pa_cuda_plan_destroy(ctx->eng_plan);
+    for (auto &e : ctx->eng_cache) {
+        if (e.graph) cudaGraphExecDestroy(e.graph);
+        if (e.plan) pa_cuda_plan_destroy(e.plan);
+    }
     if (ctx->h_q) cudaFreeHost(ctx->h_q);
     if (ctx->h_out) cudaFreeHost(ctx->h_out);
     if (ctx->d_q) cudaFree(ctx->d_q);
@@ -760,35 +777,111 @@ void pa_cuda_free_page(pa_cuda_ctx *ctx, pa_cuda_page *pg) {
     pg->hk = pg->hv = nullptr;
 }
 
-int pa_cuda_begin(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *nkeys, int n_pages,
-                  const uint16_t *Qs_host, const pa_cuda_shape *shape, int ng, int ntok) {
-    if (!ctx) return PA_CUDA_EINVAL;
-    if (ctx->eng_active) return fail(ctx, PA_CUDA_EINVAL, "begin while a call is in flight (call end first)");
-    if (ng < 1 || n_pages < 0 || (n_pages && (!pages || !nkeys)) || !Qs_host)
+}  // extern "C"
+
+namespace {
+
+// One engine call's plan from the cache (created on a miss, the least recently used one evicted past kEngCache), with
+// the staging buffers sized for it. Cached graphs capture the staging buffers' addresses: a reallocation drops them.
+int eng_prepare(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *nkeys, int n_pages, const pa_cuda_shape *shape,
+                int ng, int ntok, pa_cuda_shape &sh, int &nt, EngEntry *&entry) {
+    if (ng < 1 || n_pages < 0 || (n_pages && (!pages || !nkeys)) || !shape)
         return fail(ctx, PA_CUDA_EINVAL, "bad begin arguments");
     cudaSetDevice(ctx->device);
     const int NR = 48;
-    pa_cuda_shape sh = *shape;
-    const int nt = (ng == 1 && ntok >= 1 && ntok < 8) ? ntok : 0;   // packed real rows (pa-metal.mm:627-646)
+    sh = *shape;
+    nt = (ng == 1 && ntok >= 1 && ntok < 8) ? ntok : 0;   // packed real rows (pa-metal.mm:627-646)
     sh.rows = nt ? 6u * (uint32_t) nt : (uint32_t) NR;
     int rc = check_shape(ctx, &sh);
     if (rc) return rc;
-    const uint32_t nkv = sh.nkv, hd = sh.hd;
-    // one output set per group
-    ctx->eng_segs.clear();
-    for (int g = 0; g < ng; g++)
-        for (int i = 0; i < n_pages; i++)
-            if (nkeys[i]) ctx->eng_segs.push_back(pa_cuda_seg{pages[i].k, pages[i].v, nkeys[i], (uint32_t) g});
-    if (ctx->eng_plan) { pa_cuda_plan_destroy(ctx->eng_plan); ctx->eng_plan = nullptr; }
-    if ((rc = pa_cuda_plan_create(ctx, &sh, (uint32_t) ng, ctx->eng_segs.data(), (uint32_t) ctx->eng_segs.size(), 0,
-                                  &ctx->eng_plan)))
-        return rc;
-    const size_t rows = (size_t) ng * nkv * sh.rows;
-    const size_t qb = rows * hd * 2, ob = rows * hd * 4, mb = rows * 4;
+    std::vector<uint64_t> key = {sh.hd, sh.nkv, sh.rows, sh.quant, sh.rs, sh.hb, (uint64_t) ng, (uint64_t) nt,
+                                 (uint64_t) n_pages};
+    for (int i = 0; i < n_pages; i++) {
+        key.push_back((uint64_t) (uintptr_t) pages[i].k);
+        key.push_back((uint64_t) (uintptr_t) pages[i].v);
+        key.push_back(nkeys[i]);
+    }
+    entry = nullptr;
+    for (auto &e : ctx->eng_cache)
+        if (e.key == key) { entry = &e; break; }
+    if (!entry) {
+        if (ctx->eng_cache.size() >= kEngCache) {   // evict the least recently used entry
+            auto lru = std::min_element(ctx->eng_cache.begin(), ctx->eng_cache.end(),
+                                        [](const EngEntry &a, const EngEntry &b) { return a.used < b.used; });
+            cudaStreamSynchronize(ctx->stream);
+            if (lru->graph) cudaGraphExecDestroy(lru->graph);
+            if (lru->plan) pa_cuda_plan_destroy(lru->plan);
+            ctx->eng_cache.erase(lru);
+        }
+        std::vector<pa_cuda_seg> segs;
+        for (int g = 0; g < ng; g++)
+            for (int i = 0; i < n_pages; i++)
+                if (nkeys[i]) segs.push_back(pa_cuda_seg{pages[i].k, pages[i].v, nkeys[i], (uint32_t) g});
+        pa_cuda_plan *plan = nullptr;
+        if ((rc = pa_cuda_plan_create(ctx, &sh, (uint32_t) ng, segs.data(), (uint32_t) segs.size(), 0, &plan))) return rc;
+        ctx->eng_cache.push_back(EngEntry{});
+        entry = &ctx->eng_cache.back();
+        entry->key = std::move(key);
+        entry->plan = plan;
+    }
+    entry->used = ++ctx->eng_tick;
+    const size_t rows = (size_t) ng * sh.nkv * sh.rows;
+    const size_t qb = rows * sh.hd * 2, ob = rows * sh.hd * 4, mb = rows * 4;
+    const void *before[4] = {ctx->h_q, ctx->h_out, ctx->d_q, ctx->d_out};
     if ((rc = ensure_host(ctx, ctx->h_q, ctx->h_q_bytes, qb))) return rc;
     if ((rc = ensure_host(ctx, ctx->h_out, ctx->h_out_bytes, ob + 2 * mb))) return rc;
     if ((rc = ensure_dev(ctx, ctx->d_q, ctx->d_q_bytes, qb))) return rc;
     if ((rc = ensure_dev(ctx, ctx->d_out, ctx->d_out_bytes, ob + 2 * mb))) return rc;
+    if (before[0] != ctx->h_q || before[1] != ctx->h_out || before[2] != ctx->d_q || before[3] != ctx->d_out)
+        for (auto &e : ctx->eng_cache)
+            if (e.graph) { cudaGraphExecDestroy(e.graph); e.graph = nullptr; }
+    return PA_CUDA_OK;
+}
+
+// stream-ordered migration of managed pages the host may have written since the last call
+void eng_prefetch(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *nkeys, int n_pages, uint64_t rs) {
+    for (int i = 0; i < n_pages; i++) {
+#if CUDART_VERSION >= 13000
+        cudaMemLocation loc{cudaMemLocationTypeDevice, ctx->device};
+        cudaMemPrefetchAsync(pages[i].k, (size_t) nkeys[i] * rs, loc, 0, ctx->stream);
+        cudaMemPrefetchAsync(pages[i].v, (size_t) nkeys[i] * rs, loc, 0, ctx->stream);
+#else
+        cudaMemPrefetchAsync(pages[i].k, (size_t) nkeys[i] * rs, ctx->device, ctx->stream);
+        cudaMemPrefetchAsync(pages[i].v, (size_t) nkeys[i] * rs, ctx->device, ctx->stream);
+#endif
+    }
+    cudaGetLastError();
+}
+
+// the device part of one engine call: Q up, the plan's kernels, (O, m, l) back
+int eng_enqueue(pa_cuda_ctx *ctx, pa_cuda_plan *plan, const pa_cuda_shape &sh, int ng) {
+    const size_t rows = (size_t) ng * sh.nkv * sh.rows;
+    const size_t qb = rows * sh.hd * 2, ob = rows * sh.hd * 4, mb = rows * 4;
+    PA_CK(cudaMemcpyAsync(ctx->d_q, ctx->h_q, qb, cudaMemcpyHostToDevice, ctx->stream), "Q to device");
+    float *dO = ctx->d_out, *dm = (float *) ((char *) ctx->d_out + ob), *dl = dm + rows;
+    int rc = run_plan(plan, ctx->d_q, dO, dm, dl, ctx->stream);
+    if (rc) return rc;
+    PA_CK(cudaMemcpyAsync(ctx->h_out, ctx->d_out, ob + 2 * mb, cudaMemcpyDeviceToHost, ctx->stream), "O to host");
+    return PA_CUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int pa_cuda_begin(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *nkeys, int n_pages,
+                  const uint16_t *Qs_host, const pa_cuda_shape *shape, int ng, int ntok) {
+    if (!ctx) return PA_CUDA_EINVAL;
+    if (ctx->eng_active) return fail(ctx, PA_CUDA_EINVAL, "begin while a call is in flight (call end first)");
+    if (!Qs_host) return fail(ctx, PA_CUDA_EINVAL, "bad begin arguments");
+    pa_cuda_shape sh;
+    int nt = 0;
+    EngEntry *entry = nullptr;
+    int rc = eng_prepare(ctx, pages, nkeys, n_pages, shape, ng, ntok, sh, nt, entry);
+    if (rc) return rc;
+    ctx->eng_plan = entry->plan;
+    const int NR = 48;
+    const uint32_t nkv = sh.nkv, hd = sh.hd;
     // pack Q: wire row r = g*8 + t of head h; packed (nt) row = g*nt + t
     for (int gi = 0; gi < ng; gi++)
         for (uint32_t h = 0; h < nkv; h++) {
@@ -798,24 +891,16 @@ int pa_cuda_begin(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *n
             else
                 for (int gg = 0; gg < 6; gg++) memcpy(dst + (size_t) gg * nt * hd, src + (size_t) gg * 8 * hd, (size_t) nt * hd * 2);
         }
-    for (int i = 0; i < n_pages; i++) {
-        // stream-ordered migration of pages the host wrote since the last call
-#if CUDART_VERSION >= 13000
-        cudaMemLocation loc{cudaMemLocationTypeDevice, ctx->device};
-        cudaMemPrefetchAsync(pages[i].k, (size_t) nkeys[i] * sh.rs, loc, 0, ctx->stream);
-        cudaMemPrefetchAsync(pages[i].v, (size_t) nkeys[i] * sh.rs, loc, 0, ctx->stream);
-#else
-        cudaMemPrefetchAsync(pages[i].k, (size_t) nkeys[i] * sh.rs, ctx->device, ctx->stream);
-        cudaMemPrefetchAsync(pages[i].v, (size_t) nkeys[i] * sh.rs, ctx->device, ctx->stream);
-#endif
-    }
-    cudaGetLastError();
+    eng_prefetch(ctx, pages, nkeys, n_pages, sh.rs);
     ctx->t_begin = std::chrono::steady_clock::now();
     PA_CK(cudaEventRecord(ctx->ev_begin, ctx->stream), "event");
-    PA_CK(cudaMemcpyAsync(ctx->d_q, ctx->h_q, qb, cudaMemcpyHostToDevice, ctx->stream), "Q to device");
-    float *dO = ctx->d_out, *dm = (float *) ((char *) ctx->d_out + ob), *dl = dm + rows;
-    if ((rc = run_plan(ctx->eng_plan, ctx->d_q, dO, dm, dl, ctx->stream))) return rc;
-    PA_CK(cudaMemcpyAsync(ctx->h_out, ctx->d_out, ob + 2 * mb, cudaMemcpyDeviceToHost, ctx->stream), "O to host");
+    if (entry->graph && !entry->plan->profile) {   // armed: one graph launch replays the whole call
+        PA_CK(cudaGraphLaunch(entry->graph, ctx->stream), "graph launch");
+        ctx->launches += entry->graph_launches;
+        ctx->eng_graph_calls++;
+    } else if ((rc = eng_enqueue(ctx, entry->plan, sh, ng))) {
+        return rc;
+    }
     PA_CK(cudaEventRecord(ctx->ev_end, ctx->stream), "event");
     ctx->eng_ng = ng;
     ctx->eng_nt = nt;
@@ -825,6 +910,44 @@ int pa_cuda_begin(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *n
     ctx->eng_active = true;
     return PA_CUDA_OK;
 }
+
+int pa_cuda_arm(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *nkeys, int n_pages,
+                const pa_cuda_shape *shape, int ntok) {
+    if (!ctx) return PA_CUDA_EINVAL;
+    if (ctx->eng_active) return fail(ctx, PA_CUDA_EINVAL, "arm while a call is in flight (call end first)");
+    pa_cuda_shape sh;
+    int nt = 0;
+    EngEntry *entry = nullptr;
+    int rc = eng_prepare(ctx, pages, nkeys, n_pages, shape, 1, ntok, sh, nt, entry);
+    if (rc) return rc;
+    eng_prefetch(ctx, pages, nkeys, n_pages, sh.rs);
+    if (entry->graph) return PA_CUDA_OK;
+    // capture the call on the context's stream (nothing of this thread is in flight on it between end and begin)
+    const uint64_t launches0 = ctx->launches;
+    cudaGraph_t g = nullptr;
+    PA_CK(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    rc = eng_enqueue(ctx, entry->plan, sh, 1);
+    const cudaError_t ec = cudaStreamEndCapture(ctx->stream, &g);
+    const uint64_t per_run = ctx->launches - launches0;
+    ctx->launches = launches0;   // captured, not run
+    if (rc || ec != cudaSuccess || !g) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        return rc ? rc : cuda_fail(ctx, ec, "capture of the armed call");
+    }
+    cudaGraphExec_t ex = nullptr;
+    const cudaError_t ei = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (ei != cudaSuccess) {
+        cudaGetLastError();
+        return cuda_fail(ctx, ei, "instantiating the armed call");
+    }
+    entry->graph = ex;
+    entry->graph_launches = per_run;
+    return PA_CUDA_OK;
+}
+
+uint64_t pa_cuda_graph_calls(const pa_cuda_ctx *ctx) { return ctx ? ctx->eng_graph_calls : 0; }
 
 double pa_cuda_end(pa_cuda_ctx *ctx, float *O, float *m, float *l) {
     if (!ctx || !ctx->eng_active) return -1;

@@ -21,6 +21,7 @@
 //                          rows as received, or f16 rows (is_q8 == 0, store_f16), all on the split-K kernel; the
 //                          tcgen05 kernel takes quantised rows with hd 128 only.
 #pragma once
+#include <cstdlib>
 #include <string>
 #include <vector>
 
@@ -68,17 +69,29 @@ public:
         return ms;
     }
     double exec_ms() const override { return pa_cuda_exec_ms(ctx_); }
+    // the server's hint that the next call is this one (phone-attn/phone-attn.h:686-697): its plan and a CUDA graph of
+    // the whole call are prepared now, off the next call's critical path (PA_CUDA_ARM=0 turns it off)
+    void arm(const page * pages, const uint32_t * nkeys, int n_pages, const config_req & cfg, int ntok) override {
+        static const bool on = !getenv("PA_CUDA_ARM") || atoi(getenv("PA_CUDA_ARM")) != 0;
+        if (!on || n_pages <= 0) return;
+        std::vector<pa_cuda_page> cp((size_t) n_pages);
+        for (int i = 0; i < n_pages; i++) cp[(size_t) i] = pa_cuda_page{pages[i].k, pages[i].v, pages[i].hk, pages[i].hv};
+        const pa_cuda_shape sh{(uint32_t) HD, cfg.n_head_kv, (uint32_t) NR, cfg.is_q8, cfg.rs, cfg.hb};
+        if (pa_cuda_arm(ctx_, cp.data(), nkeys, n_pages, &sh, ntok) == PA_CUDA_OK) armed_++;
+    }
     std::string describe() override {
-        char b[160];
-        snprintf(b, sizeof b, "engine=pa-cuda calls=%llu last_gpu_exec_ms=%.3f launches=%llu", (unsigned long long) calls_,
-                 pa_cuda_exec_ms(ctx_), (unsigned long long) pa_cuda_launch_count(ctx_));
+        char b[224];
+        snprintf(b, sizeof b, "engine=pa-cuda calls=%llu armed=%llu graph_calls=%llu last_gpu_exec_ms=%.3f launches=%llu",
+                 (unsigned long long) calls_, (unsigned long long) armed_,
+                 (unsigned long long) pa_cuda_graph_calls(ctx_), pa_cuda_exec_ms(ctx_),
+                 (unsigned long long) pa_cuda_launch_count(ctx_));
         return b;
     }
 
 private:
     pa_cuda_ctx * ctx_ = nullptr;
     int ng_ = 1, rows_ = 0;
-    unsigned long long calls_ = 0;
+    unsigned long long calls_ = 0, armed_ = 0;
 };
 
 }  // namespace pa

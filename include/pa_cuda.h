@@ -17,6 +17,7 @@
  *   pa_cuda_free_page,
  *   pa_cuda_begin,
  *   pa_cuda_end            pa::engine                     phone-attn/phone-attn.h:166-183 (pa-metal.mm:804-953)
+ *   pa_cuda_arm            engine::arm (pre-armed call)   phone-attn/phone-attn.h:179-182, pa-metal.mm:716-765
  *
  * Data layout (the reference's, unchanged):
  *   K/V rows: key position j, KV head h at base + j*rs + h*hb; Q8_0 head = hd/32 blocks of (f16 d, 32 x int8),
@@ -162,6 +163,16 @@ int pa_cuda_begin(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *n
 double pa_cuda_end(pa_cuda_ctx *ctx, float *O, float *m, float *l);
 /* GPU execution time of the last completed begin/end call (CUDA events), ms */
 double pa_cuda_exec_ms(const pa_cuda_ctx *ctx);
+/* engine::arm (phone-attn/phone-attn.h:179-182): the next one-group call will likely be this one (the next layer, same
+ * split and tokens). Prepares it: the call's plan (kept per call shape, as every begin keeps its own) and a CUDA graph
+ * of the whole call (Q upload, kernels, readback). The graph stays with the cached plan: every later begin with the
+ * same pages, key counts, geometry and ntok packs Q and launches it; any other begin runs as usual (pa-metal.mm:716-765
+ * encodes and parks a one-shot command buffer instead). Call between end and the next begin, from the thread that calls
+ * begin. Advisory: an error leaves begin unaffected. */
+int pa_cuda_arm(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *nkeys, int n_pages, const pa_cuda_shape *shape,
+                int ntok);
+/* number of begin calls served by an armed graph */
+uint64_t pa_cuda_graph_calls(const pa_cuda_ctx *ctx);
 
 /* ---- allocation-free call (no counterpart in the reference: an addition of this library)
  * For callers that cannot allocate device memory: a host runtime that owns every device allocation itself (a fixed

@@ -264,6 +264,66 @@ def test_engine_pages_begin_end(ctx, quant, ntok, ng):
         eng.free_page(pg)
 
 
+@pytest.mark.parametrize("ntok", [1, 8])
+def test_engine_arm_replays_the_call_as_a_graph(ctx, ntok):
+    """engine::arm (phone-attn/phone-attn.h:179-182): after arm(), a begin with the same pages, key counts and tokens
+    replays a CUDA graph of the whole call and returns exactly what the plain path returned; the graph stays with the
+    call's cached plan, so later calls of that shape replay it too, each reading its own Q; a call of another shape runs
+    the plain path."""
+    hd, nkv, NR, PAGE, quant = 256, 4, 48, 4096, orc.Q8_0
+    nk = 9000
+    c = orc.gen_case(71 + ntok, hd, nkv, NR, nk, quant)
+    c2 = orc.gen_case(72 + ntok, hd, nkv, NR, nk, quant)
+    def wire(cc):
+        q = cc["Qs"].reshape(nkv, 1, NR, hd).transpose(1, 0, 2, 3).copy()
+        q[:, :, (np.arange(NR) % 8) >= ntok, :] = 0
+        return q
+    Qa, Qb = wire(c), wire(c2)
+    shape = pa.shape_for(hd, nkv, NR, quant)
+    sh = orc.shape(hd, nkv, NR, quant)
+    real = (np.arange(NR) % 8) < ntok
+    eng = pa.Engine(ctx)
+    pages, nkeys = [], []
+    for p0 in range(0, nk, PAGE):
+        n = min(PAGE, nk - p0)
+        pg = eng.alloc_page(PAGE * shape.rs)
+        eng.page_view(pg, n * shape.rs, "k")[:] = c["K"][p0:p0 + n].ravel()
+        eng.page_view(pg, n * shape.rs, "v")[:] = c["V"][p0:p0 + n].ravel()
+        pages.append(pg)
+        nkeys.append(n)
+    out = lambda: (np.empty((1, nkv * NR, hd), np.float32), np.empty((1, nkv * NR), np.float32),
+                   np.empty((1, nkv * NR), np.float32))
+    def check(res, Q, n):
+        Of, mf, lf = orc.partial_f64(sh, Q[0].reshape(nkv, NR, hd), c["K"][:n], c["V"][:n], n)
+        O, m, l = res
+        e = orc.rel_err(O[0].reshape(nkv, NR, hd)[:, real], m[0].reshape(nkv, NR)[:, real], l[0].reshape(nkv, NR)[:, real],
+                        Of[:, real], mf[:, real], lf[:, real])
+        assert e[0] <= TOL_F64 and e[1] <= TOL_F64, e
+    g0 = eng.graph_calls
+    r1 = out()
+    eng.begin(pages, nkeys, Qa, shape, 1, ntok)
+    assert eng.end(*r1) >= 0
+    assert eng.graph_calls == g0                      # not armed yet: the plain path
+    eng.arm(pages, nkeys, shape, ntok)
+    r2 = out()
+    eng.begin(pages, nkeys, Qa, shape, 1, ntok)
+    assert eng.end(*r2) >= 0
+    assert eng.graph_calls == g0 + 1
+    assert all(np.array_equal(a, b) for a, b in zip(r1, r2))
+    r3 = out()                                       # another shape (the first page only), never armed: plain path
+    eng.begin(pages[:1], nkeys[:1], Qa, shape, 1, ntok)
+    assert eng.end(*r3) >= 0
+    assert eng.graph_calls == g0 + 1
+    check(r3, Qa, nkeys[0])
+    r4 = out()                                       # the armed shape again, with another Q: replayed, new Q read
+    eng.begin(pages, nkeys, Qb, shape, 1, ntok)
+    assert eng.end(*r4) >= 0
+    assert eng.graph_calls == g0 + 2
+    check(r4, Qb, nk)
+    for pg in pages:
+        eng.free_page(pg)
+
+
 def test_bounded_wait_reports_and_context_recovers(ctx):
     """Failure detection without a GPU fault: with the stall hook on, the consumer warps wait on a barrier that nothing
     completes; after the 1 ms limit the kernel records the timeout and returns (no trap), the host reads ETIMEOUT,
