@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--chunk-keys", type=int, default=0,
                     help="keys per decode job (0: the plan's own choice); lets a small capture keep the full run's job size")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--prefill-steps", type=int, default=3)
+    ap.add_argument("--prefill-steps", type=int, default=5)
     ap.add_argument("--prefill-layers", type=int, default=LAYERS)
     return ap.parse_args()
 
@@ -254,11 +254,12 @@ def bench_prefill(torch, pa, ctx, device, stream, layers: int, steps: int):
     torch.cuda.synchronize()
     plan.profile(steps)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        plan.run(Qs, O, m, l, stream)
-    e1.record(stream)
-    torch.cuda.synchronize()
+    with ClockSampler(device.index if device.index is not None else 0) as clk:
+        e0.record(stream)
+        for _ in range(steps):
+            plan.run(Qs, O, m, l, stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
     ctx.status(stream)
     ms = e0.elapsed_time(e1) / steps
     kms, kn = plan.kernel_ms()
@@ -274,7 +275,7 @@ def bench_prefill(torch, pa, ctx, device, stream, layers: int, steps: int):
             "roofline": {"bound": "tensor", "achieved": round(flops / (kms * 1e-3) / 1e12, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(flops / (kms * 1e-3) / 1e12 / peak, 4), "peak_kind": kind,
                          "kernel": "pa::pre::prefill_kernel<1,2>", "kernel_ms": round(kms, 3),
-                         "algorithmic_flops_per_launch": flops}}
+                         "algorithmic_flops_per_launch": flops}, "clocks": clk.summary()}
 
 
 # --------------------------------------------------------------------------------------------- GPU arm
