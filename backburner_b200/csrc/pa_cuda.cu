@@ -219,6 +219,22 @@ cudaError_t launch_decode(const pa_cuda_plan *p, const pa::dec::Params &prm, cud
     kern<<<grid, 32 * p->n_consumers, p->smem, st>>>(prm);
     return cudaGetLastError();
 }
+// CTAs of a plan's decode-kernel instance that fit one SM at once (registers, shared memory, threads)
+template <int HD, int Q>
+int decode_regs() {
+    cudaFuncAttributes a{};
+    return cudaFuncGetAttributes(&a, pa::dec::decode_kernel<HD, Q>) == cudaSuccess ? a.numRegs : 128;
+}
+int decode_ctas_per_sm(const pa_cuda_plan *p) {
+    const uint32_t hd = p->sh.hd, q = p->sh.quant;
+    const int regs = hd == 128 ? (q == PA_CUDA_Q8_0 ? decode_regs<128, 1>() : q == PA_CUDA_Q4_0 ? decode_regs<128, 2>() : decode_regs<128, 0>())
+                               : (q == PA_CUDA_Q8_0 ? decode_regs<256, 1>() : q == PA_CUDA_Q4_0 ? decode_regs<256, 2>() : decode_regs<256, 0>());
+    const int threads = 32 * (int) p->n_consumers;
+    const int by_regs = 65536 / std::max(1, threads * ((regs + 7) / 8 * 8));
+    const int by_smem = (int) ((228u * 1024u) / (p->smem + 1024));
+    const int by_threads = 2048 / std::max(1, threads);
+    return std::max(1, std::min(std::min(by_regs, by_smem), std::min(by_threads, 32)));
+}
 // the decode-kernel instance of a geometry (hd 128 / 256; f16, Q8_0 or Q4_0 rows)
 cudaError_t launch_decode_any(const pa_cuda_plan *p, const pa::dec::Params &prm, cudaStream_t st, uint32_t hd,
                               uint32_t quant) {
@@ -480,9 +496,25 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
         const uint64_t jobs_wanted = std::max<uint64_t>(1, ((uint64_t) ctx->n_sm * 4 + p->grid_y - 1) / p->grid_y);
         chunk = (uint32_t) std::max<uint64_t>(1024, (total + jobs_wanted - 1) / jobs_wanted);
     } else if (chunk == 0) {
-        // about 16 waves of CTAs over the SMs (one CTA per SM), 128..16384 keys per job
-        const uint64_t per_y = std::max<uint64_t>(1, (uint64_t) ctx->n_sm * 16 / std::max<uint32_t>(1, p->grid_y));
-        chunk = (uint32_t) std::min<uint64_t>(16384, std::max<uint64_t>(128, (total + per_y - 1) / per_y));
+        // The job size that minimises the modelled time: waves x (keys per job + a per-job overhead worth ~150 keys,
+        // fitted on B200 from config-1 runs: 1M keys took 3,233 GB/s as 448-key jobs, 3,898 as 1,024, 4,142 as 3,584
+        // and 3,682 as 8,192, the last being less than one wave). Waves count the CTAs that fit the SMs at once.
+        const uint32_t slots = (uint32_t) ctx->n_sm * (uint32_t) decode_ctas_per_sm(p);
+        uint64_t best = ~0ull;
+        for (uint32_t c = 128; c <= 16384; c += 64) {
+            uint64_t jobs = 0, cmax = 0;
+            for (uint32_t i = 0; i < n_segs; i++) {
+                const uint32_t nk = segs[i].nk;
+                if (!nk) continue;
+                const uint32_t nj = (nk + c - 1) / c, cj = ((nk + nj - 1) / nj + 63) / 64 * 64;
+                jobs += (nk + cj - 1) / cj;
+                cmax = std::max<uint64_t>(cmax, cj);
+            }
+            const uint64_t waves = (jobs * p->grid_y + slots - 1) / slots;
+            const uint64_t cost = waves * (cmax + 150);
+            if (cost <= best) { best = cost; chunk = c; }
+        }
+        if (!chunk) chunk = 128;
     }
     chunk = (chunk + 63) / 64 * 64;
 
