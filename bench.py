@@ -71,13 +71,16 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
-def measured_tensor_peak():
+def measured_tensor_peak(sustained: bool = False):
+    """bf16 dense TFLOP/s from MEASURED_PEAKS.json: the burst figure, or the power-capped sustained one."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             d = json.load(f)
+        if sustained:
+            return float(d["bf16_tflops_sustained"]), "measured (sustained)"
         return float(d["bf16_tflops"]), "measured (burst)"
     except Exception:
-        return 1590.0, "fallback"
+        return (1400.0, "fallback (sustained)") if sustained else (1590.0, "fallback")
 
 
 class ClockSampler:
@@ -266,6 +269,7 @@ def bench_prefill(torch, pa, ctx, device, stream, layers: int, steps: int):
     kms /= max(1, kn)
     flops = 4.0 * PF_TOKENS * Q_HEADS * HD * PF_KEYS * layers
     peak, kind = measured_tensor_peak()
+    peak_s, _ = measured_tensor_peak(sustained=True)
     plan.close()
     del K, V, Qs, O
     torch.cuda.empty_cache()
@@ -274,6 +278,7 @@ def bench_prefill(torch, pa, ctx, device, stream, layers: int, steps: int):
             "layers": layers, "steps": steps,
             "roofline": {"bound": "tensor", "achieved": round(flops / (kms * 1e-3) / 1e12, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(flops / (kms * 1e-3) / 1e12 / peak, 4), "peak_kind": kind,
+                         "frac_of_sustained": round(flops / (kms * 1e-3) / 1e12 / peak_s, 4),
                          "kernel": "pa::pre::prefill_kernel<1,2>", "kernel_ms": round(kms, 3),
                          "algorithmic_flops_per_launch": flops}, "clocks": clk.summary()}
 
