@@ -30,7 +30,8 @@ struct Plan;
 // pa::engine calls: plans are kept per call shape (a layer's pages, its key counts, the geometry), so the per-layer
 // calls of a decode step reuse their job lists and partial buffers instead of allocating them every call; a plan
 // armed for the next call (pa_cuda_arm) also holds a CUDA graph of the whole call.
-constexpr size_t kEngCache = 256;
+constexpr size_t kEngCache = 256;                 // plans at most
+constexpr size_t kEngCacheBytes = 1ull << 30;     // and at most this much plan scratch (partials, job lists)
 struct EngEntry {
     std::vector<uint64_t> key;           // geometry, groups, packed tokens, then (k, v, nkeys) per page
     pa_cuda_plan *plan = nullptr;
@@ -837,7 +838,13 @@ int eng_prepare(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *nke
     for (auto &e : ctx->eng_cache)
         if (e.key == key) { entry = &e; break; }
     if (!entry) {
-        if (ctx->eng_cache.size() >= kEngCache) {   // evict the least recently used entry
+        // evict least recently used entries while the cache is full (by count or by plan scratch)
+        auto held = [&]() {
+            size_t b = 0;
+            for (auto &e : ctx->eng_cache) b += e.plan ? e.plan->scratch : 0;
+            return b;
+        };
+        while (!ctx->eng_cache.empty() && (ctx->eng_cache.size() >= kEngCache || held() > kEngCacheBytes)) {
             auto lru = std::min_element(ctx->eng_cache.begin(), ctx->eng_cache.end(),
                                         [](const EngEntry &a, const EngEntry &b) { return a.used < b.used; });
             cudaStreamSynchronize(ctx->stream);
