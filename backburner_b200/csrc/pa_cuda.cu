@@ -129,13 +129,14 @@ int check_shape(pa_cuda_ctx *ctx, const pa_cuda_shape *sh) {
 // launch shape of the decode kernel for a geometry
 int plan_decode_shape(pa_cuda_ctx *ctx, pa_cuda_plan *p) {
     const pa_cuda_shape &sh = p->sh;
-    const uint32_t maxw = sh.hd == 128 ? 16 : 12;
+    // warps per CTA: 8 at hd 128, so that two CTAs (two independent stage rings) share an SM; 12 at hd 256
+    const uint32_t maxw = sh.hd == 128 ? 8 : 12;
     p->n_rg = (sh.rows + 7) / 8;
     // shared memory of NSTAGE stages of key pairs for head-group rows of `row` bytes (pairs padded to an odd number of
     // 16-byte units)
     auto pair_stride = [](uint32_t row) { uint32_t gs = 2 * row; return (gs / 16) % 2 == 0 ? gs + 16 : gs; };
-    auto smem_for = [](uint32_t gs) {
-        return (size_t) pa::dec::NSTAGE * pa::dec::STAGE_KEYS * gs + pa::dec::SMEM_SLACK + (pa::dec::NSTAGE + 3) * 8 +
+    auto smem_for = [&sh](uint32_t gs) {
+        return (size_t) pa::dec::NSTAGE * pa::dec::stage_keys((int) sh.hd) * gs + pa::dec::SMEM_SLACK + (pa::dec::NSTAGE + 3) * 8 +
                2 * pa::dec::NSTAGE * 4 + 16;
     };
     // the largest head group that divides nkv, gives 16-byte aligned rows and fits shared memory
@@ -154,7 +155,8 @@ int plan_decode_shape(pa_cuda_ctx *ctx, pa_cuda_plan *p) {
     p->hg = hg;
     p->rgc = std::min(p->n_rg, maxw / hg);
     const uint32_t S = hg * p->rgc;
-    p->pw = 2 * S <= maxw ? 2 : 1;
+    // two warps per stream split a stage's tiles; with one tile per stage each stream has one warp
+    p->pw = (pa::dec::stage_keys((int) sh.hd) / pa::dec::TILE_KEYS >= 2 && 2 * S <= maxw) ? 2 : 1;
     p->n_consumers = S * p->pw;
     p->grid_y = (sh.nkv / hg) * ((p->n_rg + p->rgc - 1) / p->rgc);
     p->row = (uint32_t) (hg * sh.hb);                  // a multiple of 16 by the choice of hg

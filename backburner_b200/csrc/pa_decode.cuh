@@ -7,11 +7,12 @@
 // (pa-metal.mm:452-464). Output per chunk of keys: the unnormalised partial (O, m, l); pa_merge.cuh folds chunks.
 //
 // B200 design (one CTA = one key chunk x a group of heads x a group of query rows):
-//   * each 32-key stage of K and V rows is streamed from HBM into shared memory with 1-D bulk copies (TMA engine), one
-//     copy per PAIR of key rows (requests of one 1 KB row cap a B200 at ~5.4 TB/s, two rows reach ~7.4 TB/s), pairs
-//     padded to an odd number of 16-byte units; NSTAGE stages ring on "full" mbarriers; the last warp to finish with a
-//     stage (a shared counter) refills it, so there is no producer warp and every warp of the CTA computes (16 warps:
-//     128 registers each);
+//   * each stage of K and V rows (16 keys at hd 128, 32 at hd 256) is streamed from HBM into shared memory with 1-D
+//     bulk copies (TMA engine), one copy per PAIR of key rows (requests of one 1 KB row cap a B200 at ~5.4 TB/s, two
+//     rows reach ~7.4 TB/s), pairs padded to an odd number of 16-byte units; NSTAGE stages ring on "full" mbarriers;
+//     the last warp to finish with a stage (a shared counter) refills it, so there is no producer warp and every warp
+//     of the CTA computes. At hd 128 a CTA has 8 warps of 128 registers and two CTAs share an SM: their stage rings
+//     run independently (one 16-warp CTA with 32-key stages measured 6% slower);
 //   * the MMA's 16 key rows are ordered even keys first (row g = key 2g, row g+8 = key 2g+1): with the pair layout
 //     every 32-bit shared-memory read of K and V hits at most 2 lanes per bank;
 //   * each consumer warp owns one (head, 8-row group) and, when there are few such groups, every other 16-key tile;
@@ -31,7 +32,9 @@
 namespace pa {
 namespace dec {
 
-constexpr int STAGE_KEYS = 32;   // keys per pipeline stage (= lanes of the warp that issues its copies)
+// keys per pipeline stage: one 16-key MMA tile at hd 128 (8-warp CTAs, two per SM: two independent stage rings), two
+// tiles at hd 256 (12-warp CTAs); one lane copies a pair of rows
+__host__ __device__ constexpr int stage_keys(int hd) { return hd == 128 ? 16 : 32; }
 constexpr int TILE_KEYS = 16;    // keys per MMA tile
 constexpr int NSTAGE = 3;
 constexpr int SMEM_SLACK = 64;   // readable bytes past the last row (a lane may load one unused word there)
@@ -127,8 +130,9 @@ __device__ __forceinline__ void q4_word(uint32_t w, uint32_t s2, uint32_t &l02, 
 
 // ---------------------------------------------------------------- the kernel
 template <int HD, int QUANT>
-__global__ void __launch_bounds__(32 * (HD == 128 ? 16 : 12), 1) decode_kernel(const Params p) {
+__global__ void __launch_bounds__(32 * (HD == 128 ? 8 : 12), HD == 128 ? 2 : 1) decode_kernel(const Params p) {
     constexpr int NMT = HD / 16;   // k-steps of QK^T = m-tiles of P.V
+    constexpr int STAGE_KEYS = stage_keys(HD);
     constexpr int GB = q_group_bytes(QUANT);
     constexpr int PAIR = 2 * GB;   // bytes of an aligned pair of quant blocks
 
