@@ -263,7 +263,9 @@ __global__ void __launch_bounds__(32 * (HD == 128 ? 8 : 12), HD == 128 ? 2 : 1) 
         const uint32_t valid = min((uint32_t) STAGE_KEYS, job.nk - it * STAGE_KEYS);
         const uint32_t kbase = smem_u32(smem + s * stage_bytes) + hoff;
         const uint32_t vbase = kbase + half_stage;
-        for (uint32_t tt = par; tt < STAGE_KEYS / TILE_KEYS; tt += p.pw) {
+        // one tile per stage (hd 128: the host sets one warp per stream) or the stream's warps split the stage's tiles
+        constexpr bool ONE_TILE = STAGE_KEYS == TILE_KEYS;
+        for (uint32_t tt = ONE_TILE ? 0u : par; tt < STAGE_KEYS / TILE_KEYS; tt += ONE_TILE ? 1u : p.pw) {
             const int tvalid = (int) valid - (int) tt * TILE_KEYS;
             if (tvalid <= 0) break;
             const uint32_t tk = kbase + tt * (TILE_KEYS / 2) * gs;   // the tile's 8 pairs
