@@ -251,8 +251,8 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     // NT == 2: 16 warps launched with 128 registers each; every warpgroup's branch starts by resizing its share:
-    // control 88 (the MMA issuer keeps its operand descriptors in registers), softmax 2 x 160, dequant 104
-    // (128 x (88 + 160 + 160 + 104) = 65,536 = the launched total)
+    // control 128 (TMA and the MMA issuers), softmax 2 x 152, dequant 80 (128 x (128 + 152 + 152 + 80) = 65,536 = the
+    // launched total): the split at which no role spills
 
     auto wait = [&](uint64_t *b, uint32_t parity) -> bool {
         if (!ok) return false;
@@ -265,7 +265,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
     };
 
     if (warp < 4) {
-      if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 88;");
+      if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 128;");
       if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
       }   // warp 3: idle
     } else if (warp < (uint32_t) DQ0) {
         // ------------------------------------------------ softmax warpgroup of tile t
-        if (NT == 2) asm volatile("setmaxnreg.inc.sync.aligned.u32 160;");
+        if (NT == 2) asm volatile("setmaxnreg.inc.sync.aligned.u32 152;");
         const int t = (int) (warp - SM0) / 4;
         const uint32_t wq = warp % 4;                      // TMEM lane quarter of this warp
         const uint32_t r = wq * 32 + lane;                 // row of the tile = TMEM lane
@@ -462,7 +462,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
         }
     } else {
         // ------------------------------------------------ dequantisers: warp dw owns quant block dw of every key
-        if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 104;");
+        if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 80;");
         const uint32_t dw = warp - DQ0;
         const uint32_t bo = hoff + GB * dw;                 // block start inside the raw window row
         const uint32_t w16 = bo & ~15u;                     // 16-byte aligned start of the words covering it
