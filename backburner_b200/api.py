@@ -57,6 +57,7 @@ _SIGS = {
     "pa_cuda_plan_scratch_bytes": (ctypes.c_size_t, [_P]),
     "pa_cuda_plan_jobs": (ctypes.c_uint32, [_P]),
     "pa_cuda_plan_launches": (ctypes.c_uint32, [_P]),
+    "pa_cuda_plan_kernel": (ctypes.c_char_p, [_P]),
     "pa_cuda_plan_run": (ctypes.c_int, [_P, _P, _P, _P, _P, _P]),
     "pa_cuda_plan_run_host": (ctypes.c_int, [_P, _P, _P, _P, _P, _P]),
     "pa_cuda_plan_destroy": (None, [_P]),
@@ -187,7 +188,8 @@ class Context:
         lib().pa_cuda_set_timeout_ns(self._h, int(ns))
 
     def set_kernel(self, which: int):
-        """0: by shape; 1: split-K mma.sync kernel; 2: tcgen05 kernel (hd 128) — for plans created afterwards."""
+        """0: by shape; 1: split-K mma.sync kernel; 2: tcgen05 kernel on single CTAs; 3: tcgen05 kernel on CTA pairs
+        (2 and 3: hd 128, quantised rows) — for plans created afterwards."""
         lib().pa_cuda_set_kernel(self._h, int(which))
 
     def set_stall_test(self, on: bool):
@@ -233,6 +235,11 @@ class Plan:
     @property
     def launches(self) -> int:
         return int(lib().pa_cuda_plan_launches(self._h))
+
+    @property
+    def kernel(self) -> str:
+        """Name of the attention-kernel instance the plan launches."""
+        return lib().pa_cuda_plan_kernel(self._h).decode()
 
     def run(self, Qs, O, m, l, stream=None):
         self.ctx.check(lib().pa_cuda_plan_run(self._h, _ptr(Qs), _ptr(O), _ptr(m), _ptr(l), _stream_ptr(stream)),

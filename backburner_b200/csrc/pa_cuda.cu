@@ -19,11 +19,13 @@
 #include "pa_decode.cuh"
 #include "pa_merge.cuh"
 #include "pa_prefill.cuh"
+#include "pa_prefill_pair.cuh"
 
 namespace {
 
 constexpr int kMaxSmem = 227 * 1024;
 constexpr uint32_t kPrefillMinRows = 64;   // query rows per KV head from which the tcgen05 kernel is used
+constexpr uint32_t kPairMinRows = 512;     // ... and from which it runs on CTA pairs
 
 struct Plan;
 
@@ -50,7 +52,7 @@ struct pa_cuda_ctx {
     uint64_t timeout_ns = 2000000000ull;
     uint64_t launches = 0;
     int stall_test = 0;
-    int kernel_choice = 0;   // 0 auto, 1 split-K mma.sync kernel, 2 tcgen05 kernel
+    int kernel_choice = 0;   // 0 auto, 1 split-K mma.sync kernel, 2 tcgen05 kernel (one CTA), 3 tcgen05 on CTA pairs
     std::string err;
     // pa::engine state (begin/end)
     pa_cuda_plan *eng_plan = nullptr;      // the current call's plan (owned by eng_cache)
@@ -81,8 +83,9 @@ struct pa_cuda_plan {
     // decode launch shape
     uint32_t hg = 1, rgc = 1, n_rg = 1, pw = 1, n_consumers = 1, row = 0, gs = 0, grid_y = 1;
     size_t smem = 0;
-    // tcgen05 path (many query rows per KV head, hd 128): tiles of NT x 128 rows, tensor maps of the K/V segments
-    bool prefill = false;
+    // tcgen05 path (many query rows per KV head, hd 128): tiles of NT x 128 rows (NT x 256 on a CTA pair), tensor
+    // maps of the K/V segments
+    bool prefill = false, pair = false;
     int nt = 1;
     uint32_t n_rt = 0;
     CUtensorMap *d_maps = nullptr;
@@ -178,12 +181,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 // quantised rows of one segment as a 2-D u8 tensor {rs bytes, nk keys}; a box is one head's 16-byte-aligned window
-bool map_rows(CUtensorMap *m, const void *base, uint64_t rs, uint32_t nk, uint32_t raw_bytes) {
+bool map_rows(CUtensorMap *m, const void *base, uint64_t rs, uint32_t nk, uint32_t raw_bytes, uint32_t box_keys) {
     auto fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[2] = {rs, nk};
     const cuuint64_t strides[1] = {rs};
-    const cuuint32_t box[2] = {raw_bytes, (cuuint32_t) pa::pre::BN};
+    const cuuint32_t box[2] = {raw_bytes, box_keys};
     const cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -211,6 +214,28 @@ cudaError_t launch_prefill(const pa_cuda_plan *p, const CUtensorMap &tq, const p
     dim3 grid(p->n_jobs, p->sh.nkv * p->n_rt);
     kern<<<grid, 32 * (8 + 4 * NT), smem, st>>>(tq, prm);
     return cudaGetLastError();
+}
+// the CTA-pair kernel: clusters of 2 CTAs along x, one cluster per job
+template <int Q, int NT>
+cudaError_t launch_prefill_pair(const pa_cuda_plan *p, const CUtensorMap &tq, const pa::pre::Params &prm, cudaStream_t st) {
+    auto kern = pa::pre::prefill_pair_kernel<Q, NT>;
+    constexpr int smem = pa::pre::PairSmem<Q, NT>::TOTAL + 1024;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * p->n_jobs, p->sh.nkv * p->n_rt);
+    cfg.blockDim = dim3(32 * (8 + 4 * NT));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, tq, prm);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <int HD, int Q>
@@ -279,8 +304,16 @@ int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, 
         const bool prof = p->profile && p->ev_used + 2 <= p->ev.size();
         if (prof) cudaEventRecord(p->ev[p->ev_used], st);
         cudaError_t e;
-        if (sh.quant == PA_CUDA_Q8_0) e = p->nt == 2 ? launch_prefill<1, 2>(p, tq, prm, st) : launch_prefill<1, 1>(p, tq, prm, st);
-        else e = p->nt == 2 ? launch_prefill<2, 2>(p, tq, prm, st) : launch_prefill<2, 1>(p, tq, prm, st);
+        if (p->pair) {
+            if (sh.quant == PA_CUDA_Q8_0)
+                e = p->nt == 2 ? launch_prefill_pair<1, 2>(p, tq, prm, st) : launch_prefill_pair<1, 1>(p, tq, prm, st);
+            else
+                e = p->nt == 2 ? launch_prefill_pair<2, 2>(p, tq, prm, st) : launch_prefill_pair<2, 1>(p, tq, prm, st);
+        } else if (sh.quant == PA_CUDA_Q8_0) {
+            e = p->nt == 2 ? launch_prefill<1, 2>(p, tq, prm, st) : launch_prefill<1, 1>(p, tq, prm, st);
+        } else {
+            e = p->nt == 2 ? launch_prefill<2, 2>(p, tq, prm, st) : launch_prefill<2, 1>(p, tq, prm, st);
+        }
         if (e != cudaSuccess) return cuda_fail(ctx, e, "prefill kernel launch");
         if (prof) {
             cudaEventRecord(p->ev[p->ev_used + 1], st);
@@ -471,16 +504,19 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
     // the tcgen05 kernel takes calls with many query rows per KV head (prefill, ATTN_BIG, long verify batches), the
     // split-K kernel the decode-sized ones (as the reference engine switches kernels by rows, pa-metal.mm:818-835)
     const bool tc_ok = shape->hd == 128 && shape->quant != PA_CUDA_F16 && encode_fn() != nullptr;
-    p->prefill = tc_ok && (ctx->kernel_choice == 2 || (ctx->kernel_choice == 0 && shape->rows >= kPrefillMinRows));
-    if (ctx->kernel_choice == 2 && !tc_ok) {
+    p->prefill = tc_ok && (ctx->kernel_choice >= 2 || (ctx->kernel_choice == 0 && shape->rows >= kPrefillMinRows));
+    if (ctx->kernel_choice >= 2 && !tc_ok) {
         delete p;
         return fail(ctx, PA_CUDA_EUNSUPPORTED, "tcgen05 kernel needs hd 128 and quantised (Q8_0 / Q4_0) rows");
     }
     if (p->prefill) {
         // PA_CUDA_TC_TILES=1|2: Q tiles of 128 rows per CTA (default: 2 when there are more than 128 rows)
         static const int tiles_env = getenv("PA_CUDA_TC_TILES") ? atoi(getenv("PA_CUDA_TC_TILES")) : 0;
-        p->nt = (tiles_env == 1 || tiles_env == 2) ? tiles_env : (shape->rows > (uint32_t) pa::pre::BM ? 2 : 1);
-        p->n_rt = (shape->rows + pa::pre::BM * p->nt - 1) / (pa::pre::BM * p->nt);
+        // CTA pairs (2-SM MMAs, half of each K/V block dequantised per SM) from kPairMinRows rows per KV head
+        p->pair = ctx->kernel_choice == 3 || (ctx->kernel_choice == 0 && shape->rows >= kPairMinRows);
+        const uint32_t tile_rows = (uint32_t) pa::pre::BM * (p->pair ? 2u : 1u);
+        p->nt = (tiles_env == 1 || tiles_env == 2) ? tiles_env : (shape->rows > tile_rows ? 2 : 1);
+        p->n_rt = (shape->rows + tile_rows * p->nt - 1) / (tile_rows * p->nt);
         p->grid_y = shape->nkv * p->n_rt;
     }
 
@@ -496,7 +532,8 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
     uint32_t chunk = chunk_keys;
     if (chunk == 0 && p->prefill) {
         // at least ~4 CTAs per SM in total, >= 1024 keys per job
-        const uint64_t jobs_wanted = std::max<uint64_t>(1, ((uint64_t) ctx->n_sm * 4 + p->grid_y - 1) / p->grid_y);
+        const uint64_t ctas_per_job = (uint64_t) p->grid_y * (p->pair ? 2 : 1);
+        const uint64_t jobs_wanted = std::max<uint64_t>(1, ((uint64_t) ctx->n_sm * 4 + ctas_per_job - 1) / ctas_per_job);
         chunk = (uint32_t) std::max<uint64_t>(1024, (total + jobs_wanted - 1) / jobs_wanted);
     } else if (chunk == 0) {
         // The job size that minimises the modelled time: waves x (keys per job + a per-job overhead worth ~150 keys,
@@ -567,8 +604,10 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
         const uint32_t rawb = (uint32_t) pa::pre::raw_row_bytes((int) shape->quant);
         for (uint32_t i = 0; i < n_segs; i++) {
             if (!segs[i].nk) continue;
-            if (!map_rows(&maps[2 * i], segs[i].k, shape->rs, segs[i].nk, rawb) ||
-                !map_rows(&maps[2 * i + 1], segs[i].v, shape->rs, segs[i].nk, rawb)) {
+            // a CTA of a pair loads half of each block's K rows and all of its V rows
+            const uint32_t kbox = p->pair ? (uint32_t) pa::pre::BN / 2 : (uint32_t) pa::pre::BN;
+            if (!map_rows(&maps[2 * i], segs[i].k, shape->rs, segs[i].nk, rawb, kbox) ||
+                !map_rows(&maps[2 * i + 1], segs[i].v, shape->rs, segs[i].nk, rawb, (uint32_t) pa::pre::BN)) {
                 pa_cuda_plan_destroy(p);
                 return fail(ctx, PA_CUDA_ECUDA, "cuTensorMapEncodeTiled (K/V rows) failed");
             }
@@ -587,6 +626,22 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
 size_t pa_cuda_plan_scratch_bytes(const pa_cuda_plan *p) { return p ? p->scratch : 0; }
 uint32_t pa_cuda_plan_jobs(const pa_cuda_plan *p) { return p ? p->n_jobs : 0; }
 uint32_t pa_cuda_plan_launches(const pa_cuda_plan *p) { return p ? (p->n_jobs ? 2u : 1u) : 0u; }
+
+const char *pa_cuda_plan_kernel(const pa_cuda_plan *p) {
+    if (!p) return "";
+    const uint32_t q = p->sh.quant;
+    if (p->prefill) {
+        static const char *names[2][2][2] = {
+            {{"pa::pre::prefill_kernel<1,1>", "pa::pre::prefill_kernel<1,2>"},
+             {"pa::pre::prefill_kernel<2,1>", "pa::pre::prefill_kernel<2,2>"}},
+            {{"pa::pre::prefill_pair_kernel<1,1>", "pa::pre::prefill_pair_kernel<1,2>"},
+             {"pa::pre::prefill_pair_kernel<2,1>", "pa::pre::prefill_pair_kernel<2,2>"}}};
+        return names[p->pair ? 1 : 0][q == PA_CUDA_Q8_0 ? 0 : 1][p->nt == 2 ? 1 : 0];
+    }
+    static const char *dec[2][3] = {{"pa::dec::decode_kernel<128,0>", "pa::dec::decode_kernel<128,1>", "pa::dec::decode_kernel<128,2>"},
+                                    {"pa::dec::decode_kernel<256,0>", "pa::dec::decode_kernel<256,1>", "pa::dec::decode_kernel<256,2>"}};
+    return dec[p->sh.hd == 128 ? 0 : 1][q <= 2 ? q : 0];
+}
 
 int pa_cuda_plan_run(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, void *stream) {
     if (!p) return PA_CUDA_EINVAL;

@@ -267,6 +267,7 @@ def bench_prefill(torch, pa, ctx, device, stream, layers: int, steps: int):
     ms = e0.elapsed_time(e1) / steps
     kms, kn = plan.kernel_ms()
     kms /= max(1, kn)
+    kname = plan.kernel
     flops = 4.0 * PF_TOKENS * Q_HEADS * HD * PF_KEYS * layers
     peak, kind = measured_tensor_peak()
     peak_s, _ = measured_tensor_peak(sustained=True)
@@ -279,7 +280,7 @@ def bench_prefill(torch, pa, ctx, device, stream, layers: int, steps: int):
             "roofline": {"bound": "tensor", "achieved": round(flops / (kms * 1e-3) / 1e12, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(flops / (kms * 1e-3) / 1e12 / peak, 4), "peak_kind": kind,
                          "frac_of_sustained": round(flops / (kms * 1e-3) / 1e12 / peak_s, 4),
-                         "kernel": "pa::pre::prefill_kernel<1,2>", "kernel_ms": round(kms, 3),
+                         "kernel": kname, "kernel_ms": round(kms, 3),
                          "algorithmic_flops_per_launch": flops}, "clocks": clk.summary()}
 
 
@@ -387,7 +388,7 @@ def main():
         pass
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                "kernel": "pa::dec::decode_kernel<128,1>", "kernel_ms": round(kern_avg_ms, 4),
+                "kernel": plan.kernel, "kernel_ms": round(kern_avg_ms, 4),
                 "algorithmic_bytes_per_launch": launch_bytes}
 
     # ---- end to end through the host-buffer path (pinned Q in, O/m/l out, copies inside the timed region)

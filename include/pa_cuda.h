@@ -90,7 +90,8 @@ int pa_cuda_status(pa_cuda_ctx *ctx, void *stream);
 void pa_cuda_set_timeout_ns(pa_cuda_ctx *ctx, uint64_t ns);
 /* Kernel selection for plans created afterwards (as the reference engine's PA_BIG_KERNEL / PA_BIG_MIN_NG switches,
  * phone-attn/pa-metal.mm:818-821): 0 = by shape (default: the tcgen05 kernel for hd 128 and >= 64 query rows per KV
- * head, the split-K mma.sync kernel otherwise), 1 = always the split-K kernel, 2 = the tcgen05 kernel (hd 128 only). */
+ * head, on CTA pairs from 512 rows; the split-K mma.sync kernel otherwise), 1 = always the split-K kernel, 2 = the
+ * tcgen05 kernel on single CTAs, 3 = the tcgen05 kernel on CTA pairs (2 and 3: hd 128 and quantised rows only). */
 void pa_cuda_set_kernel(pa_cuda_ctx *ctx, int which);
 /* Failure-detection test hook: while on, the decode kernel's consumer warps first wait on a barrier that nothing
  * completes, so their bounded wait runs out after the timeout; the kernel records PA_CUDA_ETIMEOUT and returns
@@ -108,6 +109,8 @@ size_t pa_cuda_plan_scratch_bytes(const pa_cuda_plan *plan);
 uint32_t pa_cuda_plan_jobs(const pa_cuda_plan *plan);
 /* kernel launches one pa_cuda_plan_run makes */
 uint32_t pa_cuda_plan_launches(const pa_cuda_plan *plan);
+/* name of the plan's attention-kernel instance, e.g. "pa::pre::prefill_pair_kernel<1,2>" (static storage) */
+const char *pa_cuda_plan_kernel(const pa_cuda_plan *plan);
 /* Qs, O, m, l: device pointers laid out [set][nkv][rows]...; stream: cudaStream_t (NULL = the context's stream).
  * Asynchronous. */
 int pa_cuda_plan_run(pa_cuda_plan *plan, const uint16_t *Qs, float *O, float *m, float *l, void *stream);

@@ -38,20 +38,32 @@ def test_tcgen05_kernel_parity(ctx, rows, nk, quant):
     _check(c, O, m, l, nk)
 
 
+# the CTA-pair instance (kernel 3): 256-row pair tiles, NT = 1 up to 256 rows and 2 above; ragged rows and keys
+@pytest.mark.parametrize("rows,nk,quant", [
+    (512, 4096, orc.Q8_0), (640, 4096, orc.Q8_0), (300, 1500, orc.Q4_0), (129, 700, orc.Q8_0), (257, 65, orc.Q8_0),
+    (256, 1, orc.Q8_0), (200, 63, orc.Q4_0), (1024, 2048, orc.Q4_0), (5, 333, orc.Q8_0), (768, 97, orc.Q8_0)])
+def test_tcgen05_pair_kernel_parity(ctx, rows, nk, quant):
+    c = orc.gen_case(5000 + rows + nk + quant, 128, 8, rows, nk, quant)
+    O, m, l = _run_kernel(ctx, c, 3)
+    _check(c, O, m, l, nk)
+
+
 @pytest.mark.parametrize("rows,nk", [(80, 3000), (256, 2000)])
 def test_tcgen05_matches_split_k_kernel(ctx, rows, nk):
     c = orc.gen_case(77 + rows, 128, 8, rows, nk, orc.Q8_0)
-    O2, m2, l2 = _run_kernel(ctx, c, 2)
     O1, m1, l1 = _run_kernel(ctx, c, 1)
-    e = orc.rel_err(O2, m2, l2, O1.astype(np.float64), m1.astype(np.float64), l1.astype(np.float64))
-    assert e[0] <= 1e-3 and e[1] <= 1e-3, e
+    for which in (2, 3):
+        O2, m2, l2 = _run_kernel(ctx, c, which)
+        e = orc.rel_err(O2, m2, l2, O1.astype(np.float64), m1.astype(np.float64), l1.astype(np.float64))
+        assert e[0] <= 1e-3 and e[1] <= 1e-3, (which, e)
 
 
-def test_tcgen05_many_sets_and_split_keys(ctx):
+@pytest.mark.parametrize("which,rows", [(2, 160), (3, 160), (3, 600)])
+def test_tcgen05_many_sets_and_split_keys(ctx, which, rows):
     """Several layers (output sets) in one plan, each split into several key chunks (jobs), run twice."""
     import torch
-    hd, nkv, rows = 128, 8, 160
-    ctx.set_kernel(2)
+    hd, nkv = 128, 8
+    ctx.set_kernel(which)
     try:
         shape = pa.shape_for(hd, nkv, rows, pa.Q8_0)
         cases = [orc.gen_case(900 + i, hd, nkv, rows, nk, orc.Q8_0) for i, nk in enumerate([5000, 64, 2100])]
@@ -73,7 +85,8 @@ def test_tcgen05_many_sets_and_split_keys(ctx):
         ctx.set_kernel(0)
 
 
-def test_tcgen05_student_t_values(ctx):
+@pytest.mark.parametrize("which", [2, 3])
+def test_tcgen05_student_t_values(ctx, which):
     c = orc.gen_case(44, 128, 8, 256, 3000, orc.Q8_0, student_t=True)
-    O, m, l = _run_kernel(ctx, c, 2)
+    O, m, l = _run_kernel(ctx, c, which)
     _check(c, O, m, l, 3000)
