@@ -10,6 +10,7 @@ over that ABI (ctypes), mirroring the reference's engine and kernel interfaces:
     merge_partial / pa_merge (phone-attn.h:231-239,
         pa-metal.mm:137-159)                             -> merge()
     attn_core's normalisation (phone-attn.h:651-655)     -> normalize()
+    the co-attention slot of a reply (phone-attn.h:18-20) -> fold_reply()
     pa::engine (phone-attn.h:166-183)                    -> Engine (pages, begin, end)
 
 There is no CPU fallback: importing works without a GPU (so the host logic can be tested), but every compute call
@@ -19,6 +20,7 @@ from __future__ import annotations
 
 from .api import (  # noqa: F401
     F16, Q8_0, Q4_0, PaCudaError, LibraryMissing, Shape, Seg, Context, Plan, Engine, lib, lib_path,
-    head_bytes, shape_for, attn, attn_partial, merge, merge_gathered, packed_views, normalize, scale_q, available,
+    head_bytes, shape_for, attn, attn_partial, merge, merge_gathered, packed_views, normalize, fold_reply, scale_q,
+    available,
 )
 from .formats import quantize_q8_0, quantize_q4_0, dequantize  # noqa: F401

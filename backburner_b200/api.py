@@ -73,6 +73,7 @@ _SIGS = {
                                               ctypes.c_int, _P]),
     "pa_cuda_normalize": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint64, _P, _P, _P, _P, _P, _P]),
     "pa_cuda_scale_q": (ctypes.c_int, [_P, _P, ctypes.c_float, ctypes.c_uint64, _P, _P]),
+    "pa_cuda_fold_reply": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint64, _P, _P, _P, _P, _P, _P]),
     "pa_cuda_alloc_page": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.POINTER(_Page)]),
     "pa_cuda_free_page": (None, [_P, ctypes.POINTER(_Page)]),
     "pa_cuda_begin": (ctypes.c_int, [_P, ctypes.POINTER(_Page), ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, _P,
@@ -348,6 +349,15 @@ def normalize(ctx: Context, hd: int, O, m, l, stream=None):
     ctx.check(lib().pa_cuda_normalize(ctx.handle, hd, rows, _ptr(O), _ptr(m), _ptr(l), _ptr(Oh), _ptr(lse),
                                       _stream_ptr(stream)), "normalize")
     return Oh, lse
+
+
+def fold_reply(ctx: Context, hd: int, Oh, lse, O, m, l, stream=None):
+    """Fold a normalised reply (f16 Oh [rows][hd], lse [rows]) into the unnormalised partial (O, m, l) in place, as
+    the co-attention slot O_unnorm = Oh, l = 1, m = lse (pa_cuda_fold_reply)."""
+    rows = lse.numel()
+    ctx.check(lib().pa_cuda_fold_reply(ctx.handle, hd, rows, _ptr(Oh), _ptr(lse), _ptr(O), _ptr(m), _ptr(l),
+                                       _stream_ptr(stream)), "fold_reply")
+    return O, m, l
 
 
 def scale_q(ctx: Context, Q, scale: float, stream=None):

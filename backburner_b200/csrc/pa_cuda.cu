@@ -829,6 +829,21 @@ int pa_cuda_normalize(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, const float 
     return PA_CUDA_OK;
 }
 
+int pa_cuda_fold_reply(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, const uint16_t *Oh, const float *lse, float *O,
+                       float *m, float *l, void *stream) {
+    if (!ctx) return PA_CUDA_EINVAL;
+    if (hd != 128 && hd != 256) return fail(ctx, PA_CUDA_EUNSUPPORTED, "hd must be 128 or 256");
+    if (rows == 0) return PA_CUDA_OK;
+    if (!Oh || !lse || !O || !m || !l) return fail(ctx, PA_CUDA_EINVAL, "null argument");
+    cudaSetDevice(ctx->device);
+    const unsigned blocks = (unsigned) ((rows + 7) / 8);
+    if (hd == 128) pa::mrg::fold_reply_kernel<128><<<blocks, 256, 0, pick(ctx, stream)>>>(Oh, lse, rows, O, m, l);
+    else pa::mrg::fold_reply_kernel<256><<<blocks, 256, 0, pick(ctx, stream)>>>(Oh, lse, rows, O, m, l);
+    PA_CK(cudaGetLastError(), "fold_reply launch");
+    ctx->launches++;
+    return PA_CUDA_OK;
+}
+
 // ------------------------------------------------------------------------------------------ pa::engine
 int pa_cuda_alloc_page(pa_cuda_ctx *ctx, size_t bytes, pa_cuda_page *pg) {
     if (!ctx || !pg) return PA_CUDA_EINVAL;

@@ -105,6 +105,37 @@ __global__ void __launch_bounds__(256) normalize_kernel(const float *O, const fl
     if (lane == 0) lse[r] = l > 0.f ? M[r] + logf(l) : -INFINITY;
 }
 
+// The host's co-attention fold of a normalised reply (phone-attn/phone-attn.h:18-20: "O_unnorm = O, S = 1, M = lse"):
+// the reply row (f16 O = O/l, lse = m + log l) is the part (O, m = lse, l = 1), merged into the unnormalised partial
+// already in (O, M, L) by merge_partial's rule (phone-attn/phone-attn.h:231-239): a reply with lse = -inf (no keys)
+// adds nothing; a partial with L <= 0 is replaced. One warp per row.
+template <int HD>
+__global__ void __launch_bounds__(256) fold_reply_kernel(const uint16_t *Oh, const float *lse, uint64_t n_rows, float *O,
+                                                         float *M, float *L) {
+    constexpr int V = HD / 32;
+    const uint64_t r = (uint64_t) blockIdx.x * 8 + threadIdx.x / 32;
+    const uint32_t lane = threadIdx.x % 32;
+    if (r >= n_rows) return;
+    const float mr = lse[r];
+    if (!(mr > -INFINITY)) return;
+    const float m_in = M[r], l_in = L[r];
+    const bool keep = l_in > 0.f;
+    const float Mx = keep ? fmaxf(m_in, mr) : mr;
+    const float a = keep ? ex2((m_in - Mx) * LOG2E) : 0.f, b = ex2((mr - Mx) * LOG2E);
+    float *o = O + r * HD + lane * V;
+    const uint16_t *h = Oh + r * HD + lane * V;
+#pragma unroll
+    for (int i = 0; i < V; i++) {
+        const float x = __half2float(__ushort_as_half(h[i]));
+        o[i] = keep ? fmaf(o[i], a, x * b) : x * b;
+    }
+    __syncwarp();
+    if (lane == 0) {
+        M[r] = Mx;
+        L[r] = keep ? fmaf(l_in, a, b) : b;
+    }
+}
+
 // f16(q * scale) for n fp32 values (scripts/sme/sme_attn.c:276-280; phone-attn/phone-attn.h:595-599)
 __global__ void scale_q_kernel(const float *Q, float scale, uint64_t n, uint16_t *Qs) {
     for (uint64_t i = (uint64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t) gridDim.x * blockDim.x)

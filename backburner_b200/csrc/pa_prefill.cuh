@@ -145,6 +145,25 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
     return r;
 }
 
+// 2^t0, 2^t1 on the FMA pipe (relieves the MUFU unit, which the softmax's exp2 keeps busy): t = n + f with n = rint(t)
+// by the 1.5 * 2^23 addition trick, 2^f on [-0.5, 0.5] by a degree-3 polynomial least-squares fitted for this kernel
+// (max relative error 7.5e-5, below P's f16 rounding), and n added to the result's exponent field by one integer
+// multiply-add. Inputs below -125 give 2^-125 (P rounds to 0 in f16, and the row sum changes by < 1e-37).
+__device__ __forceinline__ void ex2_pair_fma(float t0, float t1, float &p0, float &p1) {
+    const uint64_t xa = pack_f2(fmaxf(t0, -125.f), fmaxf(t1, -125.f));
+    const uint64_t tt = add_f2(xa, pack_f2(12582912.f, 12582912.f));
+    float r0, r1, u0, u1;
+    unpack_f2(add_f2(tt, pack_f2(-12582912.f, -12582912.f)), r0, r1);
+    const uint64_t fv = add_f2(xa, pack_f2(-r0, -r1));
+    uint64_t pp = fma_f2(pack_f2(0.0551716648f, 0.0551716648f), fv, pack_f2(0.2426111251f, 0.2426111251f));
+    pp = fma_f2(pp, fv, pack_f2(0.6932609677f, 0.6932609677f));
+    pp = fma_f2(pp, fv, pack_f2(0.9999280572f, 0.9999280572f));
+    unpack_f2(pp, u0, u1);
+    unpack_f2(tt, r0, r1);
+    p0 = __uint_as_float(__float_as_uint(r0) * 0x800000u + __float_as_uint(u0));
+    p1 = __uint_as_float(__float_as_uint(r1) * 0x800000u + __float_as_uint(u1));
+}
+
 __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }

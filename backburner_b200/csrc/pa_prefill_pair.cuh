@@ -354,7 +354,10 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
             for (int i = 0; i < 32; i++) {
                 float t0, t1;
                 unpack_f2(fma_f2(pack_f2(s[2 * i], s[2 * i + 1]), l2e2, nm2), t0, t1);
-                const float p0 = ex2(t0), p1 = ex2(t1);
+                // every 4th pair on the FMA pipe, the rest on MUFU (measured: +3-5% over MUFU alone; every 2nd: -2%)
+                float p0, p1;
+                if (i % 4 == 3) ex2_pair_fma(t0, t1, p0, p1);
+                else { p0 = ex2(t0); p1 = ex2(t1); }
                 const uint64_t pp = pack_f2(p0, p1);
                 acc = add_f2(acc, pp);
                 ph[i] = pack_h2(p0, p1);

@@ -12,6 +12,7 @@
  *                          merge_partial                  phone-attn/phone-attn.h:231-239
  *   pa_cuda_merge_gathered the multi-phone merge           docs/TWO-PHONES.md:14-18 (host loop in the absent llama.cpp)
  *   pa_cuda_normalize      attn_core's O/l, lse           phone-attn/phone-attn.h:651-655
+ *   pa_cuda_fold_reply     co-attention slot of a reply   phone-attn/phone-attn.h:18-20 (host merge in the absent llama.cpp)
  *   pa_cuda_scale_q        f16(q * scale)                 phone-attn/phone-attn.h:595-599, scripts/sme/sme_attn.c:276-280
  *   pa_cuda_alloc_page,
  *   pa_cuda_free_page,
@@ -149,6 +150,12 @@ int pa_cuda_merge_gathered(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, uint32_
 /* O/l -> f16 Oh, lse = m + log l (device) */
 int pa_cuda_normalize(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, const float *O, const float *m, const float *l,
                       uint16_t *Oh, float *lse, void *stream);
+/* The host's co-attention fold (phone-attn/phone-attn.h:18-20): a normalised reply row (f16 Oh = O/l, lse = m + log l,
+ * as ATTN returns it) is re-expanded as the part (O = Oh, m = lse, l = 1) and merged into the unnormalised partial in
+ * (O, m, l) with merge_partial's rule (phone-attn/phone-attn.h:231-239): rows with lse = -inf add nothing, rows whose
+ * l <= 0 take the reply. Device pointers; Oh [rows][hd], lse [rows]. */
+int pa_cuda_fold_reply(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, const uint16_t *Oh, const float *lse, float *O,
+                       float *m, float *l, void *stream);
 /* Qs = f16(Q * scale) for n values (device) */
 int pa_cuda_scale_q(pa_cuda_ctx *ctx, const float *Q, float scale, uint64_t n, uint16_t *Qs, void *stream);
 

@@ -226,6 +226,22 @@ def normalize(O, m, l):
     return Oh, lse
 
 
+def reexpand(Oh, lse):
+    """A normalised reply row as the host's co-attention slot (phone-attn.h:18-20: "O_unnorm = O, S = 1, M = lse"):
+    (O = f32(Oh), m = lse, l = 1), or l = 0 for a reply with no keys (lse = -inf)."""
+    lse = np.ascontiguousarray(lse, np.float32)
+    O = h2f(np.ascontiguousarray(Oh, np.uint16)).astype(np.float32)
+    l = np.where(lse > -np.inf, 1.0, 0.0).astype(np.float32)
+    return O, lse.copy(), l
+
+
+def fold_reply(O, m, l, Oh, lse):
+    """The host's fold of a normalised reply into its unnormalised partial (O, m, l), in place: merge_partial
+    (phone-attn.h:231-239) of the re-expanded reply."""
+    O2, m2, l2 = reexpand(Oh, lse)
+    merge_partial(O, m, l, O2.reshape(O.shape), m2.reshape(m.shape), l2.reshape(l.shape))
+
+
 # ------------------------------------------------------------------ synthetic inputs (BASELINE configs)
 def gen_case(seed: int, hd: int, nkv: int, rows: int, nk: int, quant=Q8_0, outliers: int = 4, student_t: bool = False,
              scale: float | None = None):

@@ -222,6 +222,43 @@ def test_normalize_matches_attn_core(ctx):
     np.testing.assert_allclose(lse.cpu().numpy(), lser, rtol=1e-6, atol=1e-6)
 
 
+def test_fold_reply_matches_oracle(ctx):
+    """pa_cuda_fold_reply: the engine's partial over the offloaded keys goes out normalised (ATTN's reply: f16 O/l,
+    lse) and is folded into the host's own unnormalised partial as O_unnorm = O, l = 1, m = lse
+    (phone-attn.h:18-20). Checked against the oracle's fold of the same reply bits, and the folded result against
+    the oracle over all keys at the 2e-3 gate; rows with an empty reply or an empty host partial included."""
+    import torch
+    c = orc.gen_case(4321, 128, 8, 40, 6000, orc.Q8_0)
+    sh = c["shape"]
+    na = 5000
+    shape = pa.shape_for(128, 8, 40, pa.Q8_0)
+    K, V = _dev(c["K"][:na]), _dev(c["V"][:na])
+    Qs = _dev(c["Qs"].view(np.int16)).view(torch.float16)
+    O, m, l = pa.attn(ctx, shape, Qs, [pa.Seg(K.data_ptr(), V.data_ptr(), na, 0)])
+    Oh, lse = pa.normalize(ctx, 128, O.reshape(-1, 128), m.reshape(-1), l.reshape(-1))
+    lse[7] = -float("inf")                                    # an empty reply row
+    OB, mB, lB = orc.partial_f32(sh, c["Qs"], c["K"][na:], c["V"][na:], 6000 - na)
+    lB = lB.copy()
+    lB.reshape(-1)[11] = 0.0                                  # an empty host row
+    Od, md, ld = _dev(OB.reshape(-1, 128)), _dev(mB.reshape(-1)), _dev(lB.reshape(-1))
+    pa.fold_reply(ctx, 128, Oh, lse, Od, md, ld)
+    ctx.status()
+    Oh_h, lse_h = Oh.cpu().numpy().view(np.uint16), lse.cpu().numpy()
+    Or, mr, lr = OB.reshape(-1, 128).copy(), mB.reshape(-1).copy(), lB.reshape(-1).copy()
+    orc.fold_reply(Or, mr, lr, Oh_h, lse_h)
+    np.testing.assert_allclose(Od.cpu().numpy(), Or, rtol=2e-5, atol=2e-6)
+    np.testing.assert_allclose(md.cpu().numpy(), mr, rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(ld.cpu().numpy(), lr, rtol=2e-5)
+    # the folded partial against the oracle over all keys (rows without an empty side)
+    Oa, ma, la = orc.partial_f32(sh, c["Qs"], c["K"], c["V"], 6000)
+    keep = np.ones(8 * 40, bool)
+    keep[[7, 11]] = False
+    got = (Od.cpu().numpy()[keep], md.cpu().numpy()[keep], ld.cpu().numpy()[keep])
+    e = orc.rel_err(*got, Oa.reshape(-1, 128)[keep].astype(np.float64), ma.reshape(-1)[keep].astype(np.float64),
+                    la.reshape(-1)[keep].astype(np.float64))
+    assert e[0] <= TOL_REF and e[1] <= TOL_REF, e
+
+
 @pytest.mark.parametrize("quant,ntok,ng", [(orc.Q8_0, 8, 1), (orc.Q8_0, 1, 1), (orc.Q8_0, 3, 1), (orc.Q4_0, 8, 1),
                                            (orc.Q8_0, 8, 3)])
 def test_engine_pages_begin_end(ctx, quant, ntok, ng):

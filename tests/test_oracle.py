@@ -112,6 +112,37 @@ def test_empty_partial_and_merge_conventions():
     assert np.all(Oh == 0) and np.all(np.isneginf(lse))
 
 
+def test_reply_fold_equals_merging_the_partials():
+    """The host's co-attention fold of a normalised reply (phone-attn.h:18-20: O_unnorm = O, S = 1, M = lse) gives the
+    merge of the unnormalised partials (phone-attn.h:231-239), up to the reply's f16 rounding of O/l; a reply with no
+    keys (lse = -inf) leaves the host's partial as it is, and a host row with no keys takes the reply."""
+    c = orc.gen_case(808, 128, 2, 10, 3000, orc.Q8_0)
+    sh = c["shape"]
+    na = 1900
+    OA, mA, lA = orc.partial_f32(sh, c["Qs"], c["K"][:na], c["V"][:na], na)
+    OB, mB, lB = orc.partial_f32(sh, c["Qs"], c["K"][na:], c["V"][na:], 3000 - na)
+    O1, m1, l1 = OB.copy(), mB.copy(), lB.copy()
+    orc.merge_partial(O1, m1, l1, OA, mA, lA)
+    Oh, lse = orc.normalize(OA, mA, lA)
+    lse = lse.reshape(mA.shape)
+    lse[0, 3] = -np.inf                     # the reply has no keys for this row
+    O2, m2, l2 = OB.copy(), mB.copy(), lB.copy()
+    l2[1, 4] = 0.0                          # the host has none for this one
+    orc.fold_reply(O2, m2, l2, Oh.reshape(OA.shape), lse)
+    Oh1, lse1 = orc.normalize(O1, m1, l1)
+    Oh2, lse2 = orc.normalize(O2, m2, l2)
+    Oh1, Oh2 = orc.h2f(Oh1).reshape(OA.shape), orc.h2f(Oh2).reshape(OA.shape)
+    lse1, lse2 = lse1.reshape(mA.shape), lse2.reshape(mA.shape)
+    ok = np.ones(mA.shape, bool)
+    ok[0, 3] = ok[1, 4] = False
+    assert np.abs(Oh2 - Oh1)[ok].max() <= 1e-3 * np.abs(Oh1).max()
+    assert np.abs(lse2 - lse1)[ok].max() <= 1e-5 * np.abs(lse1).max()
+    OBh, lseB = orc.normalize(OB, mB, lB)
+    assert np.array_equal(Oh2[0, 3], orc.h2f(OBh).reshape(OA.shape)[0, 3]) and lse2[0, 3] == lseB.reshape(mA.shape)[0, 3]
+    assert np.allclose(Oh2[1, 4], orc.h2f(Oh).reshape(OA.shape)[1, 4], rtol=1e-3, atol=1e-4)
+    assert abs(lse2[1, 4] - lse[1, 4]) <= 1e-6
+
+
 def test_merge_slots_equals_whole():
     c = orc.gen_case(11, 128, 8, 5, 3000, orc.Q8_0)
     sh = c["shape"]
