@@ -94,6 +94,14 @@ class ClockSampler:
         self.device = device
         self.proc = None
         self.path = None
+        self.skip = 0
+
+    def _lines(self) -> int:
+        try:
+            with open(self.path) as f:
+                return sum(1 for _ in f)
+        except Exception:
+            return 0
 
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(suffix=".csv")
@@ -104,10 +112,19 @@ class ClockSampler:
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+        # nvidia-smi takes a few hundred ms to start: wait for its first sample, so that a short timed region (an
+        # 8-GPU run's is ~0.15 s) is sampled too, and count only the samples taken from here on
+        t0 = time.time()
+        while self.proc and self._lines() == 0 and time.time() - t0 < 3.0:
+            time.sleep(0.02)
+        self.skip = self._lines()
         return self
 
     def __exit__(self, *a):
         if self.proc:
+            t0 = time.time()
+            while self._lines() <= self.skip and time.time() - t0 < 0.5:   # at least one sample of the region
+                time.sleep(0.02)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -117,9 +134,9 @@ class ClockSampler:
     def summary(self):
         rows = []
         try:
-            for line in open(self.path):
+            for i, line in enumerate(open(self.path)):
                 parts = [x.strip() for x in line.split(",")]
-                if len(parts) >= 9:
+                if i >= self.skip and len(parts) >= 9:
                     rows.append(parts)
         except Exception:
             pass
