@@ -181,23 +181,24 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 // quantised rows of one segment as a 2-D u8 tensor {rs bytes, nk keys}; a box is one head's 16-byte-aligned window
+// (16-bit elements: a 272-byte hd-256 window is 136 elements, within TMA's 256-element box limit; rs % 16 == 0)
 bool map_rows(CUtensorMap *m, const void *base, uint64_t rs, uint32_t nk, uint32_t raw_bytes, uint32_t box_keys) {
     auto fn = encode_fn();
     if (!fn) return false;
-    const cuuint64_t dims[2] = {rs, nk};
+    const cuuint64_t dims[2] = {rs / 2, nk};
     const cuuint64_t strides[1] = {rs};
-    const cuuint32_t box[2] = {raw_bytes, box_keys};
+    const cuuint32_t box[2] = {raw_bytes / 2, box_keys};
     const cuuint32_t estr[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void *>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
-// Qs [all rows][128] f16 with the 128-byte swizzle of the UMMA operand layout; a box is 64 dims x 128 rows
-bool map_q(CUtensorMap *m, const void *Qs, uint64_t n_rows) {
+// Qs [all rows][hd] f16 with the 128-byte swizzle of the UMMA operand layout; a box is 64 dims x 128 rows
+bool map_q(CUtensorMap *m, const void *Qs, uint64_t n_rows, uint32_t hd) {
     auto fn = encode_fn();
     if (!fn) return false;
-    const cuuint64_t dims[2] = {128, n_rows};
-    const cuuint64_t strides[1] = {256};
+    const cuuint64_t dims[2] = {hd, n_rows};
+    const cuuint64_t strides[1] = {(cuuint64_t) hd * 2};
     const cuuint32_t box[2] = {64, (cuuint32_t) pa::pre::BM};
     const cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(Qs), dims, strides, box, estr,
@@ -216,10 +217,11 @@ cudaError_t launch_prefill(const pa_cuda_plan *p, const CUtensorMap &tq, const p
     return cudaGetLastError();
 }
 // the CTA-pair kernel: clusters of 2 CTAs along x, one cluster per job
-template <int Q, int NT>
+template <int Q, int NT, int D>
 cudaError_t launch_prefill_pair(const pa_cuda_plan *p, const CUtensorMap &tq, const pa::pre::Params &prm, cudaStream_t st) {
-    auto kern = pa::pre::prefill_pair_kernel<Q, NT>;
-    constexpr int smem = pa::pre::PairSmem<Q, NT>::TOTAL + 1024;
+    auto kern = pa::pre::prefill_pair_kernel<Q, NT, D>;
+    constexpr int smem = pa::pre::PairSmem<Q, NT, D>::TOTAL + 1024;
+    static_assert(smem <= 227 * 1024, "shared memory of a CTA");
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
@@ -286,7 +288,7 @@ int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, 
     const pa_cuda_shape &sh = p->sh;
     if (p->n_jobs > 0 && p->prefill) {
         CUtensorMap tq;
-        if (!map_q(&tq, Qs, (uint64_t) p->n_sets * sh.nkv * sh.rows))
+        if (!map_q(&tq, Qs, (uint64_t) p->n_sets * sh.nkv * sh.rows, sh.hd))
             return fail(ctx, PA_CUDA_ECUDA, "cuTensorMapEncodeTiled (Q) failed");
         pa::pre::Params prm{};
         prm.jobs = p->d_jobs;
@@ -304,11 +306,14 @@ int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, 
         const bool prof = p->profile && p->ev_used + 2 <= p->ev.size();
         if (prof) cudaEventRecord(p->ev[p->ev_used], st);
         cudaError_t e;
-        if (p->pair) {
+        if (p->pair && sh.hd == 256) {
+            e = sh.quant == PA_CUDA_Q8_0 ? launch_prefill_pair<1, 1, 256>(p, tq, prm, st)
+                                         : launch_prefill_pair<2, 1, 256>(p, tq, prm, st);
+        } else if (p->pair) {
             if (sh.quant == PA_CUDA_Q8_0)
-                e = p->nt == 2 ? launch_prefill_pair<1, 2>(p, tq, prm, st) : launch_prefill_pair<1, 1>(p, tq, prm, st);
+                e = p->nt == 2 ? launch_prefill_pair<1, 2, 128>(p, tq, prm, st) : launch_prefill_pair<1, 1, 128>(p, tq, prm, st);
             else
-                e = p->nt == 2 ? launch_prefill_pair<2, 2>(p, tq, prm, st) : launch_prefill_pair<2, 1>(p, tq, prm, st);
+                e = p->nt == 2 ? launch_prefill_pair<2, 2, 128>(p, tq, prm, st) : launch_prefill_pair<2, 1, 128>(p, tq, prm, st);
         } else if (sh.quant == PA_CUDA_Q8_0) {
             e = p->nt == 2 ? launch_prefill<1, 2>(p, tq, prm, st) : launch_prefill<1, 1>(p, tq, prm, st);
         } else {
@@ -503,19 +508,22 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
     if ((rc = plan_decode_shape(ctx, p))) { delete p; return rc; }
     // the tcgen05 kernel takes calls with many query rows per KV head (prefill, ATTN_BIG, long verify batches), the
     // split-K kernel the decode-sized ones (as the reference engine switches kernels by rows, pa-metal.mm:818-835)
-    const bool tc_ok = shape->hd == 128 && shape->quant != PA_CUDA_F16 && encode_fn() != nullptr;
+    // (hd 256, the reference server's wire geometry, runs on the CTA-pair kernel only)
+    const bool tc_ok = (shape->hd == 128 || (shape->hd == 256 && ctx->kernel_choice != 2)) &&
+                       shape->quant != PA_CUDA_F16 && encode_fn() != nullptr;
     p->prefill = tc_ok && (ctx->kernel_choice >= 2 || (ctx->kernel_choice == 0 && shape->rows >= kPrefillMinRows));
     if (ctx->kernel_choice >= 2 && !tc_ok) {
         delete p;
-        return fail(ctx, PA_CUDA_EUNSUPPORTED, "tcgen05 kernel needs hd 128 and quantised (Q8_0 / Q4_0) rows");
+        return fail(ctx, PA_CUDA_EUNSUPPORTED,
+                    "tcgen05 kernels need quantised (Q8_0 / Q4_0) rows and hd 128 (single CTA) or 128 / 256 (CTA pairs)");
     }
     if (p->prefill) {
         // PA_CUDA_TC_TILES=1|2: Q tiles of 128 rows per CTA (default: 2 when there are more than 128 rows)
         static const int tiles_env = getenv("PA_CUDA_TC_TILES") ? atoi(getenv("PA_CUDA_TC_TILES")) : 0;
         // CTA pairs (2-SM MMAs, half of each K/V block dequantised per SM) from kPairMinRows rows per KV head
-        p->pair = ctx->kernel_choice == 3 || (ctx->kernel_choice == 0 && shape->rows >= kPairMinRows);
+        p->pair = shape->hd == 256 || ctx->kernel_choice == 3 || (ctx->kernel_choice == 0 && shape->rows >= kPairMinRows);
         const uint32_t tile_rows = (uint32_t) pa::pre::BM * (p->pair ? 2u : 1u);
-        p->nt = (tiles_env == 1 || tiles_env == 2) ? tiles_env : (shape->rows > tile_rows ? 2 : 1);
+        p->nt = shape->hd == 256 ? 1 : (tiles_env == 1 || tiles_env == 2) ? tiles_env : (shape->rows > tile_rows ? 2 : 1);
         p->n_rt = (shape->rows + tile_rows * p->nt - 1) / (tile_rows * p->nt);
         p->grid_y = shape->nkv * p->n_rt;
     }
@@ -601,7 +609,7 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
         e = cudaMemcpy(p->d_crange, crange.data(), crange.size() * 4, cudaMemcpyHostToDevice);
     if (e == cudaSuccess && p->prefill && n_segs) {
         std::vector<CUtensorMap> maps(2 * (size_t) n_segs);
-        const uint32_t rawb = (uint32_t) pa::pre::raw_row_bytes((int) shape->quant);
+        const uint32_t rawb = (uint32_t) pa::pre::raw_row_bytes((int) shape->quant, (int) shape->hd);
         for (uint32_t i = 0; i < n_segs; i++) {
             if (!segs[i].nk) continue;
             // a CTA of a pair loads half of each block's K rows and all of its V rows
@@ -631,12 +639,14 @@ const char *pa_cuda_plan_kernel(const pa_cuda_plan *p) {
     if (!p) return "";
     const uint32_t q = p->sh.quant;
     if (p->prefill) {
-        static const char *names[2][2][2] = {
+        static const char *names[3][2][2] = {
             {{"pa::pre::prefill_kernel<1,1>", "pa::pre::prefill_kernel<1,2>"},
              {"pa::pre::prefill_kernel<2,1>", "pa::pre::prefill_kernel<2,2>"}},
-            {{"pa::pre::prefill_pair_kernel<1,1>", "pa::pre::prefill_pair_kernel<1,2>"},
-             {"pa::pre::prefill_pair_kernel<2,1>", "pa::pre::prefill_pair_kernel<2,2>"}}};
-        return names[p->pair ? 1 : 0][q == PA_CUDA_Q8_0 ? 0 : 1][p->nt == 2 ? 1 : 0];
+            {{"pa::pre::prefill_pair_kernel<1,1,128>", "pa::pre::prefill_pair_kernel<1,2,128>"},
+             {"pa::pre::prefill_pair_kernel<2,1,128>", "pa::pre::prefill_pair_kernel<2,2,128>"}},
+            {{"pa::pre::prefill_pair_kernel<1,1,256>", "pa::pre::prefill_pair_kernel<1,1,256>"},
+             {"pa::pre::prefill_pair_kernel<2,1,256>", "pa::pre::prefill_pair_kernel<2,1,256>"}}};
+        return names[!p->pair ? 0 : p->sh.hd == 256 ? 2 : 1][q == PA_CUDA_Q8_0 ? 0 : 1][p->nt == 2 ? 1 : 0];
     }
     static const char *dec[2][3] = {{"pa::dec::decode_kernel<128,0>", "pa::dec::decode_kernel<128,1>", "pa::dec::decode_kernel<128,2>"},
                                     {"pa::dec::decode_kernel<256,0>", "pa::dec::decode_kernel<256,1>", "pa::dec::decode_kernel<256,2>"}};

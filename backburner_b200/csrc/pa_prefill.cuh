@@ -35,11 +35,17 @@ constexpr int BM = 128;   // query rows per tile = TMEM lanes
 constexpr int BN = 64;    // keys per block
 constexpr int NS = 3;     // raw stages
 
-__host__ __device__ constexpr int raw_row_bytes(int quant) { return quant == 1 ? 144 : 80; }   // 16-aligned window
+// bytes of the 16-byte-aligned window that holds one head of a key row: the head (hd/32 blocks of 34 B for Q8_0, 18 B
+// for Q4_0) plus its offset inside the window (head h starts at h * hb: offset 0 or 8 when hb % 16 == 8, else 0),
+// rounded up to 16 (hd 128: 144 / 80; hd 256: 272 / 144)
+__host__ __device__ constexpr int raw_row_bytes(int quant, int hd = 128) {
+    return ((hd / 32) * (quant == 1 ? 34 : 18) + (((hd / 32) * (quant == 1 ? 34 : 18)) % 16 ? 8 : 0) + 15) / 16 * 16;
+}
 
 struct Params {
     const dec::Job *jobs;
-    const CUtensorMap *kv_maps;   // [2*seg] K rows, [2*seg+1] V rows: u8 {rs, nk}, box {raw_row_bytes, BN}
+    const CUtensorMap *kv_maps;   // [2*seg] K rows, [2*seg+1] V rows: 16-bit elements {rs/2, nk}, box {raw_row_bytes/2,
+                                  // keys per copy} (16-bit elements keep a 272-byte window within TMA's 256-element box)
     float *Op, *Mp, *Lp;          // slot partials [slot][nkv][rows][HD], [slot][nkv][rows]
     int *status;
     uint64_t rs, hb;
@@ -300,8 +306,8 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
                 if (j >= NS && !wait(&raw_empty[st], ((j / NS) - 1) & 1)) break;
                 mbar_arrive_expect_tx(&raw_full[st], 2 * BN * RAWB);
                 uint8_t *dst = smem + L::RAW + st * L::RAW_STAGE;
-                tma_2d(dst, km, hx, (int) (job.key0 + j * BN), &raw_full[st]);
-                tma_2d(dst + BN * RAWB, vm, hx, (int) (job.key0 + j * BN), &raw_full[st]);
+                tma_2d(dst, km, hx / 2, (int) (job.key0 + j * BN), &raw_full[st]);
+                tma_2d(dst + BN * RAWB, vm, hx / 2, (int) (job.key0 + j * BN), &raw_full[st]);
                 issued = j + 1;
             }
             // on an abort, every issued copy lands before the CTA exits

@@ -4,12 +4,13 @@
 //
 // Reference semantics: pa_attn_big (phone-attn/pa-metal.mm:379-487), as in pa_prefill.cuh: rows of all groups of one
 // KV head packed back to back, K/V dequantised to f16, S = Qs.K^T and O += P.V with fp32 accumulation, online softmax
-// over the valid keys, one unnormalised (O, m, l) per chunk of keys. Head dim 128.
+// over the valid keys, one unnormalised (O, m, l) per chunk of keys. Head dim D = 128 (NT = 1 or 2 pair tiles) or 256
+// (the reference server's wire geometry, phone-attn/phone-attn.h:79; NT = 1: TMEM holds NT x (64 + 64 + D) columns).
 //
 // One cluster of 2 CTAs = one chunk of keys of one segment x one KV head x NT pair tiles of 256 query rows; CTA r of
 // the pair holds rows [128 r, 128 r + 128) of each pair tile (its TMEM lanes), and of each 64-key block
-//   K: keys [32 r, 32 r + 32), all 128 dims (the N half of B for S = Q K^T, N = 64 keys)
-//   V: all 64 keys, dims [64 r, 64 r + 64) (the N half of B for O += P V, N = 128 dims)
+//   K: keys [32 r, 32 r + 32), all D dims (the N half of B for S = Q K^T, N = 64 keys)
+//   V: all 64 keys, dims [D r / 2, D (r + 1) / 2) (the N half of B for O += P V, N = D dims)
 // Warp roles in each CTA (as in pa_prefill.cuh):
 //   warp 0             TMA: its Q tiles once, then per block its raw K rows (32 keys) and V rows (64 keys)
 //   warps 1, 2, 3      warp 1 allocates TMEM (both CTAs, cta_group::2). In CTA 0 one thread of warp 1 issues the S
@@ -101,15 +102,18 @@ __device__ __forceinline__ void tc2_commit(uint64_t *bar) {
                  : "memory");
 }
 
-template <int QUANT, int NT>
+// shared-memory map of a CTA of the pair (operand tiles 1024-aligned); D = head dim (128 or 256)
+template <int QUANT, int NT, int D>
 struct PairSmem {
-    static constexpr int RAWB = raw_row_bytes(QUANT);
+    static constexpr int RAWB = raw_row_bytes(QUANT, D);
     static constexpr int KH = BN / 2;                              // keys of K per CTA per block
-    static constexpr int KVB = 4;                                  // dequantised K and V buffers (a ring)
-    static constexpr int Q = 0;                                   // NT x [2 atom cols][128 rows][128 B]
-    static constexpr int K_BUF = 2 * KH * 128;                     // [2 atom cols][32 keys][128 B]
-    static constexpr int V_BUF = BN * 128;                         // [64 keys][128 B] (this CTA's 64 dims)
-    static constexpr int K = Q + NT * BM * HD * 2;                 // KVB K buffers
+    static constexpr int KVB = D == 128 ? 4 : 2;                   // dequantised K and V buffers (a ring)
+    static constexpr int TS = 128 + D;                             // TMEM columns per pair tile: S 64, P 2 x 32, O D
+    static constexpr int TMEM_COLS = NT * TS <= 256 ? 256 : 512;   // allocation: a power of 2
+    static constexpr int Q = 0;                                   // NT x [D/64 atom cols][128 rows][128 B]
+    static constexpr int K_BUF = (D / 64) * KH * 128;              // [D/64 atom cols][32 keys][128 B]
+    static constexpr int V_BUF = (D / 128) * BN * 128;             // [D/128 atom cols][64 keys][128 B] (this CTA's D/2 dims)
+    static constexpr int K = Q + NT * BM * D * 2;                  // KVB K buffers
     static constexpr int V = K + KVB * K_BUF;                      // KVB V buffers
     static constexpr int RAW = V + KVB * V_BUF;                    // NS x (K rows [32][RAWB], V rows [64][RAWB])
     static constexpr int RAW_V = KH * RAWB;                        // V rows' offset inside a stage
@@ -119,14 +123,15 @@ struct PairSmem {
     static constexpr int TOTAL = BAR + N_BAR * 8 + 32;
 };
 
-template <int QUANT, int NT>
+template <int QUANT, int NT, int D>
 __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(const __grid_constant__ CUtensorMap tq,
                                                                             const Params p) {
-    using L = PairSmem<QUANT, NT>;
-    constexpr int RAWB = L::RAWB, KH = L::KH, KVB = L::KVB;
+    using L = PairSmem<QUANT, NT, D>;
+    static_assert((D == 128 && (NT == 1 || NT == 2)) || (D == 256 && NT == 1), "TMEM holds NT x (128 + D) columns");
+    constexpr int RAWB = L::RAWB, KH = L::KH, KVB = L::KVB, TS = L::TS;
     constexpr int GB = dec::q_group_bytes(QUANT);
     constexpr uint32_t IDESC_S = idesc_f16(2 * BM, BN, 0);
-    constexpr uint32_t IDESC_PV = idesc_f16(2 * BM, HD, 1);
+    constexpr uint32_t IDESC_PV = idesc_f16(2 * BM, D, 1);
     constexpr int SM0 = 4, DQ0 = 4 + 4 * NT;   // first softmax warp, first dequant warp
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -187,9 +192,9 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
     const uint32_t skip = ld_cluster_u32(mapa(smem_u32((const void *) abort_flag), 0));
     cluster_sync();
     if (skip) return;
-    if (warp == 1) {   // TMEM: per pair tile S 64 + P 2 x 32 + O 128 columns, the same columns in both CTAs
+    if (warp == 1) {   // TMEM: per pair tile S 64 + P 2 x 32 + O D columns, the same columns in both CTAs
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(256 * NT)
+                     "r"(L::TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
     }
@@ -223,10 +228,10 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
         // ------------------------------------------------ TMA producer (each CTA its own operands)
         if (lane == 0) {
             const int qrow = (int) (((uint64_t) job.set * p.nkv + h) * p.rows + row0 + cr * BM);
-            mbar_arrive_expect_tx(q_full, NT * BM * HD * 2);
+            mbar_arrive_expect_tx(q_full, NT * BM * D * 2);
             for (int t = 0; t < NT; t++)
-                for (int c = 0; c < 2; c++)
-                    tma_2d(smem + L::Q + t * BM * HD * 2 + c * BM * 128, &tq, c * 64, qrow + t * 2 * BM, q_full);
+                for (int c = 0; c < D / 64; c++)
+                    tma_2d(smem + L::Q + t * BM * D * 2 + c * BM * 128, &tq, c * 64, qrow + t * 2 * BM, q_full);
             const CUtensorMap *km = p.kv_maps + 2 * job.seg, *vm = km + 1;
             uint32_t issued = 0;
             for (uint32_t j = 0; j < nblk; j++) {
@@ -234,8 +239,8 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
                 if (j >= NS && !wait(&raw_empty[st], ((j / NS) - 1) & 1)) break;
                 mbar_arrive_expect_tx(&raw_full[st], (KH + BN) * RAWB);
                 uint8_t *dst = smem + L::RAW + st * L::RAW_STAGE;
-                tma_2d(dst, km, hx, (int) (job.key0 + j * BN + cr * KH), &raw_full[st]);
-                tma_2d(dst + L::RAW_V, vm, hx, (int) (job.key0 + j * BN), &raw_full[st]);
+                tma_2d(dst, km, hx / 2, (int) (job.key0 + j * BN + cr * KH), &raw_full[st]);
+                tma_2d(dst + L::RAW_V, vm, hx / 2, (int) (job.key0 + j * BN), &raw_full[st]);
                 issued = j + 1;
             }
             if (!ok) {
@@ -253,8 +258,8 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
             // warp 1 for pair tile 0, warp 3 for tile 1 (an MMA of this shape holds its issuing thread ~100 cycles, so
             // one thread per tile doubles the issue rate)
             const int t = warp == 1 ? 0 : 1;
-            const uint64_t dq = sdesc(sbase + L::Q + t * BM * HD * 2, 16, 1024), dk0 = sdesc(sbase + L::K, 16, 1024);
-            const uint32_t d = tmem + t * 256;
+            const uint64_t dq = sdesc(sbase + L::Q + t * BM * D * 2, 16, 1024), dk0 = sdesc(sbase + L::K, 16, 1024);
+            const uint32_t d = tmem + t * TS;
             if (wait(q_full, 0) && wait_cl(q_pair, 0)) {
                 for (uint32_t j = 0; j < nblk && ok; j++) {
                     const uint32_t b = j % KVB;
@@ -263,7 +268,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
                     tc_fence_after();
                     const uint64_t dk = dk0 + b * (uint32_t) (L::K_BUF / 16);
 #pragma unroll
-                    for (int kk = 0; kk < HD / 16; kk++)
+                    for (int kk = 0; kk < D / 16; kk++)
                         tc2_mma(d, dq + (uint32_t) (((kk / 4) * BM * 128 + (kk % 4) * 32) / 16),
                                 dk + (uint32_t) (((kk / 4) * KH * 128 + (kk % 4) * 32) / 16), IDESC_S, kk > 0 ? 1u : 0u);
                     tc2_commit(&s_full[t]);
@@ -271,8 +276,9 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
                 }
             }
         } else if (cr == 0 && lane == 0) {
-            // ------------------------------------------------ O += P V issuer (M = 256, N = 128 dims, A = P in TMEM)
-            const uint64_t dv0 = sdesc(sbase + L::V, L::V_BUF, 1024);
+            // ------------------------------------------------ O += P V issuer (M = 256, N = D dims, A = P in TMEM; B:
+            // this CTA's D/2 dims, D/128 atom columns of 64 keys x 128 B apart)
+            const uint64_t dv0 = sdesc(sbase + L::V, BN * 128, 1024);
             for (uint32_t jj = 0; jj < nblk && ok; jj++) {
                 const uint32_t vb = jj % KVB, b = jj & 1;   // V buffer, P buffer
                 if (!wait_cl(&v_full[vb], (jj / KVB) & 1)) break;
@@ -281,8 +287,8 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
                 for (int t = 0; t < NT; t++) {
                     if (!wait_cl(&p_full[2 * t + b], (jj >> 1) & 1)) break;
                     tc_fence_after();
-                    const uint32_t d = tmem + t * 256 + 128;
-                    const uint32_t pa = tmem + t * 256 + BN + b * (BN / 2);
+                    const uint32_t d = tmem + t * TS + 128;
+                    const uint32_t pa = tmem + t * TS + BN + b * (BN / 2);
 #pragma unroll
                     for (int ks = 0; ks < BN / 16; ks++)
                         tc2_mma_ts(d, pa + ks * 8, dv + (uint32_t) (ks * 2048 / 16), IDESC_PV, (jj > 0 || ks > 0) ? 1u : 0u);
@@ -310,7 +316,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
         const int t = (int) (warp - SM0) / 4;
         const uint32_t wq = warp % 4;
         const uint32_t r = wq * 32 + lane;
-        const uint32_t tl = tmem + ((wq * 32) << 16) + t * 256;
+        const uint32_t tl = tmem + ((wq * 32) << 16) + t * TS;
         float m_used = -INFINITY, l = 0.f;
         for (uint32_t j = 0; j < nblk; j++) {
             const uint32_t b = j & 1;
@@ -372,7 +378,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
                 if (!wait(&pv_free[2 * t + (b ^ 1)], ((j - 1) >> 1) & 1)) break;
                 tc_fence_after();
 #pragma unroll
-                for (int q = 0; q < HD / 32; q++) {
+                for (int q = 0; q < D / 32; q++) {
                     float o[32];
                     tmem_ld32(tl + 128 + q * 32, o);
                     tmem_wait_ld();
@@ -394,12 +400,12 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
             const uint32_t row = row0 + t * 2 * BM + cr * BM + r;
             const uint64_t orow = ((uint64_t) job.slot * p.nkv + h) * p.rows + row;
 #pragma unroll
-            for (int q = 0; q < HD / 32; q++) {
+            for (int q = 0; q < D / 32; q++) {
                 float o[32];
                 tmem_ld32(tl + 128 + q * 32, o);
                 tmem_wait_ld();
                 if (row < p.rows) {
-                    float4 *dst = reinterpret_cast<float4 *>(p.Op + orow * HD + q * 32);
+                    float4 *dst = reinterpret_cast<float4 *>(p.Op + orow * D + q * 32);
 #pragma unroll
                     for (int i = 0; i < 8; i++) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
                 }
@@ -410,9 +416,11 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
             }
         }
     } else {
-        // ------------------------------------------------ dequantisers: one (key, quant block) per lane per operand
-        //   K: warp dw = quant block dw of this CTA's 32 keys (lane = key)
-        //   V: warp dw = quant block 2 cr + (dw & 1) (this CTA's dims) of keys 32 (dw >> 1) + lane
+        // ------------------------------------------------ dequantisers: (key, quant block) items, one per lane and pass
+        //   K: 32 keys x D/32 blocks; pass ps, warp dw: block dw + 4 ps of key `lane`
+        //   V: 64 keys x D/64 blocks (this CTA's dims: blocks cr D/64 ..); pass ps, warp dw: block cr D/64 +
+        //      (dw & 1) + 2 ps of key 32 (dw >> 1) + lane
+        // (D = 128: one pass of each; D = 256: two)
         if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 80;");
         const uint32_t dw = warp - DQ0;
         for (uint32_t j = 0; j < nblk; j++) {
@@ -422,19 +430,22 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
 #pragma unroll
             for (int kv = 0; kv < 2; kv++) {
                 if (j >= KVB && !wait(kv == 0 ? &k_free[b] : &v_free[b], ((j / KVB) - 1) & 1)) break;
-                const uint32_t qb = kv == 0 ? dw : 2 * cr + (dw & 1);            // quant block of the head
-                const uint32_t key = kv == 0 ? lane : (dw >> 1) * 32 + lane;      // key row in the raw stage
+#pragma unroll
+              for (int ps = 0; ps < D / 128; ps++) {
+                const uint32_t ql = kv == 0 ? dw + 4 * ps : (dw & 1) + 2 * ps;          // block within the tile
+                const uint32_t qb = kv == 0 ? ql : cr * (D / 64) + ql;                   // block of the head
+                const uint32_t key = kv == 0 ? lane : (dw >> 1) * 32 + lane;             // key row in the raw stage
                 const uint32_t rb = raw + (kv == 0 ? 0u : (uint32_t) L::RAW_V) + key * RAWB;
                 const uint32_t bo = hoff + GB * qb;
                 const uint32_t w16 = bo & ~15u;
                 const uint32_t ds = bo + 2;
                 const uint32_t w0 = (ds - w16) / 4, shift = 8 * (ds % 4);
-                // destination: K [2 atom cols (dims 64 c ..)][32 keys][128 B], V [64 keys][128 B]; 16-byte chunk
-                // (4 (qb % 2) + cc) of the key's 128-byte row, swizzled by key % 8
-                const uint32_t dst = kv == 0 ? sbase + L::K + b * L::K_BUF + (qb / 2) * KH * 128
-                                             : sbase + L::V + b * L::V_BUF;
+                // destination: K [D/64 atom cols][32 keys][128 B], V [D/128 atom cols][64 keys][128 B] (atom column
+                // = 64 dims = 2 blocks); 16-byte chunk (4 (ql % 2) + cc) of the key's 128-byte row, swizzled by key % 8
+                const uint32_t dst = kv == 0 ? sbase + L::K + b * L::K_BUF + (ql / 2) * KH * 128
+                                             : sbase + L::V + b * L::V_BUF + (ql / 2) * BN * 128;
                 const uint32_t kbase = dst + (key / 8) * 1024 + (key % 8) * 128;
-                const uint32_t c0 = 4 * (qb % 2);
+                const uint32_t c0 = 4 * (ql % 2);
                 const uint32_t s2 = lds16(rb + bo);
                 const uint32_t sc2 = s2 | (s2 << 16);
                 uint32_t W[12];
@@ -460,11 +471,11 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
                         sts128(kbase + (((c0 + cc) ^ (key % 8)) * 16), h0, h1, h2, h3);
                     }
                 } else {
-                    uint32_t D[4];
+                    uint32_t Dw[4];
                     switch (w0) {
 #define PA_ALIGN4(W0)                                                                        \
     case W0:                                                                                 \
-        _Pragma("unroll") for (int i = 0; i < 4; i++) D[i] = __funnelshift_r(W[W0 + i], W[W0 + i + 1], shift); \
+        _Pragma("unroll") for (int i = 0; i < 4; i++) Dw[i] = __funnelshift_r(W[W0 + i], W[W0 + i + 1], shift); \
         break;
                         PA_ALIGN4(0) PA_ALIGN4(1) PA_ALIGN4(2) PA_ALIGN4(3) default: PA_ALIGN4(4)
 #undef PA_ALIGN4
@@ -473,7 +484,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
                     const uint32_t m = 0x000F000Fu, magic = 0x64006400u, off8 = 0x64086408u;
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
-                        const uint32_t y = prmt(D[i], D[i], 0x3120u);
+                        const uint32_t y = prmt(Dw[i], Dw[i], 0x3120u);
                         lo[2 * i] = hmul2(hsub2(and_or(y, m, magic), off8), sc2);
                         lo[2 * i + 1] = hmul2(hsub2(and_or(y >> 8, m, magic), off8), sc2);
                         hi[2 * i] = hmul2(hsub2(and_or(y >> 4, m, magic), off8), sc2);
@@ -484,6 +495,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
                     sts128(kbase + (((c0 + 2) ^ (key % 8)) * 16), hi[0], hi[1], hi[2], hi[3]);
                     sts128(kbase + (((c0 + 3) ^ (key % 8)) * 16), hi[4], hi[5], hi[6], hi[7]);
                 }
+              }
                 fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cl(lead(kv == 0 ? &k_full[b] : &v_full[b]));
@@ -501,7 +513,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
     cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256 * NT) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::TMEM_COLS) : "memory");
     }
 }
 

@@ -48,11 +48,38 @@ def test_tcgen05_pair_kernel_parity(ctx, rows, nk, quant):
     _check(c, O, m, l, nk)
 
 
-@pytest.mark.parametrize("rows,nk", [(80, 3000), (256, 2000)])
-def test_tcgen05_matches_split_k_kernel(ctx, rows, nk):
-    c = orc.gen_case(77 + rows, 128, 8, rows, nk, orc.Q8_0)
+# head dim 256 (the reference server's wire geometry: HD 256, 48 rows per group, phone-attn.h:79-80) on the pair
+# kernel, chosen by default from 64 rows per KV head: ATTN_BIG groups (rows = 48 ng), ragged keys, Q4_0
+@pytest.mark.parametrize("rows,nk,quant", [
+    (96, 2048, orc.Q8_0), (144, 4096, orc.Q8_0), (256, 1500, orc.Q4_0), (512, 777, orc.Q8_0), (300, 65, orc.Q8_0),
+    (64, 1, orc.Q4_0), (768, 3000, orc.Q8_0)])
+def test_tcgen05_pair_kernel_hd256_parity(ctx, rows, nk, quant):
+    c = orc.gen_case(7000 + rows + nk + quant, 256, 8, rows, nk, quant)
+    O, m, l = _run_kernel(ctx, c, 0)
+    _check(c, O, m, l, nk)
+
+
+def test_hd256_plans_pick_the_pair_kernel(ctx):
+    import torch
+    for rows, want in [(48, "pa::dec::decode_kernel<256,1>"), (96, "pa::pre::prefill_pair_kernel<1,1,256>")]:
+        shape = pa.shape_for(256, 8, rows, pa.Q8_0)
+        K = torch.zeros((128, shape.rs), dtype=torch.uint8, device="cuda")
+        plan = pa.Plan(ctx, shape, 1, [pa.Seg(K.data_ptr(), K.data_ptr(), 128, 0)])
+        assert plan.kernel == want
+        plan.close()
+    ctx.set_kernel(2)
+    try:
+        with pytest.raises(pa.PaCudaError):
+            pa.Plan(ctx, pa.shape_for(256, 8, 96, pa.Q8_0), 1, [pa.Seg(K.data_ptr(), K.data_ptr(), 128, 0)])
+    finally:
+        ctx.set_kernel(0)
+
+
+@pytest.mark.parametrize("hd,rows,nk", [(128, 80, 3000), (128, 256, 2000), (256, 192, 2500)])
+def test_tcgen05_matches_split_k_kernel(ctx, hd, rows, nk):
+    c = orc.gen_case(77 + rows, hd, 8, rows, nk, orc.Q8_0)
     O1, m1, l1 = _run_kernel(ctx, c, 1)
-    for which in (2, 3):
+    for which in ((2, 3) if hd == 128 else (3,)):
         O2, m2, l2 = _run_kernel(ctx, c, which)
         e = orc.rel_err(O2, m2, l2, O1.astype(np.float64), m1.astype(np.float64), l1.astype(np.float64))
         assert e[0] <= 1e-3 and e[1] <= 1e-3, (which, e)
