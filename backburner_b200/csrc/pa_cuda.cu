@@ -303,6 +303,7 @@ int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, 
         prm.rows = sh.rows;
         prm.n_rt = p->n_rt;
         prm.timeout_ns = ctx->timeout_ns;
+        prm.stall = ctx->stall_test;
         const bool prof = p->profile && p->ev_used + 2 <= p->ev.size();
         if (prof) cudaEventRecord(p->ev[p->ev_used], st);
         cudaError_t e;

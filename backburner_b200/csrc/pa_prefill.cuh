@@ -51,6 +51,7 @@ struct Params {
     uint64_t rs, hb;
     uint32_t nkv, rows, n_rt;     // n_rt: groups of NT*BM rows per head
     uint64_t timeout_ns;
+    int stall;                    // test hook: the softmax warps first wait on a barrier that nothing completes (bounded)
 };
 
 // ---------------------------------------------------------------- tcgen05 / TMA helpers
@@ -199,7 +200,7 @@ struct Smem {
     static constexpr int RAW = V + 2 * BN * HD * 2;                // NS x (K rows, V rows) x [64][RAWB]
     static constexpr int RAW_STAGE = (2 * BN * RAWB + 1023) / 1024 * 1024;
     static constexpr int BAR = RAW + NS * RAW_STAGE;
-    static constexpr int N_BAR = 1 + 2 * NS + 8 + 7 * NT + 1;
+    static constexpr int N_BAR = 1 + 2 * NS + 8 + 7 * NT + 1 + 1;
     static constexpr int TOTAL = BAR + N_BAR * 8 + 32;
 };
 
@@ -229,6 +230,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
     uint64_t *pv_free = p_full + 2 * NT;       // [NT][2]: P.V of a block with P buffer b completed
     uint64_t *o_ready = pv_free + 2 * NT;      // [NT]: the last P.V completed (once)
     uint64_t *mma_done = o_ready + NT;         // every MMA this CTA issued has completed (before TMEM is freed)
+    uint64_t *never = mma_done + 1;            // completed by nobody: the stall test hook waits on it
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + L::N_BAR);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -259,6 +261,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
             mbar_init(&o_ready[t], 1);
         }
         mbar_init(mma_done, 2);
+        mbar_init(never, 1);
         // a CTA started after another one gave up a wait does no work (a systematic failure ends in one timeout)
         *abort_flag = *(volatile int *) p.status != ST_OK;
         fence_mbar_init();
@@ -383,6 +386,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
     } else if (warp < (uint32_t) DQ0) {
         // ------------------------------------------------ softmax warpgroup of tile t
         if (NT == 2) asm volatile("setmaxnreg.inc.sync.aligned.u32 152;");
+        if (p.stall) wait(never, 0);                       // runs out: records the timeout, every role unwinds
         const int t = (int) (warp - SM0) / 4;
         const uint32_t wq = warp % 4;                      // TMEM lane quarter of this warp
         const uint32_t r = wq * 32 + lane;                 // row of the tile = TMEM lane

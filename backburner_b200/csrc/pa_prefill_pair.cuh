@@ -119,7 +119,7 @@ struct PairSmem {
     static constexpr int RAW_V = KH * RAWB;                        // V rows' offset inside a stage
     static constexpr int RAW_STAGE = ((KH + BN) * RAWB + 1023) / 1024 * 1024;
     static constexpr int BAR = RAW + NS * RAW_STAGE;
-    static constexpr int N_BAR = 2 + 2 * NS + 4 * KVB + 7 * NT + 1;
+    static constexpr int N_BAR = 2 + 2 * NS + 4 * KVB + 7 * NT + 1 + 1;
     static constexpr int TOTAL = BAR + N_BAR * 8 + 32;
 };
 
@@ -148,6 +148,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
     uint64_t *pv_free = p_full + 2 * NT;       // [NT][2]
     uint64_t *o_ready = pv_free + 2 * NT;      // [NT]
     uint64_t *mma_done = o_ready + NT;         // both issuers' MMAs completed
+    uint64_t *never = mma_done + 1;            // completed by nobody: the stall test hook waits on it
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + L::N_BAR);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -183,6 +184,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
             mbar_init(&o_ready[t], 1);
         }
         mbar_init(mma_done, 1 + NT);
+        mbar_init(never, 1);
         *abort_flag = cr == 0 && *(volatile int *) p.status != ST_OK;
         fence_mbar_init();
     }
@@ -313,6 +315,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
     } else if (warp < (uint32_t) DQ0) {
         // ------------------------------------------------ softmax of pair tile t, this CTA's 128 rows
         if (NT == 2) asm volatile("setmaxnreg.inc.sync.aligned.u32 152;");
+        if (p.stall) wait(never, 0);   // runs out: records the timeout; the roles of both CTAs unwind (bounded waits)
         const int t = (int) (warp - SM0) / 4;
         const uint32_t wq = warp % 4;
         const uint32_t r = wq * 32 + lane;

@@ -94,9 +94,9 @@ void pa_cuda_set_timeout_ns(pa_cuda_ctx *ctx, uint64_t ns);
  * head, on CTA pairs from 512 rows; the split-K mma.sync kernel otherwise), 1 = always the split-K kernel, 2 = the
  * tcgen05 kernel on single CTAs, 3 = the tcgen05 kernel on CTA pairs (2 and 3: hd 128 and quantised rows only). */
 void pa_cuda_set_kernel(pa_cuda_ctx *ctx, int which);
-/* Failure-detection test hook: while on, the decode kernel's consumer warps first wait on a barrier that nothing
- * completes, so their bounded wait runs out after the timeout; the kernel records PA_CUDA_ETIMEOUT and returns
- * without trapping, and the context stays usable. Off by default. */
+/* Failure-detection test hook: while on, the decode kernel's consumer warps (the tcgen05 kernels' softmax warps) first
+ * wait on a barrier that nothing completes, so their bounded wait runs out after the timeout; the kernel records
+ * PA_CUDA_ETIMEOUT, every role unwinds and returns without trapping, and the context stays usable. Off by default. */
 void pa_cuda_set_stall_test(pa_cuda_ctx *ctx, int on);
 /* Kernel launches made by this context since it was created (the bench reports launches per step from it). */
 uint64_t pa_cuda_launch_count(const pa_cuda_ctx *ctx);

@@ -117,3 +117,23 @@ def test_tcgen05_student_t_values(ctx, which):
     c = orc.gen_case(44, 128, 8, 256, 3000, orc.Q8_0, student_t=True)
     O, m, l = _run_kernel(ctx, c, which)
     _check(c, O, m, l, 3000)
+
+
+@pytest.mark.parametrize("which,hd,rows", [(2, 128, 256), (3, 128, 512), (3, 256, 96)])
+def test_tcgen05_bounded_wait_reports_and_context_recovers(ctx, which, hd, rows):
+    """Failure detection without a GPU fault, on the tcgen05 kernels (single CTA; CTA pair at hd 128 and 256): with the
+    stall hook on, the softmax warps wait on a barrier that nothing completes; after the 1 ms limit the kernel records
+    the timeout, every role of both CTAs of a pair unwinds through its bounded waits, TMEM is freed, the host reads
+    ETIMEOUT, and the next call on the same context is correct."""
+    c = orc.gen_case(55 + hd + rows, hd, 8, rows, 2048, orc.Q8_0)
+    ctx.set_timeout_ns(1_000_000)
+    ctx.set_stall_test(True)
+    try:
+        with pytest.raises(pa.PaCudaError) as ei:
+            _run_kernel(ctx, c, which)
+        assert ei.value.code == -4
+    finally:
+        ctx.set_stall_test(False)
+        ctx.set_timeout_ns(2_000_000_000)
+    O, m, l = _run_kernel(ctx, c, which)
+    _check(c, O, m, l, 2048)
