@@ -81,7 +81,7 @@ struct pa_cuda_plan {
     float *d_op = nullptr, *d_mp = nullptr, *d_lp = nullptr;
     size_t scratch = 0;
     // decode launch shape
-    uint32_t hg = 1, rgc = 1, n_rg = 1, pw = 1, n_consumers = 1, row = 0, gs = 0, grid_y = 1;
+    uint32_t hg = 1, rgc = 1, n_rg = 1, pw = 1, n_consumers = 1, row = 0, gs = 0, grid_y = 1, w = 8;
     size_t smem = 0;
     // tcgen05 path (many query rows per KV head, hd 128): tiles of NT x 128 rows (NT x 256 on a CTA pair), tensor
     // maps of the K/V segments
@@ -132,15 +132,16 @@ int check_shape(pa_cuda_ctx *ctx, const pa_cuda_shape *sh) {
 // launch shape of the decode kernel for a geometry
 int plan_decode_shape(pa_cuda_ctx *ctx, pa_cuda_plan *p) {
     const pa_cuda_shape &sh = p->sh;
-    // warps per CTA: 8 at hd 128, so that two CTAs (two independent stage rings) share an SM; 12 at hd 256
-    const uint32_t maxw = sh.hd == 128 ? 8 : 12;
+    // warps per CTA (the kernel instance): 8, except 4 at hd 256 when 8 KV heads cannot share a CTA
+    p->w = (sh.hd == 256 && sh.nkv % 8) ? 4 : 8;
+    const uint32_t maxw = p->w;
+    const int nst = pa::dec::nstage((int) sh.hd);
     p->n_rg = (sh.rows + 7) / 8;
     // shared memory of NSTAGE stages of key pairs for head-group rows of `row` bytes (pairs padded to an odd number of
     // 16-byte units)
     auto pair_stride = [](uint32_t row) { uint32_t gs = 2 * row; return (gs / 16) % 2 == 0 ? gs + 16 : gs; };
-    auto smem_for = [&sh](uint32_t gs) {
-        return (size_t) pa::dec::NSTAGE * pa::dec::stage_keys((int) sh.hd) * gs + pa::dec::SMEM_SLACK + (pa::dec::NSTAGE + 3) * 8 +
-               2 * pa::dec::NSTAGE * 4 + 16;
+    auto smem_for = [&sh, nst](uint32_t gs) {
+        return (size_t) nst * pa::dec::stage_keys((int) sh.hd) * gs + pa::dec::SMEM_SLACK + (nst + 3) * 8 + 2 * nst * 4 + 16;
     };
     // the largest head group that divides nkv, gives 16-byte aligned rows and fits shared memory
     uint32_t hg = 0;
@@ -240,9 +241,9 @@ cudaError_t launch_prefill_pair(const pa_cuda_plan *p, const CUtensorMap &tq, co
     return e != cudaSuccess ? e : cudaGetLastError();
 }
 
-template <int HD, int Q>
+template <int HD, int Q, int W>
 cudaError_t launch_decode(const pa_cuda_plan *p, const pa::dec::Params &prm, cudaStream_t st) {
-    auto kern = pa::dec::decode_kernel<HD, Q>;
+    auto kern = pa::dec::decode_kernel<HD, Q, W>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) p->smem);
     if (e != cudaSuccess) return e;
     dim3 grid(p->n_jobs, p->grid_y);
@@ -250,29 +251,34 @@ cudaError_t launch_decode(const pa_cuda_plan *p, const pa::dec::Params &prm, cud
     return cudaGetLastError();
 }
 // CTAs of a plan's decode-kernel instance that fit one SM at once (registers, shared memory, threads)
-template <int HD, int Q>
+template <int HD, int Q, int W>
 int decode_regs() {
     cudaFuncAttributes a{};
-    return cudaFuncGetAttributes(&a, pa::dec::decode_kernel<HD, Q>) == cudaSuccess ? a.numRegs : 128;
+    return cudaFuncGetAttributes(&a, pa::dec::decode_kernel<HD, Q, W>) == cudaSuccess ? a.numRegs : 128;
+}
+template <int HD, int W>
+int decode_regs_q(uint32_t q) {
+    return q == PA_CUDA_Q8_0 ? decode_regs<HD, 1, W>() : q == PA_CUDA_Q4_0 ? decode_regs<HD, 2, W>() : decode_regs<HD, 0, W>();
 }
 int decode_ctas_per_sm(const pa_cuda_plan *p) {
     const uint32_t hd = p->sh.hd, q = p->sh.quant;
-    const int regs = hd == 128 ? (q == PA_CUDA_Q8_0 ? decode_regs<128, 1>() : q == PA_CUDA_Q4_0 ? decode_regs<128, 2>() : decode_regs<128, 0>())
-                               : (q == PA_CUDA_Q8_0 ? decode_regs<256, 1>() : q == PA_CUDA_Q4_0 ? decode_regs<256, 2>() : decode_regs<256, 0>());
+    const int regs = hd == 128 ? decode_regs_q<128, 8>(q) : p->w == 4 ? decode_regs_q<256, 4>(q) : decode_regs_q<256, 8>(q);
     const int threads = 32 * (int) p->n_consumers;
     const int by_regs = 65536 / std::max(1, threads * ((regs + 7) / 8 * 8));
     const int by_smem = (int) ((228u * 1024u) / (p->smem + 1024));
     const int by_threads = 2048 / std::max(1, threads);
     return std::max(1, std::min(std::min(by_regs, by_smem), std::min(by_threads, 32)));
 }
-// the decode-kernel instance of a geometry (hd 128 / 256; f16, Q8_0 or Q4_0 rows)
+// the decode-kernel instance of a geometry (hd 128 / 256; f16, Q8_0 or Q4_0 rows; warps per CTA)
+template <int HD, int W>
+cudaError_t launch_decode_q(const pa_cuda_plan *p, const pa::dec::Params &prm, cudaStream_t st, uint32_t quant) {
+    return quant == PA_CUDA_Q8_0 ? launch_decode<HD, 1, W>(p, prm, st)
+         : quant == PA_CUDA_Q4_0 ? launch_decode<HD, 2, W>(p, prm, st) : launch_decode<HD, 0, W>(p, prm, st);
+}
 cudaError_t launch_decode_any(const pa_cuda_plan *p, const pa::dec::Params &prm, cudaStream_t st, uint32_t hd,
                               uint32_t quant) {
-    if (hd == 128)
-        return quant == PA_CUDA_Q8_0 ? launch_decode<128, 1>(p, prm, st)
-             : quant == PA_CUDA_Q4_0 ? launch_decode<128, 2>(p, prm, st) : launch_decode<128, 0>(p, prm, st);
-    return quant == PA_CUDA_Q8_0 ? launch_decode<256, 1>(p, prm, st)
-         : quant == PA_CUDA_Q4_0 ? launch_decode<256, 2>(p, prm, st) : launch_decode<256, 0>(p, prm, st);
+    if (hd == 128) return launch_decode_q<128, 8>(p, prm, st, quant);
+    return p->w == 4 ? launch_decode_q<256, 4>(p, prm, st, quant) : launch_decode_q<256, 8>(p, prm, st, quant);
 }
 
 template <int HD>
@@ -420,7 +426,7 @@ int pa_cuda_available(void) {
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return 0;
     if (major != 10) return 0;
     cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, pa::dec::decode_kernel<128, 1>) != cudaSuccess) {
+    if (cudaFuncGetAttributes(&fa, pa::dec::decode_kernel<128, 1, 8>) != cudaSuccess) {
         cudaGetLastError();
         return 0;
     }
@@ -649,9 +655,11 @@ const char *pa_cuda_plan_kernel(const pa_cuda_plan *p) {
              {"pa::pre::prefill_pair_kernel<2,1,256>", "pa::pre::prefill_pair_kernel<2,1,256>"}}};
         return names[!p->pair ? 0 : p->sh.hd == 256 ? 2 : 1][q == PA_CUDA_Q8_0 ? 0 : 1][p->nt == 2 ? 1 : 0];
     }
-    static const char *dec[2][3] = {{"pa::dec::decode_kernel<128,0>", "pa::dec::decode_kernel<128,1>", "pa::dec::decode_kernel<128,2>"},
-                                    {"pa::dec::decode_kernel<256,0>", "pa::dec::decode_kernel<256,1>", "pa::dec::decode_kernel<256,2>"}};
-    return dec[p->sh.hd == 128 ? 0 : 1][q <= 2 ? q : 0];
+    static const char *dec[3][3] = {
+        {"pa::dec::decode_kernel<128,0,8>", "pa::dec::decode_kernel<128,1,8>", "pa::dec::decode_kernel<128,2,8>"},
+        {"pa::dec::decode_kernel<256,0,8>", "pa::dec::decode_kernel<256,1,8>", "pa::dec::decode_kernel<256,2,8>"},
+        {"pa::dec::decode_kernel<256,0,4>", "pa::dec::decode_kernel<256,1,4>", "pa::dec::decode_kernel<256,2,4>"}};
+    return dec[p->sh.hd == 128 ? 0 : p->w == 4 ? 2 : 1][q <= 2 ? q : 0];
 }
 
 int pa_cuda_plan_run(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, void *stream) {

@@ -7,7 +7,7 @@
 // (pa-metal.mm:452-464). Output per chunk of keys: the unnormalised partial (O, m, l); pa_merge.cuh folds chunks.
 //
 // B200 design (one CTA = one key chunk x a group of heads x a group of query rows):
-//   * each stage of K and V rows (16 keys at hd 128, 32 at hd 256) is streamed from HBM into shared memory with 1-D
+//   * each stage of K and V rows (16 keys) is streamed from HBM into shared memory with 1-D
 //     bulk copies (TMA engine), one copy per PAIR of key rows (requests of one 1 KB row cap a B200 at ~5.4 TB/s, two
 //     rows reach ~7.4 TB/s), pairs padded to an odd number of 16-byte units; NSTAGE stages ring on "full" mbarriers;
 //     the last warp to finish with a stage (a shared counter) refills it, so there is no producer warp and every warp
@@ -32,11 +32,18 @@
 namespace pa {
 namespace dec {
 
-// keys per pipeline stage: one 16-key MMA tile at hd 128 (8-warp CTAs, two per SM: two independent stage rings), two
-// tiles at hd 256 (12-warp CTAs); one lane copies a pair of rows
-__host__ __device__ constexpr int stage_keys(int hd) { return hd == 128 ? 16 : 32; }
+// keys per pipeline stage: one 16-key MMA tile, so the tile loop of a stage is a compile-time single iteration; one lane
+// copies a pair of rows
+__host__ __device__ constexpr int stage_keys(int hd) { return 16; }
+// stages in a CTA's ring: 3 at hd 128; 2 at hd 256, whose rows are twice as long
+__host__ __device__ constexpr int nstage(int hd) { return hd == 128 ? 3 : 2; }
+// Warps per CTA (W, the kernel's third parameter) and CTAs per SM for the register budget: hd 128: 8-warp CTAs, two
+// per SM (two independent stage rings); hd 256: 8-warp CTAs, one per SM, with the ~206 registers a thread the O and Q
+// fragments of 256 dims want (8 KV heads per CTA), or 4-warp CTAs, three per SM within 170 registers (fewer heads).
+// Measured at hd 256, 16 layers x 64-131k Q8_0 keys: 8 heads x 6 rows 5,381 GB/s (8-warp) vs 4,920 (4-warp) and
+// 2,835 with 32-key stages in 12-warp CTAs; 4 heads x 8 rows 5,521 (4-warp) vs 4,986 (8-warp).
+__host__ __device__ constexpr int min_ctas(int hd, int w) { return hd == 128 ? 2 : (w == 4 ? 3 : 1); }
 constexpr int TILE_KEYS = 16;    // keys per MMA tile
-constexpr int NSTAGE = 3;
 constexpr int SMEM_SLACK = 64;   // readable bytes past the last row (a lane may load one unused word there)
 constexpr uint64_t DRAIN_NS = 1000000000ull;   // bound on waiting for copies in flight after an abort (>= 1 s)
 
@@ -129,10 +136,11 @@ __device__ __forceinline__ void q4_word(uint32_t w, uint32_t s2, uint32_t &l02, 
 }
 
 // ---------------------------------------------------------------- the kernel
-template <int HD, int QUANT>
-__global__ void __launch_bounds__(32 * (HD == 128 ? 8 : 12), HD == 128 ? 2 : 1) decode_kernel(const Params p) {
+template <int HD, int QUANT, int W>
+__global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const Params p) {
     constexpr int NMT = HD / 16;   // k-steps of QK^T = m-tiles of P.V
     constexpr int STAGE_KEYS = stage_keys(HD);
+    constexpr int NSTAGE = nstage(HD);
     constexpr int GB = q_group_bytes(QUANT);
     constexpr int PAIR = 2 * GB;   // bytes of an aligned pair of quant blocks
 

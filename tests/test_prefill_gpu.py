@@ -61,7 +61,7 @@ def test_tcgen05_pair_kernel_hd256_parity(ctx, rows, nk, quant):
 
 def test_hd256_plans_pick_the_pair_kernel(ctx):
     import torch
-    for rows, want in [(48, "pa::dec::decode_kernel<256,1>"), (96, "pa::pre::prefill_pair_kernel<1,1,256>")]:
+    for rows, want in [(48, "pa::dec::decode_kernel<256,1,8>"), (96, "pa::pre::prefill_pair_kernel<1,1,256>")]:
         shape = pa.shape_for(256, 8, rows, pa.Q8_0)
         K = torch.zeros((128, shape.rs), dtype=torch.uint8, device="cuda")
         plan = pa.Plan(ctx, shape, 1, [pa.Seg(K.data_ptr(), K.data_ptr(), 128, 0)])
