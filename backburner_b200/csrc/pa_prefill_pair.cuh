@@ -123,6 +123,29 @@ struct PairSmem {
     static constexpr int TOTAL = BAR + N_BAR * 8 + 32;
 };
 
+// A dequant lane's (key, quant block) item: pass ps of operand kv (0 = K, 1 = V) for dequant warp dw and lane `lane`
+// of CTA cr. ql: block within this CTA's tile, qb: block of the head, key: key row in the raw stage.
+//   K: 32 keys x D/32 blocks; pass ps, warp dw: block dw + 4 ps of key `lane`
+//   V: 64 keys x D/64 blocks (this CTA's dims: blocks cr D/64 ..); pass ps, warp dw: block cr D/64 + (dw & 1) + 2 ps of
+//      key 32 (dw >> 1) + lane
+template <int D>
+__host__ __device__ __forceinline__ void dq_item(int kv, int ps, uint32_t dw, uint32_t lane, uint32_t cr, uint32_t &ql,
+                                                 uint32_t &qb, uint32_t &key) {
+    ql = kv == 0 ? dw + 4 * (uint32_t) ps : (dw & 1) + 2 * (uint32_t) ps;
+    qb = kv == 0 ? ql : cr * (D / 64) + ql;
+    key = kv == 0 ? lane : (dw >> 1) * 32 + lane;
+}
+// Where an item goes in its operand buffer: K [D/64 atom cols][32 keys][128 B], V [D/128 atom cols][64 keys][128 B],
+// an atom column = 64 dims = 2 blocks. dq_row: byte offset of the key's 128-byte row in the item's atom column;
+// dq_chunk: offset of 16-byte chunk cc (8 f16) of the item in that row, chunk 4 (ql % 2) + cc swizzled by key % 8 (the
+// UMMA 128-byte swizzle)
+__host__ __device__ __forceinline__ uint32_t dq_row(int kv, uint32_t ql, uint32_t key) {
+    return (ql / 2) * (kv == 0 ? BN / 2 : BN) * 128 + (key / 8) * 1024 + (key % 8) * 128;
+}
+__host__ __device__ __forceinline__ uint32_t dq_chunk(uint32_t ql, uint32_t key, uint32_t cc) {
+    return ((4 * (ql % 2) + cc) ^ (key % 8)) * 16;
+}
+
 template <int QUANT, int NT, int D>
 __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(const __grid_constant__ CUtensorMap tq,
                                                                             const Params p) {
@@ -419,11 +442,8 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
             }
         }
     } else {
-        // ------------------------------------------------ dequantisers: (key, quant block) items, one per lane and pass
-        //   K: 32 keys x D/32 blocks; pass ps, warp dw: block dw + 4 ps of key `lane`
-        //   V: 64 keys x D/64 blocks (this CTA's dims: blocks cr D/64 ..); pass ps, warp dw: block cr D/64 +
-        //      (dw & 1) + 2 ps of key 32 (dw >> 1) + lane
-        // (D = 128: one pass of each; D = 256: two)
+        // ------------------------------------------------ dequantisers: (key, quant block) items (dq_item), one per lane
+        // and pass (D = 128: one pass of each operand; D = 256: two)
         if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 80;");
         const uint32_t dw = warp - DQ0;
         for (uint32_t j = 0; j < nblk; j++) {
@@ -435,18 +455,17 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
                 if (j >= KVB && !wait(kv == 0 ? &k_free[b] : &v_free[b], ((j / KVB) - 1) & 1)) break;
 #pragma unroll
               for (int ps = 0; ps < D / 128; ps++) {
-                const uint32_t ql = kv == 0 ? dw + 4 * ps : (dw & 1) + 2 * ps;          // block within the tile
-                const uint32_t qb = kv == 0 ? ql : cr * (D / 64) + ql;                   // block of the head
-                const uint32_t key = kv == 0 ? lane : (dw >> 1) * 32 + lane;             // key row in the raw stage
+                uint32_t ql, qb, key;
+                dq_item<D>(kv, ps, dw, lane, cr, ql, qb, key);
                 const uint32_t rb = raw + (kv == 0 ? 0u : (uint32_t) L::RAW_V) + key * RAWB;
                 const uint32_t bo = hoff + GB * qb;
                 const uint32_t w16 = bo & ~15u;
                 const uint32_t ds = bo + 2;
                 const uint32_t w0 = (ds - w16) / 4, shift = 8 * (ds % 4);
-                // destination: K [D/64 atom cols][32 keys][128 B], V [D/128 atom cols][64 keys][128 B] (atom column
-                // = 64 dims = 2 blocks); 16-byte chunk (4 (ql % 2) + cc) of the key's 128-byte row, swizzled by key % 8
                 const uint32_t dst = kv == 0 ? sbase + L::K + b * L::K_BUF + (ql / 2) * KH * 128
                                              : sbase + L::V + b * L::V_BUF + (ql / 2) * BN * 128;
+                // the same offsets as dq_row / dq_chunk, written out (helper calls here cost the dequant role a spill
+                // under its 80-register budget)
                 const uint32_t kbase = dst + (key / 8) * 1024 + (key % 8) * 128;
                 const uint32_t c0 = 4 * (ql % 2);
                 const uint32_t s2 = lds16(rb + bo);

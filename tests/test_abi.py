@@ -102,3 +102,71 @@ int main() {
     assert r.returncode == 0, r.stderr
     out = subprocess.run([str(exe)], capture_output=True, text=True)
     assert out.returncode == 0 and "ok" in out.stdout, out.stdout + out.stderr
+
+
+def test_pair_kernel_layouts_and_dequant_maps(tmp_path):
+    """The CTA-pair tcgen05 kernel's shared-memory map and dequant addressing (pa_prefill_pair.cuh), compiled as host
+    code, for Q8_0 / Q4_0, head dim 128 (NT = 1, 2) and 256, both CTAs of a pair and every head offset: the layout fits
+    227 KB with 1024-aligned operand tiles and the TMEM columns fit 512; every raw-stage read of a lane (scale, three or
+    two 16-byte words) stays inside its stage and covers its block's data bytes; and the items of one block write every
+    16-byte chunk of the K and V operand buffers exactly once (dq_item / dq_row / dq_chunk)."""
+    src = tmp_path / "pair_maps.cu"
+    src.write_text(r'''
+#include <cstdio>
+#include <vector>
+#include "pa_prefill_pair.cuh"
+using namespace pa::pre;
+template <int Q, int NT, int D> int check() {
+  using L = PairSmem<Q, NT, D>;
+  constexpr int GB = pa::dec::q_group_bytes(Q), HB = (D / 32) * GB, RAWB = L::RAWB;
+  if (L::TOTAL + 1024 > 227 * 1024) { printf("smem %d\n", L::TOTAL); return 1; }
+  if (L::K % 1024 || L::V % 1024 || L::RAW % 1024 || L::RAW_STAGE % 1024 || L::K_BUF % 1024 || L::V_BUF % 1024 ||
+      L::RAW_V % 128) { printf("alignment\n"); return 1; }
+  if (NT * L::TS > L::TMEM_COLS || L::TMEM_COLS > 512) { printf("tmem\n"); return 1; }
+  const int nload = Q == 1 ? 3 : 2;
+  for (uint32_t hoff : {0u, 8u}) {
+    if (HB % 16 == 0 && hoff) continue;                 // heads of these sizes start 16-aligned
+    if ((int) hoff + HB > RAWB) { printf("window\n"); return 1; }
+    for (uint32_t cr = 0; cr < 2; cr++) for (int kv = 0; kv < 2; kv++) {
+      std::vector<int> hit((kv == 0 ? L::K_BUF : L::V_BUF) / 16, 0);
+      for (int ps = 0; ps < D / 128; ps++) for (uint32_t dw = 0; dw < 4; dw++) for (uint32_t lane = 0; lane < 32; lane++) {
+        uint32_t ql, qb, key;
+        dq_item<D>(kv, ps, dw, lane, cr, ql, qb, key);
+        if (qb >= (uint32_t) (D / 32) || key >= (uint32_t) (kv == 0 ? BN / 2 : BN)) { printf("item\n"); return 1; }
+        if (kv == 1 && qb / (D / 64) != cr) { printf("V block of the other CTA\n"); return 1; }
+        const uint32_t rb = (kv == 0 ? 0u : (uint32_t) L::RAW_V) + key * RAWB;
+        const uint32_t bo = hoff + GB * qb, w16 = bo & ~15u, lo = rb + w16, hi = rb + w16 + 16 * nload;
+        if (hi > (uint32_t) L::RAW_STAGE || rb + bo + 2 > (uint32_t) L::RAW_STAGE) { printf("read past stage\n"); return 1; }
+        if (bo + GB > w16 + 16 * nload) { printf("block not covered\n"); return 1; }
+        (void) lo;
+        for (uint32_t cc = 0; cc < 4; cc++) {
+          const uint32_t off = dq_row(kv, ql, key) + dq_chunk(ql, key, cc);
+          // the UMMA K-major 128-byte-swizzle layout: chunk cc holds tile dims 32 ql + 8 cc of row `key`; 8-row atoms
+          // 1024 B apart, 64-dim atom columns (rows x 128 B) apart, 16-byte chunk j of row r at (j ^ r % 8) * 16
+          const uint32_t dd = 32 * ql + 8 * cc, rows = kv == 0 ? BN / 2 : BN, j = (dd % 64) / 8;
+          const uint32_t want = (dd / 64) * rows * 128 + (key / 8) * 1024 + (key % 8) * 128 + ((j ^ (key % 8)) * 16);
+          if (off != want) { printf("not the swizzled layout (kv%d ql%u key%u cc%u)\n", kv, ql, key, cc); return 1; }
+          if (off % 16 || off + 16 > (uint32_t) (kv == 0 ? L::K_BUF : L::V_BUF)) { printf("write out of buffer\n"); return 1; }
+          hit[off / 16]++;
+        }
+      }
+      for (int h : hit) if (h != 1) { printf("chunk written %d times (q%d nt%d d%d kv%d)\n", h, Q, NT, D, kv); return 1; }
+    }
+  }
+  return 0;
+}
+int main() {
+  if (check<1, 1, 128>() || check<1, 2, 128>() || check<2, 1, 128>() || check<2, 2, 128>() || check<1, 1, 256>() ||
+      check<2, 1, 256>()) return 1;
+  printf("ok\n");
+  return 0;
+}
+''')
+    exe = tmp_path / "pair_maps"
+    nvcc = "/usr/local/cuda/bin/nvcc" if os.path.exists("/usr/local/cuda/bin/nvcc") else "nvcc"
+    r = subprocess.run([nvcc, "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-I",
+                        os.path.join(ROOT, "backburner_b200", "csrc"), "-I", os.path.join(ROOT, "include"), "-o", str(exe),
+                        str(src)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0 and "ok" in out.stdout, out.stdout + out.stderr
