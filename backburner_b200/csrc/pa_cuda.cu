@@ -24,7 +24,11 @@
 namespace {
 
 constexpr int kMaxSmem = 227 * 1024;
-constexpr uint32_t kPrefillMinRows = 64;   // query rows per KV head from which the tcgen05 kernel is used
+// query rows per KV head from which the tcgen05 kernels are used: they dequantise each key block once for all rows,
+// where the split-K kernel repeats it per 8-row group. Measured crossover (8 KV heads, Q8_0, GB/s split-K vs tcgen05):
+// hd 128: 16 rows 2,337 vs 2,024, 24 rows 1,578 vs 2,021, 40 rows 944 vs 1,942; hd 256 (pair kernel): 24 rows 1,642
+// vs 1,454, 32 rows 1,242 vs 1,468, 48 rows 848 vs 1,464
+constexpr uint32_t kPrefillMinRows128 = 24, kPrefillMinRows256 = 32;
 constexpr uint32_t kPairMinRows = 512;     // ... and from which it runs on CTA pairs
 
 struct Plan;
@@ -518,7 +522,8 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
     // (hd 256, the reference server's wire geometry, runs on the CTA-pair kernel only)
     const bool tc_ok = (shape->hd == 128 || (shape->hd == 256 && ctx->kernel_choice != 2)) &&
                        shape->quant != PA_CUDA_F16 && encode_fn() != nullptr;
-    p->prefill = tc_ok && (ctx->kernel_choice >= 2 || (ctx->kernel_choice == 0 && shape->rows >= kPrefillMinRows));
+    const uint32_t min_rows = shape->hd == 128 ? kPrefillMinRows128 : kPrefillMinRows256;
+    p->prefill = tc_ok && (ctx->kernel_choice >= 2 || (ctx->kernel_choice == 0 && shape->rows >= min_rows));
     if (ctx->kernel_choice >= 2 && !tc_ok) {
         delete p;
         return fail(ctx, PA_CUDA_EUNSUPPORTED,

@@ -19,8 +19,8 @@
 //                          (phone-attn/pa-metal.mm:928-937).
 //   page formats         : whatever the server's store_cfg() says (phone-attn/phone-attn.h:298-302): Q8_0 and Q4_0
 //                          rows as received, or f16 rows (is_q8 == 0, store_f16), all on the split-K kernel; calls of
-//                          >= 64 rows per KV head with quantised rows (ATTN_BIG) run on the tcgen05 CTA-pair kernel
-//                          at the server's HD 256.
+//                          >= 32 rows per KV head with quantised rows (ATTN_BIG, multi-token ATTN) run on the tcgen05
+//                          CTA-pair kernel at the server's HD 256.
 #pragma once
 #include <cstdlib>
 #include <string>

@@ -71,10 +71,15 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("which", [0, 1])   # the kernel the plan picks by shape; the split-K kernel forced
 @pytest.mark.parametrize("hd,nkv,rows,quant,nk", CASES)
-def test_decode_parity(ctx, hd, nkv, rows, quant, nk):
+def test_decode_parity(ctx, hd, nkv, rows, quant, nk, which):
     c = orc.gen_case(1000 + hd + nkv + rows + nk + quant, hd, nkv, rows, nk, quant)
-    O, m, l = _run(ctx, c)
+    ctx.set_kernel(which)
+    try:
+        O, m, l = _run(ctx, c)
+    finally:
+        ctx.set_kernel(0)
     _check(c, O, m, l, nk)
 
 

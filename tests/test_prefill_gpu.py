@@ -49,10 +49,11 @@ def test_tcgen05_pair_kernel_parity(ctx, rows, nk, quant):
 
 
 # head dim 256 (the reference server's wire geometry: HD 256, 48 rows per group, phone-attn.h:79-80) on the pair
-# kernel, chosen by default from 64 rows per KV head: ATTN_BIG groups (rows = 48 ng), ragged keys, Q4_0
+# kernel, chosen by default from 32 rows per KV head: ATTN_BIG groups (rows = 48 ng), an 8-token ATTN (48 rows), ragged
+# keys, Q4_0
 @pytest.mark.parametrize("rows,nk,quant", [
     (96, 2048, orc.Q8_0), (144, 4096, orc.Q8_0), (256, 1500, orc.Q4_0), (512, 777, orc.Q8_0), (300, 65, orc.Q8_0),
-    (64, 1, orc.Q4_0), (768, 3000, orc.Q8_0)])
+    (64, 1, orc.Q4_0), (768, 3000, orc.Q8_0), (48, 2500, orc.Q8_0), (32, 999, orc.Q4_0)])
 def test_tcgen05_pair_kernel_hd256_parity(ctx, rows, nk, quant):
     c = orc.gen_case(7000 + rows + nk + quant, 256, 8, rows, nk, quant)
     O, m, l = _run_kernel(ctx, c, 0)
@@ -61,7 +62,7 @@ def test_tcgen05_pair_kernel_hd256_parity(ctx, rows, nk, quant):
 
 def test_hd256_plans_pick_the_pair_kernel(ctx):
     import torch
-    for rows, want in [(48, "pa::dec::decode_kernel<256,1,8>"), (96, "pa::pre::prefill_pair_kernel<1,1,256>")]:
+    for rows, want in [(24, "pa::dec::decode_kernel<256,1,8>"), (48, "pa::pre::prefill_pair_kernel<1,1,256>")]:
         shape = pa.shape_for(256, 8, rows, pa.Q8_0)
         K = torch.zeros((128, shape.rs), dtype=torch.uint8, device="cuda")
         plan = pa.Plan(ctx, shape, 1, [pa.Seg(K.data_ptr(), K.data_ptr(), 128, 0)])
