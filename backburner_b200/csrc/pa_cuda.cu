@@ -218,7 +218,7 @@ cudaError_t launch_prefill(const pa_cuda_plan *p, const CUtensorMap &tq, const p
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid(p->n_jobs, p->sh.nkv * p->n_rt);
-    kern<<<grid, 32 * (8 + 4 * NT), smem, st>>>(tq, prm);
+    kern<<<grid, 32 * (4 + 4 * NT + pa::pre::dq_warps(NT)), smem, st>>>(tq, prm);
     return cudaGetLastError();
 }
 // the CTA-pair kernel: clusters of 2 CTAs along x, one cluster per job

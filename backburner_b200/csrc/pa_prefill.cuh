@@ -204,8 +204,11 @@ struct Smem {
     static constexpr int TOTAL = BAR + N_BAR * 8 + 32;
 };
 
+// dequant warps of the single-CTA kernel: 8 with one Q tile (the dequant is the larger cost per row there), 4 with two
+__host__ __device__ constexpr int dq_warps(int nt) { return nt == 1 ? 8 : 4; }
+
 template <int QUANT, int NT>
-__global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __grid_constant__ CUtensorMap tq,
+__global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_kernel(const __grid_constant__ CUtensorMap tq,
                                                                        const Params p) {
     using L = Smem<QUANT, NT>;
     constexpr int RAWB = L::RAWB;
@@ -214,6 +217,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
     constexpr uint32_t IDESC_PV = idesc_f16(BM, HD, 1);
     // warpgroups: 0 = TMA (warp 0) + MMA (warp 1) + 2 idle warps, 1..NT = softmax of tile t, last = dequant
     constexpr int SM0 = 4, DQ0 = 4 + 4 * NT;   // first softmax warp, first dequant warp
+    constexpr int NDQ = dq_warps(NT);
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // operand tiles need 1024-byte alignment (128-byte swizzle atoms): align the dynamic base explicitly
@@ -247,9 +251,9 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < NS; s++) { mbar_init(&raw_full[s], 1); mbar_init(&raw_empty[s], 4); }
+        for (int s = 0; s < NS; s++) { mbar_init(&raw_full[s], 1); mbar_init(&raw_empty[s], NDQ); }
         for (int b = 0; b < 2; b++) {
-            mbar_init(&k_full[b], 4); mbar_init(&k_free[b], 1); mbar_init(&v_full[b], 4); mbar_init(&v_free[b], 1);
+            mbar_init(&k_full[b], NDQ); mbar_init(&k_free[b], 1); mbar_init(&v_full[b], NDQ); mbar_init(&v_free[b], 1);
         }
         for (int t = 0; t < NT; t++) {
             mbar_init(&s_full[t], 1);
@@ -293,7 +297,9 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
     };
 
     if (warp < 4) {
-      if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 128;");
+      // 16 warps launched with 128 registers each at NT = 1 and 2; each warpgroup resizes its share (NT = 1: control 160,
+      // softmax 168, two dequant warpgroups 88: 128 x (160 + 168 + 88 + 88) = 64,512 <= 65,536)
+      if (NT == 1) asm volatile("setmaxnreg.inc.sync.aligned.u32 160;");
       if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
@@ -386,15 +392,26 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
     } else if (warp < (uint32_t) DQ0) {
         // ------------------------------------------------ softmax warpgroup of tile t
         if (NT == 2) asm volatile("setmaxnreg.inc.sync.aligned.u32 152;");
+        else asm volatile("setmaxnreg.inc.sync.aligned.u32 168;");
         if (p.stall) wait(never, 0);                       // runs out: records the timeout, every role unwinds
         const int t = (int) (warp - SM0) / 4;
         const uint32_t wq = warp % 4;                      // TMEM lane quarter of this warp
         const uint32_t r = wq * 32 + lane;                 // row of the tile = TMEM lane
         const uint32_t tl = tmem + ((wq * 32) << 16) + t * 256;
+        // a warp whose 32 rows are all past the call's rows (a partly filled tile) only keeps the barrier protocol: its
+        // rows' O is never written and MMA rows are independent, so its P may stay as it is. (Its p_full arrival for
+        // block j + 2 needs S of j + 2, which needs every warp's s_empty of j + 1, after their p_full of j.)
+        // (NT = 1 only: the small-row calls; the two-tile softmax has no registers to spare for it)
+        const bool pad = NT == 1 && row0 + t * BM + wq * 32 >= p.rows;
         float m_used = -INFINITY, l = 0.f;
         for (uint32_t j = 0; j < nblk; j++) {
             const uint32_t b = j & 1;
             if (!wait(&s_full[t], j & 1)) break;
+            if (pad) {
+                __syncwarp();
+                if (lane == 0) { mbar_arrive(&s_empty[t]); mbar_arrive(&p_full[2 * t + b]); }
+                continue;
+            }
             tc_fence_after();
             float s[64];
             {
@@ -469,7 +486,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
             if (lane == 0) mbar_arrive(&p_full[2 * t + b]);
         }
         // final: O (unnormalised, relative to m_used) from TMEM to the slot partial
-        if (ok && nblk > 0 && wait(&o_ready[t], 0)) {
+        if (ok && !pad && nblk > 0 && wait(&o_ready[t], 0)) {
             tc_fence_after();
             const uint32_t row = row0 + t * BM + r;
             const uint64_t orow = ((uint64_t) job.slot * p.nkv + h) * p.rows + row;
@@ -490,14 +507,16 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
             }
         }
     } else {
-        // ------------------------------------------------ dequantisers: warp dw owns quant block dw of every key
+        // ------------------------------------------------ dequantisers: warp dw owns quant block dw % 4 of every key
+        // (4 warps: both 32-key halves of a block; 8 warps, NT = 1: key half dw / 4)
         if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 80;");
-        const uint32_t dw = warp - DQ0;
-        const uint32_t bo = hoff + GB * dw;                 // block start inside the raw window row
+        else asm volatile("setmaxnreg.dec.sync.aligned.u32 88;");
+        const uint32_t dw = warp - DQ0, qblk = dw % 4;
+        const uint32_t bo = hoff + GB * qblk;               // block start inside the raw window row
         const uint32_t w16 = bo & ~15u;                     // 16-byte aligned start of the words covering it
         const uint32_t ds = bo + 2;                         // first data byte
         const uint32_t w0 = (ds - w16) / 4, shift = 8 * (ds % 4);
-        const uint32_t colb = (QUANT == 1 ? (dw / 2) : (dw / 2)) * BN * 128;   // atom column of this block's d's
+        const uint32_t colb = (qblk / 2) * BN * 128;        // atom column of this block's d's
         for (uint32_t j = 0; j < nblk; j++) {
             const uint32_t st = j % NS, b = j & 1;
             if (!wait(&raw_full[st], (j / NS) & 1)) break;
@@ -508,8 +527,8 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
                 const uint32_t src = raw + kv * BN * RAWB;
                 const uint32_t dst = sbase + (kv == 0 ? L::K : L::V) + b * BN * HD * 2 + colb;
 #pragma unroll
-                for (int pass = 0; pass < 2; pass++) {
-                    const uint32_t key = pass * 32 + lane;
+                for (int pass = 0; pass < 8 / NDQ; pass++) {
+                    const uint32_t key = (NDQ == 8 ? dw / 4 : (uint32_t) pass) * 32 + lane;
                     const uint32_t rb = src + key * RAWB;
                     const uint32_t s2 = lds16(rb + bo);
                     const uint32_t sc2 = s2 | (s2 << 16);
@@ -535,7 +554,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
                             uint32_t h0, h1, h2, h3;
                             dec::q8_word(A[2 * cc], sc2, h0, h1);
                             dec::q8_word(A[2 * cc + 1], sc2, h2, h3);
-                            const uint32_t c = 4 * (dw % 2) + cc;
+                            const uint32_t c = 4 * (qblk % 2) + cc;
                             sts128(kbase + ((c ^ (key % 8)) * 16), h0, h1, h2, h3);
                         }
                     } else {
@@ -559,7 +578,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_kernel(const __g
                             hi[2 * i] = hmul2(hsub2(and_or(y >> 4, m, magic), off8), sc2);
                             hi[2 * i + 1] = hmul2(hsub2(and_or(y >> 12, m, magic), off8), sc2);
                         }
-                        const uint32_t c0 = 4 * (dw % 2);
+                        const uint32_t c0 = 4 * (qblk % 2);
                         sts128(kbase + (((c0 + 0) ^ (key % 8)) * 16), lo[0], lo[1], lo[2], lo[3]);
                         sts128(kbase + (((c0 + 1) ^ (key % 8)) * 16), lo[4], lo[5], lo[6], lo[7]);
                         sts128(kbase + (((c0 + 2) ^ (key % 8)) * 16), hi[0], hi[1], hi[2], hi[3]);

@@ -343,10 +343,17 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
         const uint32_t wq = warp % 4;
         const uint32_t r = wq * 32 + lane;
         const uint32_t tl = tmem + ((wq * 32) << 16) + t * TS;
+        // a warp whose 32 rows are all past the call's rows only keeps the barrier protocol (as in pa_prefill.cuh)
+        const bool pad = NT == 1 && row0 + t * 2 * BM + cr * BM + wq * 32 >= p.rows;   // (NT = 1: registers, as there)
         float m_used = -INFINITY, l = 0.f;
         for (uint32_t j = 0; j < nblk; j++) {
             const uint32_t b = j & 1;
             if (!wait(&s_full[t], j & 1)) break;
+            if (pad) {
+                __syncwarp();
+                if (lane == 0) { mbar_arrive_cl(lead(&s_empty[t])); mbar_arrive_cl(lead(&p_full[2 * t + b])); }
+                continue;
+            }
             tc_fence_after();
             float s[64];
             {
@@ -421,7 +428,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
             __syncwarp();
             if (lane == 0) mbar_arrive_cl(lead(&p_full[2 * t + b]));
         }
-        if (ok && nblk > 0 && wait(&o_ready[t], 0)) {
+        if (ok && !pad && nblk > 0 && wait(&o_ready[t], 0)) {
             tc_fence_after();
             const uint32_t row = row0 + t * 2 * BM + cr * BM + r;
             const uint64_t orow = ((uint64_t) job.slot * p.nkv + h) * p.rows + row;
