@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
             // (f16 rows: the P.V fragments come from ldmatrix.trans in the P.V loop instead)
             constexpr int NB = QUANT == 1 ? (HD == 128 ? 16 : 32) : QUANT == 2 ? (HD == 128 ? 8 : 16) : 4;   // bytes per lane per key
             constexpr int NW = NB / 4;
-            uint32_t W[4][NW];
+            uint32_t VW[4][NW];
             uint32_t s01 = 0, s23 = 0;
             if constexpr (QUANT != 0) {
             const int b = HD == 128 ? (int) g / 2 : (int) g;
@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
                 }
                 raw[NW] = sig ? lds32(ra + 4 * NW) : 0u;
 #pragma unroll
-                for (int i = 0; i < NW; i++) W[kk][i] = __funnelshift_r(raw[i], raw[i + 1], shift);
+                for (int i = 0; i < NW; i++) VW[kk][i] = __funnelshift_r(raw[i], raw[i + 1], shift);
             }
             // keys past the stage's valid count hold whatever the buffer held before (possibly never written):
             // a zero scale makes their V exactly 0, so P = 0 times it cannot produce NaN
@@ -451,8 +451,8 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
                         constexpr uint32_t SEL[2] = {0x5140u, 0x7362u};   // (a.e, b.e, a.e+1, b.e+1), e = 2mt
                         const int wi = mt / 2;
                         uint32_t lo01, hi01, lo23, hi23;
-                        q8_word(prmt(W[0][wi], W[1][wi], SEL[mt % 2]), s01, lo01, hi01);
-                        q8_word(prmt(W[2][wi], W[3][wi], SEL[mt % 2]), s23, lo23, hi23);
+                        q8_word(prmt(VW[0][wi], VW[1][wi], SEL[mt % 2]), s01, lo01, hi01);
+                        q8_word(prmt(VW[2][wi], VW[3][wi], SEL[mt % 2]), s23, lo23, hi23);
                         mma16816(o[mt], lo01, hi01, lo23, hi23, pb0, pb1);
                     }
                 } else {
@@ -463,8 +463,8 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
                         uint32_t a_l0, a_l1, a_h0, a_h1, c_l0, c_l1, c_h0, c_h1;
                         // q4_word on an interleaved word: l02 = byte e low nibble (keys a,b), l13 = byte e+1 low,
                         // h02 = byte e high, h13 = byte e+1 high
-                        q4_word(prmt(W[0][wi], W[1][wi], SEL[u % 2]), s01, a_l0, a_l1, a_h0, a_h1);
-                        q4_word(prmt(W[2][wi], W[3][wi], SEL[u % 2]), s23, c_l0, c_l1, c_h0, c_h1);
+                        q4_word(prmt(VW[0][wi], VW[1][wi], SEL[u % 2]), s01, a_l0, a_l1, a_h0, a_h1);
+                        q4_word(prmt(VW[2][wi], VW[3][wi], SEL[u % 2]), s23, c_l0, c_l1, c_h0, c_h1);
                         mma16816(o[2 * u], a_l0, a_l1, c_l0, c_l1, pb0, pb1);       // rows g <- e, g+8 <- e+1
                         mma16816(o[2 * u + 1], a_h0, a_h1, c_h0, c_h1, pb0, pb1);   // rows g <- e+16, g+8 <- e+17
                     }
