@@ -51,7 +51,25 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill-steps", type=int, default=5)
     ap.add_argument("--prefill-layers", type=int, default=LAYERS)
-    return ap.parse_args()
+    ap.add_argument("--hd", type=int, choices=[128, 256], default=HD,
+                    help="head dim of the decode workload (256: the reference server's wire geometry)")
+    ap.add_argument("--gqa", type=int, default=GQA, help="query rows per KV head of the decode workload")
+    args = ap.parse_args()
+    set_geometry(args.hd, args.gqa)
+    return args
+
+
+def set_geometry(hd: int, gqa: int):
+    """The decode workload's head dim and query rows per KV head (128 and 5)."""
+    global HD, GQA, Q_HEADS
+    HD, GQA, Q_HEADS = hd, gqa, NKV * gqa
+
+
+def decode_metric(layers: int, keys: int) -> str:
+    """The metric name: BASELINE config 1's, or the same measure at another geometry."""
+    if (HD, GQA, layers, keys) == (128, 5, LAYERS, KEYS):
+        return "decode KV-attn GB/s (config 1: 64 layers x 131072 Q8_0 keys, 40q/8kv, d128)"
+    return f"decode KV-attn GB/s ({layers} layers x {keys} Q8_0 keys, {Q_HEADS}q/{NKV}kv, d{HD})"
 
 
 def layer_bytes(keys: int) -> dict:
@@ -158,8 +176,8 @@ class ClockSampler:
 
 # --------------------------------------------------------------------------------------------- data
 def make_layer(torch, pa, layer: int, k0: int, nk: int, device):
-    """Quantised K and V rows [nk][NKV*136] for positions [k0, k0+nk) of `layer`: N(0,1) values, 4 K channels per
-    head scaled x8, Q8_0 (the BASELINE distributions)."""
+    """Quantised K and V rows [nk][NKV*HD/32*34] for positions [k0, k0+nk) of `layer`: N(0,1) values, 4 K channels
+    per head scaled x8, Q8_0 (the BASELINE distributions)."""
     g = torch.Generator(device=device)
     g.manual_seed(SEED * 1000 + layer)
     ch = torch.stack([torch.randperm(HD, generator=g, device=device)[:4] for _ in range(NKV)])   # [NKV, 4]
@@ -205,7 +223,7 @@ def cpu_baseline(target_s: float = 10.0):
             break
     b = layer_bytes(nk)["total"] * reps
     return {"value": round(b / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{reps} x (1 layer x {nk} Q8_0 positions x 8 KV heads x 5 rows (GQA 5), d128, "
+            "sample": f"{reps} x (1 layer x {nk} Q8_0 positions x {NKV} KV heads x {GQA} rows (GQA {GQA}), d{HD}, "
                       f"{layer_bytes(nk)['total'] / 1e6:.1f} MB) in {dt:.1f} s; oracle fp32 block-online port of "
                       f"sme_attn_partial on {threads} threads"}
 
@@ -229,14 +247,16 @@ def run_reference(args, rank: int, world: int):
     dt = time.perf_counter() - t0
     b = layer_bytes(nk)["total"] * args.steps
     v = b / dt / 1e9
-    sample = (f"each step: 1 layer x {nk} Q8_0 positions x 8 KV heads x 5 rows, d128 ({layer_bytes(nk)['total'] / 1e6:.1f}"
-              f" MB); oracle fp32 block-online port of sme_attn_partial (the reference CPU kernel is ARM SME2-only)")
+    sample = (f"each step: 1 layer x {nk} Q8_0 positions x {NKV} KV heads x {GQA} rows, d{HD} "
+              f"({layer_bytes(nk)['total'] / 1e6:.1f} MB); oracle fp32 block-online port of sme_attn_partial (the "
+              f"reference CPU kernel is ARM SME2-only)")
     line = {
-        "impl": "reference", "metric": "decode KV-attn GB/s (config 1: 64 layers x 131072 Q8_0 keys, 40q/8kv, d128)",
+        "impl": "reference", "metric": decode_metric(args.layers, args.keys),
         "value": round(v, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config 1 decode (bounded CPU sample per step)", "layers": LAYERS, "keys": KEYS,
+        "config": {"workload": ("config 1 decode" if (HD, GQA) == (128, 5) else "decode") + " (bounded CPU sample per step)",
+                   "layers": args.layers, "keys": args.keys,
                    "nkv": NKV, "q_heads": Q_HEADS, "hd": HD, "quant": "q8_0"},
         "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -449,7 +469,7 @@ def main():
 
     # ---- config 2 (prefill): 512 tokens x 40 q heads against 65,536 Q8_0 positions per layer, all layers per step
     prefill = None
-    if world == 1 and args.prefill_steps > 0:
+    if world == 1 and args.prefill_steps > 0 and (HD, GQA) == (128, 5):
         del Kall, Vall
         torch.cuda.empty_cache()
         prefill = bench_prefill(torch, pa, ctx, device, stream, args.prefill_layers, args.prefill_steps)
@@ -461,14 +481,15 @@ def main():
     clocks = clk.summary()
     if rank == 0:
         line = {
-            "metric": "decode KV-attn GB/s (config 1: 64 layers x 131072 Q8_0 keys, 40q/8kv, d128)",
+            "metric": decode_metric(L, args.keys),
             "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "config 1: decode, 1 token/step, fresh seeded Q per step", "layers": L,
+            "config": {"workload": ("config 1: decode" if (HD, GQA) == (128, 5) else "decode") +
+                                   ", 1 token/step, fresh seeded Q per step", "layers": L,
                        "keys": args.keys, "keys_per_gpu": shard, "nkv": NKV, "q_heads": Q_HEADS, "hd": HD,
                        "quant": "q8_0", "parallelism": f"sequence shards x{world}, 1 NCCL all-gather of (O,m,l)/step",
-                       "l2": "inputs larger than L2 (18.3 GB of KV per step), no flush",
+                       "l2": f"inputs larger than L2 ({per_step_bytes / 1e9:.1f} GB of KV per step), no flush",
                        "bytes_per_step": per_step_bytes},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
             "prefill": prefill,
