@@ -231,7 +231,7 @@ cudaError_t launch_prefill_pair(const pa_cuda_plan *p, const CUtensorMap &tq, co
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(2 * p->n_jobs, p->sh.nkv * p->n_rt);
-    cfg.blockDim = dim3(32 * (8 + 4 * NT));
+    cfg.blockDim = dim3(32 * (4 + 4 * NT + pa::pre::pair_dq_warps(D)));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];

@@ -10,15 +10,16 @@
 //   warp 0             TMA: the Q tiles once (128-byte swizzle, the UMMA operand layout), then per 64-key block the
 //                      raw quantised rows of this head (a 16-byte-aligned window of each key row, one 2-D tensor copy
 //                      for K and one for V; keys past the end read as zeros)
-//   warp 1             allocates TMEM (per tile: S 64 columns, two P buffers of 32, O 128); one thread issues the MMAs:
-//                      S_t = Q_t K^T (M=128, N=64) into S, then O_t += P_t V (M=128, N=128, A = P read from TMEM, B = V
-//                      read MN-major) into O
+//   warps 1, 2         warp 1 allocates TMEM (per tile: S 64 columns, two P buffers of 32, O 128); one thread of warp 1
+//                      issues the S_t = Q_t K^T MMAs (M=128, N=64) into S, one of warp 2 the O_t += P_t V MMAs (M=128,
+//                      N=128, A = P read from TMEM, B = V read MN-major) into O
 //   warps 4 .. 4+4NT   one warpgroup per Q tile: thread = query row = TMEM lane. Reads its row of S (64 keys; S is
 //                      free again once read), masks tail keys, online softmax in the log2 domain with lazy rescaling (the
 //                      running max moves only when a block's max exceeds it by more than 8, so O in TMEM is rescaled
 //                      rarely), writes P as packed f16 into the block's P buffer: the softmax never waits for a P.V
 //                      except to rescale
-//   last 4 warps       dequantise each raw K and V block into f16 operand tiles (f16(d * q), 128-byte swizzle)
+//   last 8 (NT = 1) or  dequantise each raw K and V block into f16 operand tiles (f16(d * q), 128-byte swizzle)
+//   4 (NT = 2) warps
 // All waits are bounded; a wait that runs out records a status, and every role still reaches the final barrier so
 // TMEM is released.
 #pragma once

@@ -18,7 +18,8 @@
 //                      CTAs; their commits arrive on the barrier at the same offset in both CTAs (multicast commit).
 //                      In CTA 1, warp 1 tells CTA 0 its Q is in place.
 //   warps 4 .. 4+4NT   softmax of pair tile t for this CTA's 128 rows
-//   last 4 warps       dequantise this CTA's halves of each K and V block
+//   last 4 (D = 128) or dequantise this CTA's halves of each K and V block
+//   8 (D = 256) warps
 // Operand-ready and buffer-free arrivals of both CTAs' dequant and softmax warps go to CTA 0's barriers over
 // distributed shared memory (8 arrivals: 4 warps x 2 CTAs). Each is preceded by the wait that completes what it
 // publishes (shared stores: fence.proxy.async; TMEM: tcgen05.wait::st / ::ld), and is a remote arrive with the default
@@ -123,17 +124,24 @@ struct PairSmem {
     static constexpr int TOTAL = BAR + N_BAR * 8 + 32;
 };
 
-// A dequant lane's (key, quant block) item: pass ps of operand kv (0 = K, 1 = V) for dequant warp dw and lane `lane`
-// of CTA cr. ql: block within this CTA's tile, qb: block of the head, key: key row in the raw stage.
-//   K: 32 keys x D/32 blocks; pass ps, warp dw: block dw + 4 ps of key `lane`
-//   V: 64 keys x D/64 blocks (this CTA's dims: blocks cr D/64 ..); pass ps, warp dw: block cr D/64 + (dw & 1) + 2 ps of
-//      key 32 (dw >> 1) + lane
-template <int D>
+// dequant warps per CTA: 4 at D = 128; 8 at D = 256 (one pair tile per CTA, and twice the dims per key)
+__host__ __device__ constexpr int pair_dq_warps(int d) { return d == 128 ? 4 : 8; }
+// A dequant lane's (key, quant block) item: pass ps of operand kv (0 = K, 1 = V) for dequant warp dw (of NDQ) and lane
+// `lane` of CTA cr. ql: block within this CTA's tile, qb: block of the head, key: key row in the raw stage.
+//   K: 32 keys x D/32 blocks; NDQ = 4: pass ps, warp dw: block dw + 4 ps of key `lane`; NDQ = 8: block dw
+//   V: 64 keys x D/64 blocks (this CTA's dims: blocks cr D/64 ..); NDQ = 4: block cr D/64 + (dw & 1) + 2 ps of key
+//      32 (dw >> 1) + lane; NDQ = 8: block cr D/64 + (dw & 3) of key 32 (dw >> 2) + lane
+template <int D, int NDQ>
 __host__ __device__ __forceinline__ void dq_item(int kv, int ps, uint32_t dw, uint32_t lane, uint32_t cr, uint32_t &ql,
                                                  uint32_t &qb, uint32_t &key) {
-    ql = kv == 0 ? dw + 4 * (uint32_t) ps : (dw & 1) + 2 * (uint32_t) ps;
+    if (NDQ == 4) {
+        ql = kv == 0 ? dw + 4 * (uint32_t) ps : (dw & 1) + 2 * (uint32_t) ps;
+        key = kv == 0 ? lane : (dw >> 1) * 32 + lane;
+    } else {
+        ql = kv == 0 ? dw : (dw & 3);
+        key = kv == 0 ? lane : (dw >> 2) * 32 + lane;
+    }
     qb = kv == 0 ? ql : cr * (D / 64) + ql;
-    key = kv == 0 ? lane : (dw >> 1) * 32 + lane;
 }
 // Where an item goes in its operand buffer: K [D/64 atom cols][32 keys][128 B], V [D/128 atom cols][64 keys][128 B],
 // an atom column = 64 dims = 2 blocks. dq_row: byte offset of the key's 128-byte row in the item's atom column;
@@ -147,7 +155,7 @@ __host__ __device__ __forceinline__ uint32_t dq_chunk(uint32_t ql, uint32_t key,
 }
 
 template <int QUANT, int NT, int D>
-__global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(const __grid_constant__ CUtensorMap tq,
+__global__ void __launch_bounds__(32 * (4 + 4 * NT + pair_dq_warps(D)), 1) prefill_pair_kernel(const __grid_constant__ CUtensorMap tq,
                                                                             const Params p) {
     using L = PairSmem<QUANT, NT, D>;
     static_assert((D == 128 && (NT == 1 || NT == 2)) || (D == 256 && NT == 1), "TMEM holds NT x (128 + D) columns");
@@ -156,6 +164,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
     constexpr uint32_t IDESC_S = idesc_f16(2 * BM, BN, 0);
     constexpr uint32_t IDESC_PV = idesc_f16(2 * BM, D, 1);
     constexpr int SM0 = 4, DQ0 = 4 + 4 * NT;   // first softmax warp, first dequant warp
+    constexpr int NDQ = pair_dq_warps(D), NPASS = (D / 128) * 4 / NDQ;
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -190,12 +199,14 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
     auto lead = [&](uint64_t *b) -> uint32_t { return mapa(smem_u32(b), 0); };
 
     if (threadIdx.x == 0) {
-        constexpr uint32_t npair = 8;   // operand-ready / buffer-free barriers of CTA 0: 4 warps of each CTA
+        // operand-ready barriers of CTA 0: NDQ dequant warps of each CTA; buffer-free (S read, P written): 4 softmax
+        // warps of each CTA
+        constexpr uint32_t npair = 8, nopnd = 2 * NDQ;
         mbar_init(q_full, 1);
         mbar_init(q_pair, 1);
-        for (int s = 0; s < NS; s++) { mbar_init(&raw_full[s], 1); mbar_init(&raw_empty[s], 4); }
+        for (int s = 0; s < NS; s++) { mbar_init(&raw_full[s], 1); mbar_init(&raw_empty[s], NDQ); }
         for (int b = 0; b < KVB; b++) {
-            mbar_init(&k_full[b], npair); mbar_init(&k_free[b], NT); mbar_init(&v_full[b], npair); mbar_init(&v_free[b], 1);
+            mbar_init(&k_full[b], nopnd); mbar_init(&k_free[b], NT); mbar_init(&v_full[b], nopnd); mbar_init(&v_free[b], 1);
         }
         for (int t = 0; t < NT; t++) {
             mbar_init(&s_full[t], 1);
@@ -248,7 +259,10 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
     };
 
     if (warp < 4) {
+      // NT = 2 (D = 128) and D = 256 launch 16 warps with 128 registers each, and every warpgroup resizes its share:
+      // NT = 2: control 128, softmax 2 x 152, dequant 80; D = 256: control 160, softmax 168, dequant 2 x 88
       if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 128;");
+      if (D == 256) asm volatile("setmaxnreg.inc.sync.aligned.u32 160;");
       if (warp == 0) {
         // ------------------------------------------------ TMA producer (each CTA its own operands)
         if (lane == 0) {
@@ -338,6 +352,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
     } else if (warp < (uint32_t) DQ0) {
         // ------------------------------------------------ softmax of pair tile t, this CTA's 128 rows
         if (NT == 2) asm volatile("setmaxnreg.inc.sync.aligned.u32 152;");
+        if (D == 256) asm volatile("setmaxnreg.inc.sync.aligned.u32 168;");
         if (p.stall) wait(never, 0);   // runs out: records the timeout; the roles of both CTAs unwind (bounded waits)
         const int t = (int) (warp - SM0) / 4;
         const uint32_t wq = warp % 4;
@@ -452,6 +467,7 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
         // ------------------------------------------------ dequantisers: (key, quant block) items (dq_item), one per lane
         // and pass (D = 128: one pass of each operand; D = 256: two)
         if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 80;");
+        if (D == 256) asm volatile("setmaxnreg.dec.sync.aligned.u32 88;");
         const uint32_t dw = warp - DQ0;
         for (uint32_t j = 0; j < nblk; j++) {
             const uint32_t st = j % NS, b = j % KVB;
@@ -461,9 +477,9 @@ __global__ void __launch_bounds__(32 * (8 + 4 * NT), 1) prefill_pair_kernel(cons
             for (int kv = 0; kv < 2; kv++) {
                 if (j >= KVB && !wait(kv == 0 ? &k_free[b] : &v_free[b], ((j / KVB) - 1) & 1)) break;
 #pragma unroll
-              for (int ps = 0; ps < D / 128; ps++) {
+              for (int ps = 0; ps < NPASS; ps++) {
                 uint32_t ql, qb, key;
-                dq_item<D>(kv, ps, dw, lane, cr, ql, qb, key);
+                dq_item<D, NDQ>(kv, ps, dw, lane, cr, ql, qb, key);
                 const uint32_t rb = raw + (kv == 0 ? 0u : (uint32_t) L::RAW_V) + key * RAWB;
                 const uint32_t bo = hoff + GB * qb;
                 const uint32_t w16 = bo & ~15u;

@@ -420,7 +420,8 @@ def main():
         with open(os.path.join(ROOT, "profiles", "decode_traffic.json")) as f:
             tr = json.load(f)
         # ncu DRAM bytes of a smaller capture, scaled to this launch: reads by key positions, writes by jobs (slots)
-        traffic = round(tr["dram_read_bytes_per_key_position"] * nk * L + tr["dram_write_bytes_per_job"] * plan.jobs)
+        if (HD, GQA) == (128, 5):   # the capture's geometry (config 1)
+            traffic = round(tr["dram_read_bytes_per_key_position"] * nk * L + tr["dram_write_bytes_per_job"] * plan.jobs)
     except Exception:
         pass
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

@@ -129,9 +129,10 @@ template <int Q, int NT, int D> int check() {
     if ((int) hoff + HB > RAWB) { printf("window\n"); return 1; }
     for (uint32_t cr = 0; cr < 2; cr++) for (int kv = 0; kv < 2; kv++) {
       std::vector<int> hit((kv == 0 ? L::K_BUF : L::V_BUF) / 16, 0);
-      for (int ps = 0; ps < D / 128; ps++) for (uint32_t dw = 0; dw < 4; dw++) for (uint32_t lane = 0; lane < 32; lane++) {
+      constexpr int NDQ = pair_dq_warps(D), NPASS = (D / 128) * 4 / NDQ;
+      for (int ps = 0; ps < NPASS; ps++) for (uint32_t dw = 0; dw < (uint32_t) NDQ; dw++) for (uint32_t lane = 0; lane < 32; lane++) {
         uint32_t ql, qb, key;
-        dq_item<D>(kv, ps, dw, lane, cr, ql, qb, key);
+        dq_item<D, NDQ>(kv, ps, dw, lane, cr, ql, qb, key);
         if (qb >= (uint32_t) (D / 32) || key >= (uint32_t) (kv == 0 ? BN / 2 : BN)) { printf("item\n"); return 1; }
         if (kv == 1 && qb / (D / 64) != cr) { printf("V block of the other CTA\n"); return 1; }
         const uint32_t rb = (kv == 0 ? 0u : (uint32_t) L::RAW_V) + key * RAWB;
