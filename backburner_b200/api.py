@@ -74,6 +74,10 @@ _SIGS = {
     "pa_cuda_normalize": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint64, _P, _P, _P, _P, _P, _P]),
     "pa_cuda_scale_q": (ctypes.c_int, [_P, _P, ctypes.c_float, ctypes.c_uint64, _P, _P]),
     "pa_cuda_fold_reply": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint64, _P, _P, _P, _P, _P, _P]),
+    "pa_cuda_nccl_unique_id": (ctypes.c_int, [_P, ctypes.c_size_t]),
+    "pa_cuda_nccl_comm_create": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]),
+    "pa_cuda_nccl_comm_destroy": (None, [_P]),
+    "pa_cuda_shard_attn_allgather_merge": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P]),
     "pa_cuda_alloc_page": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.POINTER(_Page)]),
     "pa_cuda_free_page": (None, [_P, ctypes.POINTER(_Page)]),
     "pa_cuda_begin": (ctypes.c_int, [_P, ctypes.POINTER(_Page), ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, _P,
@@ -357,6 +361,44 @@ def fold_reply(ctx: Context, hd: int, Oh, lse, O, m, l, stream=None):
     rows = lse.numel()
     ctx.check(lib().pa_cuda_fold_reply(ctx.handle, hd, rows, _ptr(Oh), _ptr(lse), _ptr(O), _ptr(m), _ptr(l),
                                        _stream_ptr(stream)), "fold_reply")
+    return O, m, l
+
+
+def nccl_unique_id() -> bytes:
+    """The NCCL unique id (128 bytes) one rank creates and every rank passes to NcclComm (pa_cuda_nccl_unique_id)."""
+    buf = ctypes.create_string_buffer(128)
+    rc = lib().pa_cuda_nccl_unique_id(buf, 128)
+    if rc != OK:
+        raise PaCudaError(rc, "pa_cuda_nccl_unique_id: NCCL could not be opened or failed")
+    return buf.raw
+
+
+class NcclComm:
+    """A communicator of the position-shard ranks over the context's device (pa_cuda_nccl_comm_create)."""
+
+    def __init__(self, ctx: Context, uid: bytes, rank: int, world: int):
+        self.ctx = ctx
+        h = ctypes.c_void_p()
+        idbuf = ctypes.create_string_buffer(bytes(uid), 128)
+        ctx.check(lib().pa_cuda_nccl_comm_create(ctx.handle, idbuf, int(rank), int(world), ctypes.byref(h)),
+                  "nccl_comm_create")
+        self._h = h
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self):
+        if self._h:
+            lib().pa_cuda_nccl_comm_destroy(self._h)
+            self._h = None
+
+
+def shard_attn_allgather_merge(plan: Plan, Qs, comm: NcclComm, O, m, l, stream=None):
+    """This rank's plan, one NCCL all-gather of every rank's packed (O, m, l), and their log-sum-exp fold into O, m, l
+    (the same on every rank); pa_cuda_shard_attn_allgather_merge."""
+    plan.ctx.check(lib().pa_cuda_shard_attn_allgather_merge(plan._h, _ptr(Qs), comm.handle, _ptr(O), _ptr(m), _ptr(l),
+                                                            _stream_ptr(stream)), "shard_attn_allgather_merge")
     return O, m, l
 
 

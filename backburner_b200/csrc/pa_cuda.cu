@@ -6,6 +6,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <chrono>
@@ -74,6 +76,9 @@ struct pa_cuda_ctx {
     int eng_ng = 0, eng_nt = 0, eng_rows = 0, eng_nkv = 0, eng_hd = 0;
     bool eng_active = false;
     double last_exec_ms = 0;
+    // position shards over NCCL: this rank's packed (O, m, l) and every rank's
+    float *d_shard = nullptr, *d_gathered = nullptr;
+    size_t d_shard_bytes = 0, d_gathered_bytes = 0;
 };
 
 struct pa_cuda_plan {
@@ -412,6 +417,41 @@ int ensure_host(pa_cuda_ctx *ctx, T *&ptr, size_t &cap, size_t bytes) {
     return PA_CUDA_OK;
 }
 
+// NCCL, opened on first use (libnccl.so.2: the copy already in the process, e.g. torch's, else the system's), so the
+// library has no link-time dependency on it and callers that never shard never load it
+struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId *);
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int);
+    ncclResult_t (*comm_destroy)(ncclComm_t);
+    ncclResult_t (*comm_count)(const ncclComm_t, int *);
+    ncclResult_t (*comm_user_rank)(const ncclComm_t, int *);
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+    const char *(*get_error_string)(ncclResult_t);
+};
+const NcclApi *nccl_api() {
+    static const NcclApi *api = []() -> const NcclApi * {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
+        if (!h) return nullptr;
+        static NcclApi a;
+        a.get_unique_id = (decltype(a.get_unique_id)) dlsym(h, "ncclGetUniqueId");
+        a.comm_init_rank = (decltype(a.comm_init_rank)) dlsym(h, "ncclCommInitRank");
+        a.comm_destroy = (decltype(a.comm_destroy)) dlsym(h, "ncclCommDestroy");
+        a.comm_count = (decltype(a.comm_count)) dlsym(h, "ncclCommCount");
+        a.comm_user_rank = (decltype(a.comm_user_rank)) dlsym(h, "ncclCommUserRank");
+        a.all_gather = (decltype(a.all_gather)) dlsym(h, "ncclAllGather");
+        a.get_error_string = (decltype(a.get_error_string)) dlsym(h, "ncclGetErrorString");
+        if (!a.get_unique_id || !a.comm_init_rank || !a.comm_destroy || !a.comm_count || !a.comm_user_rank ||
+            !a.all_gather || !a.get_error_string)
+            return nullptr;
+        return &a;
+    }();
+    return api;
+}
+int nccl_fail(pa_cuda_ctx *ctx, const NcclApi *api, ncclResult_t r, const char *what) {
+    return fail(ctx, PA_CUDA_ENCCL, std::string(what) + ": " + api->get_error_string(r));
+}
+
 }  // namespace
 
 // ====================================================================================================== C ABI
@@ -471,6 +511,8 @@ void pa_cuda_destroy(pa_cuda_ctx *ctx) {
     if (ctx->ev_begin) cudaEventDestroy(ctx->ev_begin);
     if (ctx->ev_end) cudaEventDestroy(ctx->ev_end);
     if (ctx->d_status) cudaFree(ctx->d_status);
+    if (ctx->d_shard) cudaFree(ctx->d_shard);
+    if (ctx->d_gathered) cudaFree(ctx->d_gathered);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
 }
@@ -836,6 +878,62 @@ int pa_cuda_merge_gathered(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, uint32_
     PA_CK(e, "merge launch");
     ctx->launches++;
     return PA_CUDA_OK;
+}
+
+// ---------------------------------------------------------------------------------- position shards over NCCL
+int pa_cuda_nccl_unique_id(void *id, size_t bytes) {
+    const NcclApi *api = nccl_api();
+    if (!api) return PA_CUDA_ENCCL;
+    if (!id || bytes < sizeof(ncclUniqueId)) return PA_CUDA_EINVAL;
+    ncclUniqueId u;
+    if (api->get_unique_id(&u) != ncclSuccess) return PA_CUDA_ENCCL;
+    memcpy(id, &u, sizeof u);
+    return PA_CUDA_OK;
+}
+
+int pa_cuda_nccl_comm_create(pa_cuda_ctx *ctx, const void *id, int rank, int world, void **comm) {
+    if (!ctx || !comm) return PA_CUDA_EINVAL;
+    *comm = nullptr;
+    if (!id || world < 1 || rank < 0 || rank >= world) return fail(ctx, PA_CUDA_EINVAL, "bad unique id, rank or world");
+    const NcclApi *api = nccl_api();
+    if (!api) return fail(ctx, PA_CUDA_ENCCL, "libnccl.so.2 could not be opened");
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, PA_CUDA_ECUDA, "cudaSetDevice");
+    ncclUniqueId u;
+    memcpy(&u, id, sizeof u);
+    ncclComm_t c = nullptr;
+    const ncclResult_t r = api->comm_init_rank(&c, world, u, rank);
+    if (r != ncclSuccess) return nccl_fail(ctx, api, r, "ncclCommInitRank");
+    *comm = c;
+    return PA_CUDA_OK;
+}
+
+void pa_cuda_nccl_comm_destroy(void *comm) {
+    const NcclApi *api = nccl_api();
+    if (api && comm) api->comm_destroy((ncclComm_t) comm);
+}
+
+int pa_cuda_shard_attn_allgather_merge(pa_cuda_plan *p, const uint16_t *Qs, void *comm, float *O, float *m, float *l,
+                                       void *stream) {
+    if (!p) return PA_CUDA_EINVAL;
+    pa_cuda_ctx *ctx = p->ctx;
+    if (!comm || !O || !m || !l || (p->n_jobs && !Qs)) return fail(ctx, PA_CUDA_EINVAL, "null argument");
+    const NcclApi *api = nccl_api();
+    if (!api) return fail(ctx, PA_CUDA_ENCCL, "libnccl.so.2 could not be opened");
+    int world = 0;
+    ncclResult_t r = api->comm_count((ncclComm_t) comm, &world);
+    if (r != ncclSuccess) return nccl_fail(ctx, api, r, "ncclCommCount");
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, PA_CUDA_ECUDA, "cudaSetDevice");
+    const uint32_t hd = p->sh.hd;
+    const uint64_t rows = (uint64_t) p->n_sets * p->sh.nkv * p->sh.rows, part = rows * (hd + 2);
+    int rc = ensure_dev(ctx, ctx->d_shard, ctx->d_shard_bytes, part * sizeof(float));
+    if (!rc) rc = ensure_dev(ctx, ctx->d_gathered, ctx->d_gathered_bytes, (size_t) world * part * sizeof(float));
+    if (rc) return rc;
+    cudaStream_t st = pick(ctx, stream);
+    // this rank's partial, packed O [rows][hd], m [rows], l [rows] (the layout pa_cuda_merge_gathered folds)
+    if ((rc = run_plan(p, Qs, ctx->d_shard, ctx->d_shard + rows * hd, ctx->d_shard + rows * hd + rows, st))) return rc;
+    r = api->all_gather(ctx->d_shard, ctx->d_gathered, part, ncclFloat32, (ncclComm_t) comm, st);
+    if (r != ncclSuccess) return nccl_fail(ctx, api, r, "ncclAllGather");
+    return pa_cuda_merge_gathered(ctx, hd, rows, (uint32_t) world, ctx->d_gathered, O, m, l, 0, st);
 }
 
 int pa_cuda_normalize(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, const float *O, const float *m, const float *l,

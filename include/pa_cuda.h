@@ -11,6 +11,8 @@
  *   pa_cuda_merge          pa_merge / pa_merge_big        phone-attn/pa-metal.mm:137-159, 490-524
  *                          merge_partial                  phone-attn/phone-attn.h:231-239
  *   pa_cuda_merge_gathered the multi-phone merge           docs/TWO-PHONES.md:14-18 (host loop in the absent llama.cpp)
+ *   pa_cuda_shard_attn_allgather_merge, pa_cuda_nccl_*
+ *                          the same split with the exchange   docs/TWO-PHONES.md:14-18 (one NCCL all-gather per call)
  *   pa_cuda_normalize      attn_core's O/l, lse           phone-attn/phone-attn.h:651-655
  *   pa_cuda_fold_reply     co-attention slot of a reply   phone-attn/phone-attn.h:18-20 (host merge in the absent llama.cpp)
  *   pa_cuda_scale_q        f16(q * scale)                 phone-attn/phone-attn.h:595-599, scripts/sme/sme_attn.c:276-280
@@ -148,6 +150,20 @@ int pa_cuda_merge(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, uint32_t n_parts
  * Mac + phone and two-phone split (docs/TWO-PHONES.md:14-18). */
 int pa_cuda_merge_gathered(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, uint32_t n_parts, const float *packed,
                            float *O, float *m, float *l, int fold, void *stream);
+/* ---- position shards over NCCL, in one call: one process per GPU, rank r holding a contiguous position range of every
+ * layer (the N-GPU generalisation of the Mac + phone and two-phone split, docs/TWO-PHONES.md:14-18). NCCL is opened
+ * (dlopen of libnccl.so.2) on first use; these calls fail with PA_CUDA_ENCCL when it cannot be.
+ * pa_cuda_nccl_unique_id: on one rank, the id (`bytes` >= 128) that every rank then passes to
+ * pa_cuda_nccl_comm_create, which returns a communicator over the context's device (an opaque handle: ncclComm_t). */
+int pa_cuda_nccl_unique_id(void *id, size_t bytes);
+int pa_cuda_nccl_comm_create(pa_cuda_ctx *ctx, const void *id, int rank, int world, void **comm);
+void pa_cuda_nccl_comm_destroy(void *comm);
+/* Runs this rank's plan (its shard's segments) into a packed (O, m, l), all-gathers every rank's on `stream` with one
+ * ncclAllGather, and folds them by log-sum-exp (pa_cuda_merge_gathered) into O, m, l, identical on every rank. Every
+ * rank calls it, in the same order, with plans of the same n_sets and shape. Asynchronous; the packed and gathered
+ * buffers are the context's own (grown as needed). */
+int pa_cuda_shard_attn_allgather_merge(pa_cuda_plan *plan, const uint16_t *Qs, void *comm, float *O, float *m, float *l,
+                                       void *stream);
 /* O/l -> f16 Oh, lse = m + log l (device) */
 int pa_cuda_normalize(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, const float *O, const float *m, const float *l,
                       uint16_t *Oh, float *lse, void *stream);

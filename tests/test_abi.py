@@ -171,3 +171,10 @@ int main() {
     assert r.returncode == 0, r.stderr
     out = subprocess.run([str(exe)], capture_output=True, text=True)
     assert out.returncode == 0 and "ok" in out.stdout, out.stdout + out.stderr
+
+
+def test_nccl_unique_id_without_a_gpu():
+    """pa_cuda_nccl_unique_id opens NCCL on first use (no link dependency of libpacuda.so on it) and needs no GPU."""
+    import backburner_b200 as pa
+    a, b = pa.nccl_unique_id(), pa.nccl_unique_id()
+    assert len(a) == 128 and a != b
