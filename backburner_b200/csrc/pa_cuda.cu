@@ -31,7 +31,10 @@ constexpr int kMaxSmem = 227 * 1024;
 // hd 128: 16 rows 2,337 vs 2,024, 24 rows 1,578 vs 2,021, 40 rows 944 vs 1,942; hd 256 (pair kernel): 24 rows 1,642
 // vs 1,454, 32 rows 1,242 vs 1,468, 48 rows 848 vs 1,464
 constexpr uint32_t kPrefillMinRows128 = 24, kPrefillMinRows256 = 32;
-constexpr uint32_t kPairMinRows = 512;     // ... and from which it runs on CTA pairs
+// ... and from which the hd-128 calls run on CTA pairs: past 256 rows the single-CTA kernel starts a second, partly
+// filled tile. Measured (8 KV heads x 4 layers x 65,536 Q8_0 keys, TFLOP/s single vs pair): 256 rows 676 vs 558,
+// 320 510 vs 549, 384 608 vs 643, 448 667 vs 694, 512 751 vs 784
+constexpr uint32_t kPairMinRows = 257;
 
 struct Plan;
 
