@@ -21,6 +21,6 @@ from __future__ import annotations
 from .api import (  # noqa: F401
     F16, Q8_0, Q4_0, PaCudaError, LibraryMissing, Shape, Seg, Context, Plan, Engine, lib, lib_path,
     head_bytes, shape_for, attn, attn_partial, merge, merge_gathered, packed_views, normalize, fold_reply, scale_q,
-    available, NcclComm, nccl_unique_id, shard_attn_allgather_merge,
+    available, NcclComm, nccl_unique_id, nccl_wait, shard_attn_allgather_merge,
 )
 from .formats import quantize_q8_0, quantize_q4_0, dequantize  # noqa: F401

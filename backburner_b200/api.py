@@ -78,6 +78,10 @@ _SIGS = {
     "pa_cuda_nccl_comm_create": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]),
     "pa_cuda_nccl_comm_destroy": (None, [_P]),
     "pa_cuda_shard_attn_allgather_merge": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P]),
+    "pa_cuda_set_shard_exchange": (None, [_P, ctypes.c_int]),
+    "pa_cuda_set_shard_groups": (None, [_P, ctypes.c_int]),
+    "pa_cuda_set_shard_timeout_ms": (None, [_P, ctypes.c_uint32]),
+    "pa_cuda_nccl_wait": (ctypes.c_int, [_P, _P, _P, ctypes.c_uint32]),
     "pa_cuda_alloc_page": (ctypes.c_int, [_P, ctypes.c_size_t, ctypes.POINTER(_Page)]),
     "pa_cuda_free_page": (None, [_P, ctypes.POINTER(_Page)]),
     "pa_cuda_begin": (ctypes.c_int, [_P, ctypes.POINTER(_Page), ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, _P,
@@ -204,6 +208,21 @@ class Context:
     @property
     def launches(self) -> int:
         return int(lib().pa_cuda_launch_count(self._h))
+
+    # exchange of the position-shard call (shard_attn_allgather_merge) for calls made afterwards
+    EXCHANGE_AUTO, EXCHANGE_ALLGATHER, EXCHANGE_ALLREDUCE = 0, 1, 2
+
+    def set_shard_exchange(self, mode: int):
+        """0: by size; 1: all-gather of every rank's packed (O, m, l) and the fold; 2: max / sum all-reduces."""
+        lib().pa_cuda_set_shard_exchange(self._h, int(mode))
+
+    def set_shard_groups(self, groups: int):
+        """Output-set groups whose exchange overlaps the next group's kernels (0: by size, 1: none)."""
+        lib().pa_cuda_set_shard_groups(self._h, int(groups))
+
+    def set_shard_timeout_ms(self, ms: int):
+        """> 0: the shard call waits for its exchange and aborts the communicator past ms (raises ETIMEOUT)."""
+        lib().pa_cuda_set_shard_timeout_ms(self._h, int(ms))
 
     def close(self):
         if self._h:
@@ -392,6 +411,11 @@ class NcclComm:
         if self._h:
             lib().pa_cuda_nccl_comm_destroy(self._h)
             self._h = None
+
+
+def nccl_wait(ctx: Context, comm: NcclComm, stream=None, timeout_ms: int = 0):
+    """Wait for the stream's work, aborting the communicator on an NCCL error or after timeout_ms (pa_cuda_nccl_wait)."""
+    ctx.check(lib().pa_cuda_nccl_wait(ctx.handle, comm.handle, _stream_ptr(stream), int(timeout_ms)), "nccl_wait")
 
 
 def shard_attn_allgather_merge(plan: Plan, Qs, comm: NcclComm, O, m, l, stream=None):

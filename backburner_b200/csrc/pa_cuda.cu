@@ -12,10 +12,12 @@
 #include <algorithm>
 #include <chrono>
 #include <mutex>
+#include <thread>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <string>
+#include <unordered_map>
 #include <vector>
 
 #include "pa_decode.cuh"
@@ -58,6 +60,7 @@ struct pa_cuda_ctx {
     int n_sm = 148;
     cudaStream_t stream = nullptr;
     int *d_status = nullptr;
+    int *h_status = nullptr;      // pinned: the status word read back by pa_cuda_status
     uint64_t timeout_ns = 2000000000ull;
     uint64_t launches = 0;
     int stall_test = 0;
@@ -68,8 +71,11 @@ struct pa_cuda_ctx {
     std::vector<EngEntry> eng_cache;
     uint64_t eng_tick = 0, eng_graph_calls = 0;
     std::vector<pa_cuda_seg> eng_segs;
+    // keys of each page (by its K pointer) already prefetched to the device: a call prefetches only what the host wrote
+    // since (pages new to the engine, rows appended; a page that shrank is prefetched whole)
+    std::unordered_map<uintptr_t, uint32_t> eng_resident;
     uint16_t *h_q = nullptr;      // pinned staging
-    float *h_out = nullptr;       // pinned staging: O, then m, then l
+    float *h_out = nullptr;       // pinned staging: O, then m, then l, then the call's status word
     size_t h_q_bytes = 0, h_out_bytes = 0;
     uint16_t *d_q = nullptr;
     float *d_out = nullptr;
@@ -82,6 +88,11 @@ struct pa_cuda_ctx {
     // position shards over NCCL: this rank's packed (O, m, l) and every rank's
     float *d_shard = nullptr, *d_gathered = nullptr;
     size_t d_shard_bytes = 0, d_gathered_bytes = 0;
+    int shard_exchange = 0;          // 0 by size, 1 all-gather + fold, 2 max / sum all-reduces
+    int shard_groups = 0;            // 0 by size; else output-set groups whose exchange overlaps the next group's kernels
+    uint32_t shard_timeout_ms = 0;   // > 0: the shard call waits for its exchange, bounded (abort on overrun)
+    cudaStream_t xstream = nullptr;  // exchange stream of the pipelined shard call
+    std::vector<cudaEvent_t> xev;    // [group] the group's partial is packed; back: the exchange finished
 };
 
 struct pa_cuda_plan {
@@ -90,6 +101,7 @@ struct pa_cuda_plan {
     uint32_t n_sets = 0, n_jobs = 0, n_slots = 0;
     pa::dec::Job *d_jobs = nullptr;
     uint32_t *d_crange = nullptr;
+    std::vector<uint32_t> crange;       // host copy: jobs (= slots) [crange[s], crange[s+1]) belong to set s
     float *d_op = nullptr, *d_mp = nullptr, *d_lp = nullptr;
     size_t scratch = 0;
     // decode launch shape
@@ -220,25 +232,27 @@ bool map_q(CUtensorMap *m, const void *Qs, uint64_t n_rows, uint32_t hd) {
 }
 
 template <int Q, int NT>
-cudaError_t launch_prefill(const pa_cuda_plan *p, const CUtensorMap &tq, const pa::pre::Params &prm, cudaStream_t st) {
+cudaError_t launch_prefill(const pa_cuda_plan *p, uint32_t nj, const CUtensorMap &tq, const pa::pre::Params &prm,
+                           cudaStream_t st) {
     auto kern = pa::pre::prefill_kernel<Q, NT>;
     constexpr int smem = pa::pre::Smem<Q, NT>::TOTAL + 1024;   // + alignment slack for the 1024-byte operand tiles
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    dim3 grid(p->n_jobs, p->sh.nkv * p->n_rt);
+    dim3 grid(nj * p->sh.nkv * p->n_rt);   // CTA = (row-tile group, head, job), row-tile group fastest
     kern<<<grid, 32 * (4 + 4 * NT + pa::pre::dq_warps(NT)), smem, st>>>(tq, prm);
     return cudaGetLastError();
 }
 // the CTA-pair kernel: clusters of 2 CTAs along x, one cluster per job
 template <int Q, int NT, int D>
-cudaError_t launch_prefill_pair(const pa_cuda_plan *p, const CUtensorMap &tq, const pa::pre::Params &prm, cudaStream_t st) {
+cudaError_t launch_prefill_pair(const pa_cuda_plan *p, uint32_t nj, const CUtensorMap &tq, const pa::pre::Params &prm,
+                                cudaStream_t st) {
     auto kern = pa::pre::prefill_pair_kernel<Q, NT, D>;
     constexpr int smem = pa::pre::PairSmem<Q, NT, D>::TOTAL + 1024;
     static_assert(smem <= 227 * 1024, "shared memory of a CTA");
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(2 * p->n_jobs, p->sh.nkv * p->n_rt);
+    cfg.gridDim = dim3(2 * nj * p->sh.nkv * p->n_rt);   // cluster = (row-tile group, head, job), row-tile group fastest
     cfg.blockDim = dim3(32 * (4 + 4 * NT + pa::pre::pair_dq_warps(D)));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -254,11 +268,11 @@ cudaError_t launch_prefill_pair(const pa_cuda_plan *p, const CUtensorMap &tq, co
 }
 
 template <int HD, int Q, int W>
-cudaError_t launch_decode(const pa_cuda_plan *p, const pa::dec::Params &prm, cudaStream_t st) {
+cudaError_t launch_decode(const pa_cuda_plan *p, uint32_t nj, const pa::dec::Params &prm, cudaStream_t st) {
     auto kern = pa::dec::decode_kernel<HD, Q, W>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) p->smem);
     if (e != cudaSuccess) return e;
-    dim3 grid(p->n_jobs, p->grid_y);
+    dim3 grid(nj, p->grid_y);
     kern<<<grid, 32 * p->n_consumers, p->smem, st>>>(prm);
     return cudaGetLastError();
 }
@@ -283,14 +297,14 @@ int decode_ctas_per_sm(const pa_cuda_plan *p) {
 }
 // the decode-kernel instance of a geometry (hd 128 / 256; f16, Q8_0 or Q4_0 rows; warps per CTA)
 template <int HD, int W>
-cudaError_t launch_decode_q(const pa_cuda_plan *p, const pa::dec::Params &prm, cudaStream_t st, uint32_t quant) {
-    return quant == PA_CUDA_Q8_0 ? launch_decode<HD, 1, W>(p, prm, st)
-         : quant == PA_CUDA_Q4_0 ? launch_decode<HD, 2, W>(p, prm, st) : launch_decode<HD, 0, W>(p, prm, st);
+cudaError_t launch_decode_q(const pa_cuda_plan *p, uint32_t nj, const pa::dec::Params &prm, cudaStream_t st, uint32_t quant) {
+    return quant == PA_CUDA_Q8_0 ? launch_decode<HD, 1, W>(p, nj, prm, st)
+         : quant == PA_CUDA_Q4_0 ? launch_decode<HD, 2, W>(p, nj, prm, st) : launch_decode<HD, 0, W>(p, nj, prm, st);
 }
-cudaError_t launch_decode_any(const pa_cuda_plan *p, const pa::dec::Params &prm, cudaStream_t st, uint32_t hd,
+cudaError_t launch_decode_any(const pa_cuda_plan *p, uint32_t nj, const pa::dec::Params &prm, cudaStream_t st, uint32_t hd,
                               uint32_t quant) {
-    if (hd == 128) return launch_decode_q<128, 8>(p, prm, st, quant);
-    return p->w == 4 ? launch_decode_q<256, 4>(p, prm, st, quant) : launch_decode_q<256, 8>(p, prm, st, quant);
+    if (hd == 128) return launch_decode_q<128, 8>(p, nj, prm, st, quant);
+    return p->w == 4 ? launch_decode_q<256, 4>(p, nj, prm, st, quant) : launch_decode_q<256, 8>(p, nj, prm, st, quant);
 }
 
 template <int HD>
@@ -301,15 +315,20 @@ cudaError_t launch_merge(const pa::mrg::Params &mp, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, cudaStream_t st) {
+// The plan's output sets [s0, s1): the attention kernel over their jobs (jobs are grouped by set, so they are the
+// contiguous range [crange[s0], crange[s1])) and the merge of their slots into O, m, l, which point at set s0's rows.
+// Qs is the whole call's Q (the kernels address it by each job's absolute set).
+int run_plan_sets(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, cudaStream_t st, uint32_t s0,
+                  uint32_t s1) {
     pa_cuda_ctx *ctx = p->ctx;
     const pa_cuda_shape &sh = p->sh;
-    if (p->n_jobs > 0 && p->prefill) {
+    const uint32_t j0 = p->crange[s0], nj = p->crange[s1] - j0;
+    if (nj > 0 && p->prefill) {
         CUtensorMap tq;
         if (!map_q(&tq, Qs, (uint64_t) p->n_sets * sh.nkv * sh.rows, sh.hd))
             return fail(ctx, PA_CUDA_ECUDA, "cuTensorMapEncodeTiled (Q) failed");
         pa::pre::Params prm{};
-        prm.jobs = p->d_jobs;
+        prm.jobs = p->d_jobs + j0;
         prm.kv_maps = p->d_maps;
         prm.Op = p->d_op;
         prm.Mp = p->d_mp;
@@ -326,17 +345,17 @@ int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, 
         if (prof) cudaEventRecord(p->ev[p->ev_used], st);
         cudaError_t e;
         if (p->pair && sh.hd == 256) {
-            e = sh.quant == PA_CUDA_Q8_0 ? launch_prefill_pair<1, 1, 256>(p, tq, prm, st)
-                                         : launch_prefill_pair<2, 1, 256>(p, tq, prm, st);
+            e = sh.quant == PA_CUDA_Q8_0 ? launch_prefill_pair<1, 1, 256>(p, nj, tq, prm, st)
+                                         : launch_prefill_pair<2, 1, 256>(p, nj, tq, prm, st);
         } else if (p->pair) {
             if (sh.quant == PA_CUDA_Q8_0)
-                e = p->nt == 2 ? launch_prefill_pair<1, 2, 128>(p, tq, prm, st) : launch_prefill_pair<1, 1, 128>(p, tq, prm, st);
+                e = p->nt == 2 ? launch_prefill_pair<1, 2, 128>(p, nj, tq, prm, st) : launch_prefill_pair<1, 1, 128>(p, nj, tq, prm, st);
             else
-                e = p->nt == 2 ? launch_prefill_pair<2, 2, 128>(p, tq, prm, st) : launch_prefill_pair<2, 1, 128>(p, tq, prm, st);
+                e = p->nt == 2 ? launch_prefill_pair<2, 2, 128>(p, nj, tq, prm, st) : launch_prefill_pair<2, 1, 128>(p, nj, tq, prm, st);
         } else if (sh.quant == PA_CUDA_Q8_0) {
-            e = p->nt == 2 ? launch_prefill<1, 2>(p, tq, prm, st) : launch_prefill<1, 1>(p, tq, prm, st);
+            e = p->nt == 2 ? launch_prefill<1, 2>(p, nj, tq, prm, st) : launch_prefill<1, 1>(p, nj, tq, prm, st);
         } else {
-            e = p->nt == 2 ? launch_prefill<2, 2>(p, tq, prm, st) : launch_prefill<2, 1>(p, tq, prm, st);
+            e = p->nt == 2 ? launch_prefill<2, 2>(p, nj, tq, prm, st) : launch_prefill<2, 1>(p, nj, tq, prm, st);
         }
         if (e != cudaSuccess) return cuda_fail(ctx, e, "prefill kernel launch");
         if (prof) {
@@ -344,9 +363,9 @@ int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, 
             p->ev_used += 2;
         }
         ctx->launches++;
-    } else if (p->n_jobs > 0) {
+    } else if (nj > 0) {
         pa::dec::Params prm{};
-        prm.jobs = p->d_jobs;
+        prm.jobs = p->d_jobs + j0;
         prm.Qs = Qs;
         prm.Op = p->d_op;
         prm.Mp = p->d_mp;
@@ -368,7 +387,7 @@ int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, 
         const bool prof = p->profile && p->ev_used + 2 <= p->ev.size();
         if (prof) cudaEventRecord(p->ev[p->ev_used], st);
         cudaError_t e;
-        e = launch_decode_any(p, prm, st, sh.hd, sh.quant);
+        e = launch_decode_any(p, nj, prm, st, sh.hd, sh.quant);
         if (e != cudaSuccess) return cuda_fail(ctx, e, "decode kernel launch");
         if (prof) {
             cudaEventRecord(p->ev[p->ev_used + 1], st);
@@ -380,7 +399,7 @@ int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, 
     mp.Op = p->d_op;
     mp.Mp = p->d_mp;
     mp.Lp = p->d_lp;
-    mp.c_range = p->d_crange;
+    mp.c_range = p->d_crange + s0;
     mp.n_parts = p->n_slots;
     mp.op_stride = (uint64_t) sh.nkv * sh.rows * sh.hd;
     mp.ml_stride = (uint64_t) sh.nkv * sh.rows;
@@ -389,12 +408,15 @@ int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, 
     mp.M = m;
     mp.L = l;
     mp.rows_per_set = (uint64_t) sh.nkv * sh.rows;
-    mp.n_sets = p->n_sets;
+    mp.n_sets = s1 - s0;
     mp.fold = 0;
     cudaError_t e = sh.hd == 128 ? launch_merge<128>(mp, st) : launch_merge<256>(mp, st);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "merge kernel launch");
     ctx->launches++;
     return PA_CUDA_OK;
+}
+int run_plan(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, cudaStream_t st) {
+    return run_plan_sets(p, Qs, O, m, l, st, 0, p->n_sets);
 }
 
 template <class T>
@@ -426,9 +448,14 @@ struct NcclApi {
     ncclResult_t (*get_unique_id)(ncclUniqueId *);
     ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int);
     ncclResult_t (*comm_destroy)(ncclComm_t);
+    ncclResult_t (*comm_abort)(ncclComm_t);
+    ncclResult_t (*comm_async_error)(ncclComm_t, ncclResult_t *);
     ncclResult_t (*comm_count)(const ncclComm_t, int *);
     ncclResult_t (*comm_user_rank)(const ncclComm_t, int *);
     ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*group_start)();
+    ncclResult_t (*group_end)();
     const char *(*get_error_string)(ncclResult_t);
 };
 const NcclApi *nccl_api() {
@@ -440,12 +467,18 @@ const NcclApi *nccl_api() {
         a.get_unique_id = (decltype(a.get_unique_id)) dlsym(h, "ncclGetUniqueId");
         a.comm_init_rank = (decltype(a.comm_init_rank)) dlsym(h, "ncclCommInitRank");
         a.comm_destroy = (decltype(a.comm_destroy)) dlsym(h, "ncclCommDestroy");
+        a.comm_abort = (decltype(a.comm_abort)) dlsym(h, "ncclCommAbort");
+        a.comm_async_error = (decltype(a.comm_async_error)) dlsym(h, "ncclCommGetAsyncError");
         a.comm_count = (decltype(a.comm_count)) dlsym(h, "ncclCommCount");
         a.comm_user_rank = (decltype(a.comm_user_rank)) dlsym(h, "ncclCommUserRank");
         a.all_gather = (decltype(a.all_gather)) dlsym(h, "ncclAllGather");
+        a.all_reduce = (decltype(a.all_reduce)) dlsym(h, "ncclAllReduce");
+        a.group_start = (decltype(a.group_start)) dlsym(h, "ncclGroupStart");
+        a.group_end = (decltype(a.group_end)) dlsym(h, "ncclGroupEnd");
         a.get_error_string = (decltype(a.get_error_string)) dlsym(h, "ncclGetErrorString");
-        if (!a.get_unique_id || !a.comm_init_rank || !a.comm_destroy || !a.comm_count || !a.comm_user_rank ||
-            !a.all_gather || !a.get_error_string)
+        if (!a.get_unique_id || !a.comm_init_rank || !a.comm_destroy || !a.comm_abort || !a.comm_async_error ||
+            !a.comm_count || !a.comm_user_rank || !a.all_gather || !a.all_reduce || !a.group_start || !a.group_end ||
+            !a.get_error_string)
             return nullptr;
         return &a;
     }();
@@ -453,6 +486,59 @@ const NcclApi *nccl_api() {
 }
 int nccl_fail(pa_cuda_ctx *ctx, const NcclApi *api, ncclResult_t r, const char *what) {
     return fail(ctx, PA_CUDA_ENCCL, std::string(what) + ": " + api->get_error_string(r));
+}
+
+// a shard communicator: NCCL's, plus whether it was aborted (after which NCCL has freed it)
+struct ShardComm {
+    ncclComm_t nc = nullptr;
+    int rank = 0, world = 1;
+    bool dead = false;
+};
+// exchange choices by size: the two-all-reduce exchange from this many bytes of one rank's partial (with more than 2
+// ranks), and set groups whose exchange overlaps the next group's kernels from this many
+constexpr size_t kShardReduceBytes = 8u << 20;
+constexpr size_t kShardGroupBytes = 64u << 20;
+constexpr uint32_t kShardGroups = 8;
+
+// Wait for the work queued on st, polling the stream and NCCL's asynchronous error; on an NCCL error, or when the bound
+// passes (a rank that left or stopped answering leaves the collective waiting for it), abort the communicator so that
+// its kernels return and the stream drains, and report it. The communicator is unusable afterwards.
+int shard_wait(pa_cuda_ctx *ctx, const NcclApi *api, ShardComm *sc, cudaStream_t st, uint32_t timeout_ms) {
+    const auto t0 = std::chrono::steady_clock::now();
+    auto elapsed_ms = [&]() {
+        return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    };
+    int code = PA_CUDA_OK;
+    std::string why;
+    for (;;) {
+        const cudaError_t q = cudaStreamQuery(st);
+        if (q == cudaSuccess) return PA_CUDA_OK;
+        if (q != cudaErrorNotReady) return cuda_fail(ctx, q, "stream query");
+        ncclResult_t ar = ncclSuccess;
+        if (sc->dead) { code = PA_CUDA_ENCCL; why = "the communicator was aborted earlier"; break; }
+        if (api->comm_async_error(sc->nc, &ar) == ncclSuccess && ar != ncclSuccess && ar != ncclInProgress) {
+            code = PA_CUDA_ENCCL;
+            why = std::string("NCCL asynchronous error: ") + api->get_error_string(ar);
+            break;
+        }
+        if (timeout_ms && elapsed_ms() > timeout_ms) {
+            code = PA_CUDA_ETIMEOUT;
+            why = "the shard exchange did not finish within " + std::to_string(timeout_ms) + " ms (a rank left or stalled)";
+            break;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    if (!sc->dead) {
+        api->comm_abort(sc->nc);   // its kernels in flight return; the communicator's resources are released
+        sc->dead = true;
+    }
+    // the stream drains once the aborted collectives have returned (bounded)
+    const auto t1 = std::chrono::steady_clock::now();
+    while (cudaStreamQuery(st) == cudaErrorNotReady &&
+           std::chrono::steady_clock::now() - t1 < std::chrono::seconds(10))
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    cudaGetLastError();
+    return fail(ctx, code, why + "; communicator aborted");
 }
 
 }  // namespace
@@ -490,6 +576,7 @@ int pa_cuda_create(int device, pa_cuda_ctx **out) {
     cudaDeviceGetAttribute(&ctx->n_sm, cudaDevAttrMultiProcessorCount, device);
     if ((e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking)) != cudaSuccess ||
         (e = cudaMalloc((void **) &ctx->d_status, 16)) != cudaSuccess ||
+        (e = cudaMallocHost((void **) &ctx->h_status, 16)) != cudaSuccess ||
         (e = cudaMemset(ctx->d_status, 0, 16)) != cudaSuccess || (e = cudaEventCreate(&ctx->ev_begin)) != cudaSuccess ||
         (e = cudaEventCreate(&ctx->ev_end)) != cudaSuccess) {
         pa_cuda_destroy(ctx);
@@ -514,8 +601,11 @@ void pa_cuda_destroy(pa_cuda_ctx *ctx) {
     if (ctx->ev_begin) cudaEventDestroy(ctx->ev_begin);
     if (ctx->ev_end) cudaEventDestroy(ctx->ev_end);
     if (ctx->d_status) cudaFree(ctx->d_status);
+    if (ctx->h_status) cudaFreeHost(ctx->h_status);
     if (ctx->d_shard) cudaFree(ctx->d_shard);
     if (ctx->d_gathered) cudaFree(ctx->d_gathered);
+    for (auto e : ctx->xev) cudaEventDestroy(e);
+    if (ctx->xstream) cudaStreamDestroy(ctx->xstream);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     delete ctx;
 }
@@ -539,11 +629,15 @@ void pa_cuda_set_stall_test(pa_cuda_ctx *ctx, int on) {
 int pa_cuda_status(pa_cuda_ctx *ctx, void *stream) {
     if (!ctx) return PA_CUDA_EINVAL;
     cudaStream_t st = pick(ctx, stream);
+    // the read and the clear stay on the caller's stream (no legacy-stream copy that would wait for every blocking
+    // stream of the process, or fail under another thread's global-mode capture)
+    PA_CK(cudaSetDevice(ctx->device), "cudaSetDevice");
+    PA_CK(cudaMemcpyAsync(ctx->h_status, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost, st), "status read");
     PA_CK(cudaStreamSynchronize(st), "stream synchronize");
-    int h = 0;
-    PA_CK(cudaMemcpy(&h, ctx->d_status, sizeof h, cudaMemcpyDeviceToHost), "status read");
+    const int h = *ctx->h_status;
     if (h != pa::ST_OK) {
-        PA_CK(cudaMemset(ctx->d_status, 0, sizeof h), "status clear");
+        PA_CK(cudaMemsetAsync(ctx->d_status, 0, sizeof h, st), "status clear");
+        PA_CK(cudaStreamSynchronize(st), "stream synchronize");
         return fail(ctx, PA_CUDA_ETIMEOUT, "a kernel gave up a bounded wait (code " + std::to_string(h) + ")");
     }
     return PA_CUDA_OK;
@@ -648,6 +742,7 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
         }
     }
     crange[n_sets] = (uint32_t) jobs.size();
+    p->crange = crange;
     p->n_jobs = p->n_slots = (uint32_t) jobs.size();
     if (p->n_jobs > 0 && p->grid_y > 65535) { delete p; return fail(ctx, PA_CUDA_EUNSUPPORTED, "too many head/row groups"); }
 
@@ -906,37 +1001,113 @@ int pa_cuda_nccl_comm_create(pa_cuda_ctx *ctx, const void *id, int rank, int wor
     ncclComm_t c = nullptr;
     const ncclResult_t r = api->comm_init_rank(&c, world, u, rank);
     if (r != ncclSuccess) return nccl_fail(ctx, api, r, "ncclCommInitRank");
-    *comm = c;
+    auto *sc = new ShardComm();
+    sc->nc = c;
+    sc->rank = rank;
+    sc->world = world;
+    *comm = sc;
     return PA_CUDA_OK;
 }
 
 void pa_cuda_nccl_comm_destroy(void *comm) {
+    auto *sc = (ShardComm *) comm;
+    if (!sc) return;
     const NcclApi *api = nccl_api();
-    if (api && comm) api->comm_destroy((ncclComm_t) comm);
+    if (api && sc->nc && !sc->dead) api->comm_destroy(sc->nc);
+    delete sc;
+}
+
+void pa_cuda_set_shard_exchange(pa_cuda_ctx *ctx, int mode) {
+    if (ctx) ctx->shard_exchange = (mode >= 0 && mode <= 2) ? mode : 0;
+}
+void pa_cuda_set_shard_groups(pa_cuda_ctx *ctx, int groups) {
+    if (ctx) ctx->shard_groups = groups > 0 ? groups : 0;
+}
+void pa_cuda_set_shard_timeout_ms(pa_cuda_ctx *ctx, uint32_t ms) {
+    if (ctx) ctx->shard_timeout_ms = ms;
+}
+
+int pa_cuda_nccl_wait(pa_cuda_ctx *ctx, void *comm, void *stream, uint32_t timeout_ms) {
+    if (!ctx || !comm) return PA_CUDA_EINVAL;
+    const NcclApi *api = nccl_api();
+    if (!api) return fail(ctx, PA_CUDA_ENCCL, "libnccl.so.2 could not be opened");
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, PA_CUDA_ECUDA, "cudaSetDevice");
+    return shard_wait(ctx, api, (ShardComm *) comm, pick(ctx, stream), timeout_ms);
 }
 
 int pa_cuda_shard_attn_allgather_merge(pa_cuda_plan *p, const uint16_t *Qs, void *comm, float *O, float *m, float *l,
                                        void *stream) {
     if (!p) return PA_CUDA_EINVAL;
     pa_cuda_ctx *ctx = p->ctx;
-    if (!comm || !O || !m || !l || (p->n_jobs && !Qs)) return fail(ctx, PA_CUDA_EINVAL, "null argument");
+    auto *sc = (ShardComm *) comm;
+    if (!sc || !O || !m || !l || (p->n_jobs && !Qs)) return fail(ctx, PA_CUDA_EINVAL, "null argument");
+    if (sc->dead) return fail(ctx, PA_CUDA_ENCCL, "the communicator was aborted after a failed or overdue exchange");
     const NcclApi *api = nccl_api();
     if (!api) return fail(ctx, PA_CUDA_ENCCL, "libnccl.so.2 could not be opened");
-    int world = 0;
-    ncclResult_t r = api->comm_count((ncclComm_t) comm, &world);
-    if (r != ncclSuccess) return nccl_fail(ctx, api, r, "ncclCommCount");
     if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(ctx, PA_CUDA_ECUDA, "cudaSetDevice");
-    const uint32_t hd = p->sh.hd;
-    const uint64_t rows = (uint64_t) p->n_sets * p->sh.nkv * p->sh.rows, part = rows * (hd + 2);
+    const int world = sc->world;
+    const uint32_t hd = p->sh.hd, ns = p->n_sets;
+    const uint64_t rps = (uint64_t) p->sh.nkv * p->sh.rows;            // rows per output set
+    const uint64_t rows = (uint64_t) ns * rps, part = rows * (hd + 2);   // floats of one rank's packed partial
+    // exchange: the all-gather moves (N-1) partials into every rank, the two all-reduces ~2(N-1)/N of one
+    const int mode = ctx->shard_exchange ? ctx->shard_exchange
+                   : (world > 2 && part * sizeof(float) >= kShardReduceBytes) ? 2 : 1;
+    // set groups: each group's exchange overlaps the next group's kernels
+    uint32_t G = ctx->shard_groups ? (uint32_t) ctx->shard_groups
+               : (part * sizeof(float) >= kShardGroupBytes ? kShardGroups : 1u);
+    G = std::max(1u, std::min(G, std::max(1u, ns)));
     int rc = ensure_dev(ctx, ctx->d_shard, ctx->d_shard_bytes, part * sizeof(float));
-    if (!rc) rc = ensure_dev(ctx, ctx->d_gathered, ctx->d_gathered_bytes, (size_t) world * part * sizeof(float));
+    if (!rc && mode == 1) rc = ensure_dev(ctx, ctx->d_gathered, ctx->d_gathered_bytes, (size_t) world * part * sizeof(float));
     if (rc) return rc;
-    cudaStream_t st = pick(ctx, stream);
-    // this rank's partial, packed O [rows][hd], m [rows], l [rows] (the layout pa_cuda_merge_gathered folds)
-    if ((rc = run_plan(p, Qs, ctx->d_shard, ctx->d_shard + rows * hd, ctx->d_shard + rows * hd + rows, st))) return rc;
-    r = api->all_gather(ctx->d_shard, ctx->d_gathered, part, ncclFloat32, (ncclComm_t) comm, st);
-    if (r != ncclSuccess) return nccl_fail(ctx, api, r, "ncclAllGather");
-    return pa_cuda_merge_gathered(ctx, hd, rows, (uint32_t) world, ctx->d_gathered, O, m, l, 0, st);
+    cudaStream_t st = pick(ctx, stream), xs = st;
+    if (G > 1) {
+        if (!ctx->xstream) PA_CK(cudaStreamCreateWithFlags(&ctx->xstream, cudaStreamNonBlocking), "exchange stream");
+        while (ctx->xev.size() < G + 1) {
+            cudaEvent_t e;
+            PA_CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event create");
+            ctx->xev.push_back(e);
+        }
+        xs = ctx->xstream;
+    }
+    for (uint32_t g = 0; g < G; g++) {
+        const uint32_t s0 = (uint32_t) ((uint64_t) ns * g / G), s1 = (uint32_t) ((uint64_t) ns * (g + 1) / G);
+        if (s1 == s0) continue;
+        const uint64_t r0 = (uint64_t) s0 * rps, rg = (uint64_t) (s1 - s0) * rps;
+        // this rank's partial of the group's sets, packed O [rg][hd], m [rg], l [rg] (the layout the fold reads)
+        float *pk = ctx->d_shard + r0 * (hd + 2), *pm = pk + rg * hd, *pl = pm + rg;
+        if ((rc = run_plan_sets(p, Qs, pk, pm, pl, st, s0, s1))) return rc;
+        if (G > 1) {
+            PA_CK(cudaEventRecord(ctx->xev[g], st), "event record");
+            PA_CK(cudaStreamWaitEvent(xs, ctx->xev[g], 0), "stream wait");
+        }
+        ncclResult_t r;
+        if (mode == 1) {
+            float *ga = ctx->d_gathered + (uint64_t) world * r0 * (hd + 2);
+            if ((r = api->all_gather(pk, ga, rg * (hd + 2), ncclFloat32, sc->nc, xs)) != ncclSuccess)
+                return nccl_fail(ctx, api, r, "ncclAllGather");
+            if ((rc = pa_cuda_merge_gathered(ctx, hd, rg, (uint32_t) world, ga, O + r0 * hd, m + r0, l + r0, 0, xs))) return rc;
+        } else {
+            // the rows' maxima over all ranks straight into m, this rank's (O, l) moved to them, then summed into O, l
+            if ((r = api->all_reduce(pm, m + r0, rg, ncclFloat32, ncclMax, sc->nc, xs)) != ncclSuccess)
+                return nccl_fail(ctx, api, r, "ncclAllReduce (max)");
+            const unsigned blocks = (unsigned) ((rg + 7) / 8);
+            if (hd == 128) pa::mrg::rescale_to_kernel<128><<<blocks, 256, 0, xs>>>(pk, pm, pl, m + r0, rg);
+            else pa::mrg::rescale_to_kernel<256><<<blocks, 256, 0, xs>>>(pk, pm, pl, m + r0, rg);
+            PA_CK(cudaGetLastError(), "rescale launch");
+            ctx->launches++;
+            if ((r = api->group_start()) != ncclSuccess) return nccl_fail(ctx, api, r, "ncclGroupStart");
+            ncclResult_t r1 = api->all_reduce(pk, O + r0 * hd, rg * hd, ncclFloat32, ncclSum, sc->nc, xs);
+            ncclResult_t r2 = api->all_reduce(pl, l + r0, rg, ncclFloat32, ncclSum, sc->nc, xs);
+            if ((r = api->group_end()) != ncclSuccess) return nccl_fail(ctx, api, r, "ncclGroupEnd");
+            if (r1 != ncclSuccess || r2 != ncclSuccess) return nccl_fail(ctx, api, r1 != ncclSuccess ? r1 : r2, "ncclAllReduce (sum)");
+        }
+    }
+    if (G > 1) {
+        PA_CK(cudaEventRecord(ctx->xev[G], xs), "event record");
+        PA_CK(cudaStreamWaitEvent(st, ctx->xev[G], 0), "stream wait");
+    }
+    if (ctx->shard_timeout_ms) return shard_wait(ctx, api, sc, st, ctx->shard_timeout_ms);
+    return PA_CUDA_OK;
 }
 
 int pa_cuda_normalize(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, const float *O, const float *m, const float *l,
@@ -1001,6 +1172,7 @@ void pa_cuda_free_page(pa_cuda_ctx *ctx, pa_cuda_page *pg) {
     if (!ctx || !pg) return;
     cudaSetDevice(ctx->device);
     if (ctx->eng_active) cudaStreamSynchronize(ctx->stream);
+    ctx->eng_resident.erase((uintptr_t) pg->k);
     if (pg->k) cudaFree(pg->k);
     if (pg->v) cudaFree(pg->v);
     pg->k = pg->v = nullptr;
@@ -1065,7 +1237,7 @@ int eng_prepare(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *nke
     const size_t qb = rows * sh.hd * 2, ob = rows * sh.hd * 4, mb = rows * 4;
     const void *before[4] = {ctx->h_q, ctx->h_out, ctx->d_q, ctx->d_out};
     if ((rc = ensure_host(ctx, ctx->h_q, ctx->h_q_bytes, qb))) return rc;
-    if ((rc = ensure_host(ctx, ctx->h_out, ctx->h_out_bytes, ob + 2 * mb))) return rc;
+    if ((rc = ensure_host(ctx, ctx->h_out, ctx->h_out_bytes, ob + 2 * mb + 16))) return rc;
     if ((rc = ensure_dev(ctx, ctx->d_q, ctx->d_q_bytes, qb))) return rc;
     if ((rc = ensure_dev(ctx, ctx->d_out, ctx->d_out_bytes, ob + 2 * mb))) return rc;
     if (before[0] != ctx->h_q || before[1] != ctx->h_out || before[2] != ctx->d_q || before[3] != ctx->d_out)
@@ -1074,16 +1246,26 @@ int eng_prepare(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *nke
     return PA_CUDA_OK;
 }
 
-// stream-ordered migration of managed pages the host may have written since the last call
+// Stream-ordered migration of the rows the host wrote into managed pages since the last call. The host writes pages only
+// by APPEND (rows past the keys already held) or after a TRUNCATE (the page shrinks, then grows again), so a page whose
+// key count is what was prefetched last is skipped: a steady decode step issues no prefetch at all. The prefetch is only
+// a hint: rows the host rewrote without changing the count (TRUNCATE, then APPEND of as many rows) still reach the GPU
+// correctly through managed memory's on-demand migration.
 void eng_prefetch(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *nkeys, int n_pages, uint64_t rs) {
     for (int i = 0; i < n_pages; i++) {
+        auto it = ctx->eng_resident.find((uintptr_t) pages[i].k);
+        const uint32_t had = it == ctx->eng_resident.end() ? 0u : it->second, now = nkeys[i];
+        if (it != ctx->eng_resident.end() && had == now) continue;
+        const size_t lo = now > had ? (size_t) had * rs : 0, hi = (size_t) now * rs;
+        ctx->eng_resident[(uintptr_t) pages[i].k] = now;
+        if (hi <= lo) continue;
 #if CUDART_VERSION >= 13000
         cudaMemLocation loc{cudaMemLocationTypeDevice, ctx->device};
-        cudaMemPrefetchAsync(pages[i].k, (size_t) nkeys[i] * rs, loc, 0, ctx->stream);
-        cudaMemPrefetchAsync(pages[i].v, (size_t) nkeys[i] * rs, loc, 0, ctx->stream);
+        cudaMemPrefetchAsync(pages[i].k + lo, hi - lo, loc, 0, ctx->stream);
+        cudaMemPrefetchAsync(pages[i].v + lo, hi - lo, loc, 0, ctx->stream);
 #else
-        cudaMemPrefetchAsync(pages[i].k, (size_t) nkeys[i] * rs, ctx->device, ctx->stream);
-        cudaMemPrefetchAsync(pages[i].v, (size_t) nkeys[i] * rs, ctx->device, ctx->stream);
+        cudaMemPrefetchAsync(pages[i].k + lo, hi - lo, ctx->device, ctx->stream);
+        cudaMemPrefetchAsync(pages[i].v + lo, hi - lo, ctx->device, ctx->stream);
 #endif
     }
     cudaGetLastError();
@@ -1098,6 +1280,9 @@ int eng_enqueue(pa_cuda_ctx *ctx, pa_cuda_plan *plan, const pa_cuda_shape &sh, i
     int rc = run_plan(plan, ctx->d_q, dO, dm, dl, ctx->stream);
     if (rc) return rc;
     PA_CK(cudaMemcpyAsync(ctx->h_out, ctx->d_out, ob + 2 * mb, cudaMemcpyDeviceToHost, ctx->stream), "O to host");
+    // the status word rides with the readback, so end() needs no second synchronising copy
+    PA_CK(cudaMemcpyAsync((char *) ctx->h_out + ob + 2 * mb, ctx->d_status, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream),
+          "status to host");
     return PA_CUDA_OK;
 }
 
@@ -1110,6 +1295,7 @@ int pa_cuda_begin(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *n
     if (!ctx) return PA_CUDA_EINVAL;
     if (ctx->eng_active) return fail(ctx, PA_CUDA_EINVAL, "begin while a call is in flight (call end first)");
     if (!Qs_host) return fail(ctx, PA_CUDA_EINVAL, "bad begin arguments");
+    const auto t_call = std::chrono::steady_clock::now();   // end() reports the time from here (plan lookup, Q packing)
     pa_cuda_shape sh;
     int nt = 0;
     EngEntry *entry = nullptr;
@@ -1128,7 +1314,7 @@ int pa_cuda_begin(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *n
                 for (int gg = 0; gg < 6; gg++) memcpy(dst + (size_t) gg * nt * hd, src + (size_t) gg * 8 * hd, (size_t) nt * hd * 2);
         }
     eng_prefetch(ctx, pages, nkeys, n_pages, sh.rs);
-    ctx->t_begin = std::chrono::steady_clock::now();
+    ctx->t_begin = t_call;
     PA_CK(cudaEventRecord(ctx->ev_begin, ctx->stream), "event");
     if (entry->graph && !entry->plan->profile) {   // armed: one graph launch replays the whole call
         PA_CK(cudaGraphLaunch(entry->graph, ctx->stream), "graph launch");
@@ -1191,7 +1377,17 @@ double pa_cuda_end(pa_cuda_ctx *ctx, float *O, float *m, float *l) {
     const int NR = 48, ng = ctx->eng_ng, nt = ctx->eng_nt, nkv = ctx->eng_nkv, hd = ctx->eng_hd, rows = ctx->eng_rows;
     const size_t out_rows = (size_t) ng * nkv * NR;
     cudaError_t e = cudaEventSynchronize(ctx->ev_end);
-    const int st = e == cudaSuccess ? pa_cuda_status(ctx, nullptr) : PA_CUDA_ECUDA;
+    const size_t prow = (size_t) ng * nkv * rows;
+    int st = PA_CUDA_ECUDA;
+    if (e == cudaSuccess) {
+        const int h = *reinterpret_cast<const volatile int *>((const char *) ctx->h_out + prow * hd * 4 + 2 * prow * 4);
+        st = PA_CUDA_OK;
+        if (h != pa::ST_OK) {   // a kernel of this call gave up a bounded wait: clear the word for the next call
+            cudaMemsetAsync(ctx->d_status, 0, sizeof(int), ctx->stream);
+            cudaStreamSynchronize(ctx->stream);
+            st = fail(ctx, PA_CUDA_ETIMEOUT, "a kernel gave up a bounded wait (code " + std::to_string(h) + ")");
+        }
+    }
     if (e != cudaSuccess || st != PA_CUDA_OK) {
         for (size_t r = 0; r < out_rows; r++) { m[r] = -INFINITY; l[r] = 0; }
         if (e != cudaSuccess) ctx->err = std::string("GPU call failed: ") + cudaGetErrorString(e);
@@ -1200,7 +1396,6 @@ double pa_cuda_end(pa_cuda_ctx *ctx, float *O, float *m, float *l) {
     float ms = 0;
     cudaEventElapsedTime(&ms, ctx->ev_begin, ctx->ev_end);
     ctx->last_exec_ms = ms;
-    const size_t prow = (size_t) ng * nkv * rows;
     const float *hO = ctx->h_out, *hm = hO + prow * hd, *hl = hm + prow;
     for (int gi = 0; gi < ng; gi++)
         for (int h = 0; h < nkv; h++)
@@ -1241,7 +1436,8 @@ constexpr size_t kNaParts = (kNaJobs + kNaMaxJobs * sizeof(pa::dec::Job) + 255) 
 static __device__ __align__(256) uint8_t g_na_scratch[kNaBytes];
 
 // the device address of g_na_scratch per device (set up by the first call on that device; a host-side name of a
-// __device__ array is not a device address)
+// __device__ array is not a device address). The address belongs to the device's primary context: after
+// cudaDeviceReset it would be stale, so a process that resets a device does not use this entry point afterwards.
 std::mutex g_na_mu;
 uint8_t *g_na_ptr[128] = {};
 
@@ -1282,8 +1478,8 @@ extern "C" int pa_cuda_attn_noalloc(const pa_cuda_shape *shape, const uint16_t *
     if (why) *why = "";
     if (!shape || !O || !m || !l || (nk && (!Qs || !K || !V))) return na_fail(why, PA_CUDA_EINVAL, "null argument");
     if (check_shape(nullptr, shape) != PA_CUDA_OK)
-        return na_fail(why, PA_CUDA_EUNSUPPORTED, "shape: hd 128/256, Q8_0 or Q4_0, hb of the format, rs >= nkv*hb and "
-                                                  "a multiple of 16");
+        return na_fail(why, PA_CUDA_EUNSUPPORTED, "shape: hd 128/256, F16, Q8_0 or Q4_0 rows, hb of the format, rs >= nkv*hb "
+                                                  "and a multiple of 16");
     if (nk && (((uintptr_t) K | (uintptr_t) V) & 15)) return na_fail(why, PA_CUDA_EINVAL, "K/V not 16-byte aligned");
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return na_fail(why, PA_CUDA_ECUDA, "cudaGetDevice");
@@ -1349,7 +1545,7 @@ extern "C" int pa_cuda_attn_noalloc(const pa_cuda_shape *shape, const uint16_t *
         prm.timeout_ns = 2000000000ull;
         prm.stall = 0;
         cudaError_t e;
-        e = launch_decode_any(&p, prm, st, shape->hd, shape->quant);
+        e = launch_decode_any(&p, n_jobs, prm, st, shape->hd, shape->quant);
         if (e != cudaSuccess) return na_fail(why, PA_CUDA_ECUDA, "split-K kernel launch failed");
     }
     pa::mrg::Params mp{};

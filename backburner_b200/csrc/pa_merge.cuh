@@ -136,6 +136,29 @@ __global__ void __launch_bounds__(256) fold_reply_kernel(const uint16_t *Oh, con
     }
 }
 
+// The all-reduce exchange of position shards: once M holds each row's maximum over all ranks' partials, this rank's
+// partial (O, m, l) is moved to it, w = exp(m - M), so that the ranks' partials add up to the merge of pa_merge /
+// merge_partial: O = sum_r w_r O_r, l = sum_r w_r l_r (a rank without keys in the row has l = 0 and adds nothing; a row
+// no rank has keys for keeps O = 0, l = 0, M = -inf). In place; one warp per row.
+template <int HD>
+__global__ void __launch_bounds__(256) rescale_to_kernel(float *O, const float *m, float *l, const float *M,
+                                                         uint64_t n_rows) {
+    constexpr int V = HD / 32;
+    const uint64_t r = (uint64_t) blockIdx.x * 8 + threadIdx.x / 32;
+    const uint32_t lane = threadIdx.x % 32;
+    if (r >= n_rows) return;
+    const float lr = l[r], mr = m[r], Mr = M[r];
+    const float w = (lr > 0.f && Mr > -INFINITY) ? ex2((mr - Mr) * LOG2E) : 0.f;
+    float4 *o = reinterpret_cast<float4 *>(O + r * HD + lane * V);
+#pragma unroll
+    for (int i = 0; i < V / 4; i++) {
+        const float4 x = o[i];
+        o[i] = make_float4(w * x.x, w * x.y, w * x.z, w * x.w);
+    }
+    __syncwarp();
+    if (lane == 0) l[r] = w * lr;
+}
+
 // f16(q * scale) for n fp32 values (scripts/sme/sme_attn.c:276-280; phone-attn/phone-attn.h:595-599)
 __global__ void scale_q_kernel(const float *Q, float scale, uint64_t n, uint16_t *Qs) {
     for (uint64_t i = (uint64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t) gridDim.x * blockDim.x)

@@ -239,8 +239,11 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + L::N_BAR);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
-    const dec::Job job = p.jobs[blockIdx.x];
-    const uint32_t h = blockIdx.y % p.nkv, rt = blockIdx.y / p.nkv;
+    // CTA order (a 1-D grid): row-tile group fastest, then KV head, then job, so the CTAs that read the same K/V
+    // blocks (all row groups and heads of one chunk of keys) run at the same time and share them through L2
+    const uint32_t cid = blockIdx.x;
+    const uint32_t rt = cid % p.n_rt, h = (cid / p.n_rt) % p.nkv;
+    const dec::Job job = p.jobs[cid / (p.n_rt * p.nkv)];
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const uint32_t nblk = (job.nk + BN - 1) / BN;
     const uint32_t hbyte = h * (uint32_t) p.hb;
@@ -405,6 +408,7 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
         // (NT = 1 only: the small-row calls; the two-tile softmax has no registers to spare for it)
         const bool pad = NT == 1 && row0 + t * BM + wq * 32 >= p.rows;
         float m_used = -INFINITY, l = 0.f;
+        float m_row = -INFINITY;   // the row's exact maximum (log2 units); O and l are reported against it
         for (uint32_t j = 0; j < nblk; j++) {
             const uint32_t b = j & 1;
             if (!wait(&s_full[t], j & 1)) break;
@@ -437,6 +441,7 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
             for (int i = 1; i + 1 < BN; i += 2) mx = max3(mx, s[i], s[i + 1]);
             mx = fmaxf(mx, s[BN - 1]);
             mx *= LOG2E;
+            m_row = fmaxf(m_row, mx);
             float alpha = 1.f;
             bool rescale = false;
             if (j == 0) m_used = mx;
@@ -486,11 +491,13 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[2 * t + b]);
         }
-        // final: O (unnormalised, relative to m_used) from TMEM to the slot partial
+        // final: O from TMEM to the slot partial, moved from the lazy reference max m_used to the row's exact maximum
+        // (m = max_j s_j, as sme_attn_partial reports it): one factor 2^(m_used - m_row) in (2^-8, 1] on O and l
         if (ok && !pad && nblk > 0 && wait(&o_ready[t], 0)) {
             tc_fence_after();
             const uint32_t row = row0 + t * BM + r;
             const uint64_t orow = ((uint64_t) job.slot * p.nkv + h) * p.rows + row;
+            const float fix = m_row > -INFINITY ? ex2(m_used - m_row) : 1.f;
 #pragma unroll
             for (int q = 0; q < HD / 32; q++) {
                 float o[32];
@@ -499,12 +506,13 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
                 if (row < p.rows) {
                     float4 *dst = reinterpret_cast<float4 *>(p.Op + orow * HD + q * 32);
 #pragma unroll
-                    for (int i = 0; i < 8; i++) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                    for (int i = 0; i < 8; i++)
+                        dst[i] = make_float4(o[4 * i] * fix, o[4 * i + 1] * fix, o[4 * i + 2] * fix, o[4 * i + 3] * fix);
                 }
             }
             if (row < p.rows) {
-                p.Mp[orow] = l > 0.f ? m_used * (1.0f / LOG2E) : -INFINITY;
-                p.Lp[orow] = l;
+                p.Mp[orow] = l > 0.f ? m_row * (1.0f / LOG2E) : -INFINITY;
+                p.Lp[orow] = l * fix;
             }
         }
     } else {

@@ -185,8 +185,11 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + pair_dq_warps(D)), 1) prefi
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const uint32_t cr = cluster_rank();
-    const dec::Job job = p.jobs[blockIdx.x / 2];
-    const uint32_t h = blockIdx.y % p.nkv, rt = blockIdx.y / p.nkv;
+    // cluster order (a 1-D grid of CTA pairs): row-tile group fastest, then KV head, then job, so the clusters that read
+    // the same K/V blocks (all row groups and heads of one chunk of keys) run at the same time and share them through L2
+    const uint32_t cid = blockIdx.x / 2;
+    const uint32_t rt = cid % p.n_rt, h = (cid / p.n_rt) % p.nkv;
+    const dec::Job job = p.jobs[cid / (p.n_rt * p.nkv)];
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const uint32_t nblk = (job.nk + BN - 1) / BN;
     const uint32_t hbyte = h * (uint32_t) p.hb;
@@ -361,6 +364,7 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + pair_dq_warps(D)), 1) prefi
         // a warp whose 32 rows are all past the call's rows only keeps the barrier protocol (as in pa_prefill.cuh)
         const bool pad = NT == 1 && row0 + t * 2 * BM + cr * BM + wq * 32 >= p.rows;   // (NT = 1: registers, as there)
         float m_used = -INFINITY, l = 0.f;
+        float m_row = -INFINITY;   // the row's exact maximum (log2 units); O and l are reported against it
         for (uint32_t j = 0; j < nblk; j++) {
             const uint32_t b = j & 1;
             if (!wait(&s_full[t], j & 1)) break;
@@ -393,6 +397,7 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + pair_dq_warps(D)), 1) prefi
             for (int i = 1; i + 1 < BN; i += 2) mx = max3(mx, s[i], s[i + 1]);
             mx = fmaxf(mx, s[BN - 1]);
             mx *= LOG2E;
+            m_row = fmaxf(m_row, mx);
             float alpha = 1.f;
             bool rescale = false;
             if (j == 0) m_used = mx;
@@ -443,10 +448,12 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + pair_dq_warps(D)), 1) prefi
             __syncwarp();
             if (lane == 0) mbar_arrive_cl(lead(&p_full[2 * t + b]));
         }
+        // O and l moved from the lazy reference max m_used to the row's exact maximum (as in pa_prefill.cuh)
         if (ok && !pad && nblk > 0 && wait(&o_ready[t], 0)) {
             tc_fence_after();
             const uint32_t row = row0 + t * 2 * BM + cr * BM + r;
             const uint64_t orow = ((uint64_t) job.slot * p.nkv + h) * p.rows + row;
+            const float fix = m_row > -INFINITY ? ex2(m_used - m_row) : 1.f;
 #pragma unroll
             for (int q = 0; q < D / 32; q++) {
                 float o[32];
@@ -455,12 +462,13 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + pair_dq_warps(D)), 1) prefi
                 if (row < p.rows) {
                     float4 *dst = reinterpret_cast<float4 *>(p.Op + orow * D + q * 32);
 #pragma unroll
-                    for (int i = 0; i < 8; i++) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+                    for (int i = 0; i < 8; i++)
+                        dst[i] = make_float4(o[4 * i] * fix, o[4 * i + 1] * fix, o[4 * i + 2] * fix, o[4 * i + 3] * fix);
                 }
             }
             if (row < p.rows) {
-                p.Mp[orow] = l > 0.f ? m_used * (1.0f / LOG2E) : -INFINITY;
-                p.Lp[orow] = l;
+                p.Mp[orow] = l > 0.f ? m_row * (1.0f / LOG2E) : -INFINITY;
+                p.Lp[orow] = l * fix;
             }
         }
     } else {

@@ -154,16 +154,42 @@ int pa_cuda_merge_gathered(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, uint32_
  * layer (the N-GPU generalisation of the Mac + phone and two-phone split, docs/TWO-PHONES.md:14-18). NCCL is opened
  * (dlopen of libnccl.so.2) on first use; these calls fail with PA_CUDA_ENCCL when it cannot be.
  * pa_cuda_nccl_unique_id: on one rank, the id (`bytes` >= 128) that every rank then passes to
- * pa_cuda_nccl_comm_create, which returns a communicator over the context's device (an opaque handle: ncclComm_t). */
+ * pa_cuda_nccl_comm_create, which returns a communicator over the context's device (an opaque handle that wraps an
+ * ncclComm_t; destroyed with pa_cuda_nccl_comm_destroy, also after an abort). */
 int pa_cuda_nccl_unique_id(void *id, size_t bytes);
 int pa_cuda_nccl_comm_create(pa_cuda_ctx *ctx, const void *id, int rank, int world, void **comm);
 void pa_cuda_nccl_comm_destroy(void *comm);
-/* Runs this rank's plan (its shard's segments) into a packed (O, m, l), all-gathers every rank's on `stream` with one
- * ncclAllGather, and folds them by log-sum-exp (pa_cuda_merge_gathered) into O, m, l, identical on every rank. Every
- * rank calls it, in the same order, with plans of the same n_sets and shape. Asynchronous; the packed and gathered
- * buffers are the context's own (grown as needed). */
+/* Runs this rank's plan (its shard's segments) into a packed (O, m, l), exchanges the ranks' partials on `stream`, and
+ * folds them by log-sum-exp into O, m, l, identical on every rank. Every rank calls it, in the same order, with plans of
+ * the same n_sets and shape, and the same exchange settings. The exchange (pa_cuda_set_shard_exchange):
+ *   all-gather: one ncclAllGather of every rank's packed (O, m, l), then the fold (pa_cuda_merge_gathered): each rank
+ *     receives N-1 partials. The choice by size for small partials (decode) and for 2 ranks.
+ *   all-reduce: the rows' maxima over the ranks (ncclAllReduce MAX straight into m), each rank's (O, l) moved to them,
+ *     then summed (ncclAllReduce SUM into O and l): ~2(N-1)/N of a partial per rank. The choice by size from 8 MiB of
+ *     partial per rank with more than 2 ranks (prefill).
+ * Set groups (pa_cuda_set_shard_groups): the plan's output sets are split into G contiguous groups; group g's exchange
+ * runs on a second stream while the kernels of group g+1 run (by size: 8 groups from 64 MiB of partial per rank).
+ * Asynchronous unless a bound is set (pa_cuda_set_shard_timeout_ms); the packed and gathered buffers are the context's
+ * own (grown as needed). */
 int pa_cuda_shard_attn_allgather_merge(pa_cuda_plan *plan, const uint16_t *Qs, void *comm, float *O, float *m, float *l,
                                        void *stream);
+/* Exchange of pa_cuda_shard_attn_allgather_merge for calls made afterwards: 0 = by size (default), 1 = all-gather and
+ * fold, 2 = max / sum all-reduces. */
+void pa_cuda_set_shard_exchange(pa_cuda_ctx *ctx, int mode);
+/* Output-set groups of pa_cuda_shard_attn_allgather_merge whose exchange overlaps the next group's kernels: 0 = by size
+ * (default), 1 = no overlap, G > 1 = G groups (at most n_sets). */
+void pa_cuda_set_shard_groups(pa_cuda_ctx *ctx, int groups);
+/* Bound on the shard exchange (the B200 counterpart of the client's bounded reply wait, phone-attn/phone-attn.h:796-820):
+ * with ms > 0, pa_cuda_shard_attn_allgather_merge returns only once its work on the stream has finished, polling the
+ * stream and ncclCommGetAsyncError. On an NCCL error, or when ms pass first (a rank that left or stalled keeps the
+ * collective waiting), it aborts the communicator (ncclCommAbort: the collectives in flight return and the stream
+ * drains) and returns PA_CUDA_ENCCL or PA_CUDA_ETIMEOUT; O, m and l are then undefined and the communicator fails every
+ * later call (destroy it and create a new one). 0 = asynchronous (default). */
+void pa_cuda_set_shard_timeout_ms(pa_cuda_ctx *ctx, uint32_t ms);
+/* The same bounded wait for callers of the asynchronous mode: waits for the work queued on `stream` (NULL = the
+ * context's stream), polling NCCL's asynchronous error, and aborts the communicator on an error or after timeout_ms
+ * (0 = no bound). */
+int pa_cuda_nccl_wait(pa_cuda_ctx *ctx, void *comm, void *stream, uint32_t timeout_ms);
 /* O/l -> f16 Oh, lse = m + log l (device) */
 int pa_cuda_normalize(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, const float *O, const float *m, const float *l,
                       uint16_t *Oh, float *lse, void *stream);
@@ -211,8 +237,11 @@ uint64_t pa_cuda_graph_calls(const pa_cuda_ctx *ctx);
  *   Limit: one chunk partial, nkv * rows * (hd + 2) * 4 bytes, must fit the 16 MiB array (up to 2048 chunks are used);
  *   a larger shape returns PA_CUDA_EUNSUPPORTED with the reason in *why (a static string; why may be null).
  *   Set-up: the first call on a device looks the array's device address up (cudaGetSymbolAddress, with that device
- *   current); make that first call before any stream capture. Every GPU that loads the library holds the array until
- *   the process exits.
+ *   current); make that first call before any stream capture. Under CUDA's lazy module loading (the default) that first
+ *   call is also when the library's kernels and the 16 MiB array are loaded onto the device: a host that reserves all
+ *   free device memory for its own pool makes the first call before reserving it, or leaves ~16 MiB plus the module
+ *   free. Every GPU that loads the library holds the array until the process exits. The address is kept per device for
+ *   the life of the process, so a process that calls cudaDeviceReset does not use this entry point afterwards.
  *   Sharing: all calls on a device share the one array and it keeps the last call's contents (each call rewrites what
  *   it reads); calls that overlap on the GPU (other streams, other host threads) race and must be serialised.
  *   The call returns after the stream has synchronised: PA_CUDA_OK, or PA_CUDA_ETIMEOUT if a bounded wait ran out.

@@ -58,6 +58,9 @@ def _check(O, m, l, ref, sample):
     e = orc.rel_err(O[:, sample], m[:, sample], l[:, sample], Or.astype(np.float64), mr.astype(np.float64),
                     lr.astype(np.float64))
     assert e[0] <= TOL and e[1] <= TOL, e
+    valid = lr > 0
+    dm = np.abs(m[:, sample].astype(np.float64) - mr.astype(np.float64))[valid].max() if valid.any() else 0.0
+    assert dm <= TOL, ("m is not the row maximum", dm)
     return e
 
 

@@ -46,6 +46,12 @@ def _check(c, O, m, l, nk, tol_f64=TOL_F64):
     e32 = orc.rel_err(O, m, l, O3.astype(np.float64), m3.astype(np.float64), l3.astype(np.float64))
     assert e32[0] <= TOL_REF and e32[1] <= TOL_REF, ("vs reference arithmetic", e32)
     assert e64[0] <= tol_f64 and e64[1] <= tol_f64, ("vs fp64", e64)
+    # m itself is the row's exact maximum score, as sme_attn_partial returns it (scripts/sme/sme_attn.c:281,222-227),
+    # on every kernel: not only a reference point that O and l are relative to
+    valid = l3 > 0
+    if valid.any():
+        dm = np.abs(np.asarray(m, np.float64) - m3.astype(np.float64))[valid].max()
+        assert dm <= TOL_REF, ("m vs reference arithmetic", dm)
     if nk == 0:
         assert np.all(l == 0) and np.all(np.isneginf(m)) and np.all(O == 0)
     return e32, e64

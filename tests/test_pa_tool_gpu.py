@@ -60,3 +60,39 @@ def test_reference_pa_tool_against_cuda_engine(env, nkeys, extra):
     finally:
         srv.kill()
         srv.wait()
+
+
+CLIENT = os.path.join(REF, "pa-client-check")
+
+
+@pytest.mark.skipif(not (os.path.exists(SERVE) and os.path.exists(CLIENT)),
+                    reason="oracle/_ref binaries not built (they need the reference tree at build time)")
+@pytest.mark.parametrize("quant", ["1", "2"])
+def test_store_protocol_truncate_fetch_against_cuda_engine(quant):
+    """The rest of the store protocol through pa::cuda_engine's managed pages: the reference's own pa::client
+    (oracle/_ref/pa-client-check) APPENDs, ATTNs, TRUNCATEs into the middle of a page and to a page boundary, ATTNs over
+    the kept keys, FETCHes rows the GPU has read, APPENDs new rows over the truncated range (the cut page rewritten at
+    the key count it had before) and ATTNs again; every reply is checked against the fp64 oracle over exactly the keys
+    held at that point (pa-tool's 5e-3 gate), every FETCH byte for byte (phone-attn/phone-attn.h:399-465, :766-770)."""
+    port = _free_port()
+    srv = subprocess.Popen([SERVE, str(port), "2"], stdout=subprocess.DEVNULL, stderr=subprocess.PIPE, text=True)
+    try:
+        deadline = time.time() + 60
+        while True:
+            assert srv.poll() is None, srv.stderr.read()
+            try:
+                with socket.create_connection(("127.0.0.1", port), timeout=1.0):
+                    break
+            except OSError:
+                if time.time() > deadline:
+                    raise
+                time.sleep(0.2)
+        out = subprocess.run([CLIENT, "127.0.0.1", str(port), quant], capture_output=True, text=True, timeout=300)
+        text = out.stdout + out.stderr
+        print(text)
+        assert out.returncode == 0, text
+        assert "ALL PASS" in text and "FAIL" not in text, text
+        assert "engine=pa-cuda" in text, text
+    finally:
+        srv.kill()
+        srv.wait()
