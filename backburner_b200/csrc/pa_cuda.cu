@@ -307,11 +307,17 @@ cudaError_t launch_decode_any(const pa_cuda_plan *p, uint32_t nj, const pa::dec:
     return p->w == 4 ? launch_decode_q<256, 4>(p, nj, prm, st, quant) : launch_decode_q<256, 8>(p, nj, prm, st, quant);
 }
 
+// The merge over the parts of each output row: 8 warps per row when the rows are few (8 warps each would still fit the
+// SMs twice over) and the sets have many parts, else one warp per row
 template <int HD>
-cudaError_t launch_merge(const pa::mrg::Params &mp, cudaStream_t st) {
-    const uint64_t warps = (uint64_t) mp.n_sets * mp.rows_per_set;
-    if (warps == 0) return cudaSuccess;
-    pa::mrg::merge_kernel<HD><<<(unsigned) ((warps + 7) / 8), 256, 0, st>>>(mp);
+cudaError_t launch_merge(const pa::mrg::Params &mp, cudaStream_t st, int n_sm) {
+    const uint64_t rows = (uint64_t) mp.n_sets * mp.rows_per_set;
+    if (rows == 0) return cudaSuccess;
+    const uint64_t parts_per_set = mp.n_sets ? ((uint64_t) mp.n_parts + mp.n_sets - 1) / mp.n_sets : 0;
+    if (rows * 8 <= (uint64_t) n_sm * 128 && parts_per_set >= 8)
+        pa::mrg::merge_kernel<HD, 8><<<(unsigned) rows, 256, 0, st>>>(mp);
+    else
+        pa::mrg::merge_kernel<HD, 1><<<(unsigned) ((rows + 7) / 8), 256, 0, st>>>(mp);
     return cudaGetLastError();
 }
 
@@ -410,7 +416,7 @@ int run_plan_sets(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float
     mp.rows_per_set = (uint64_t) sh.nkv * sh.rows;
     mp.n_sets = s1 - s0;
     mp.fold = 0;
-    cudaError_t e = sh.hd == 128 ? launch_merge<128>(mp, st) : launch_merge<256>(mp, st);
+    cudaError_t e = sh.hd == 128 ? launch_merge<128>(mp, st, ctx->n_sm) : launch_merge<256>(mp, st, ctx->n_sm);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "merge kernel launch");
     ctx->launches++;
     return PA_CUDA_OK;
@@ -944,7 +950,8 @@ int pa_cuda_merge(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, uint32_t n_parts
     prm.rows_per_set = rows;
     prm.n_sets = 1;
     prm.fold = fold ? 1 : 0;
-    cudaError_t e = hd == 128 ? launch_merge<128>(prm, pick(ctx, stream)) : launch_merge<256>(prm, pick(ctx, stream));
+    cudaError_t e = hd == 128 ? launch_merge<128>(prm, pick(ctx, stream), ctx->n_sm)
+                              : launch_merge<256>(prm, pick(ctx, stream), ctx->n_sm);
     PA_CK(e, "merge launch");
     ctx->launches++;
     return PA_CUDA_OK;
@@ -972,7 +979,8 @@ int pa_cuda_merge_gathered(pa_cuda_ctx *ctx, uint32_t hd, uint64_t rows, uint32_
     prm.rows_per_set = rows;
     prm.n_sets = 1;
     prm.fold = fold ? 1 : 0;
-    cudaError_t e = hd == 128 ? launch_merge<128>(prm, pick(ctx, stream)) : launch_merge<256>(prm, pick(ctx, stream));
+    cudaError_t e = hd == 128 ? launch_merge<128>(prm, pick(ctx, stream), ctx->n_sm)
+                              : launch_merge<256>(prm, pick(ctx, stream), ctx->n_sm);
     PA_CK(e, "merge launch");
     ctx->launches++;
     return PA_CUDA_OK;
@@ -1061,7 +1069,13 @@ int pa_cuda_shard_attn_allgather_merge(pa_cuda_plan *p, const uint16_t *Qs, void
     if (rc) return rc;
     cudaStream_t st = pick(ctx, stream), xs = st;
     if (G > 1) {
-        if (!ctx->xstream) PA_CK(cudaStreamCreateWithFlags(&ctx->xstream, cudaStreamNonBlocking), "exchange stream");
+        if (!ctx->xstream) {
+            // the highest priority: the block scheduler hands freed SMs to the exchange's kernels (NCCL, the fold)
+            // before the remaining CTAs of the next group's attention kernel, so the exchange really overlaps it
+            int least = 0, greatest = 0;
+            PA_CK(cudaDeviceGetStreamPriorityRange(&least, &greatest), "stream priorities");
+            PA_CK(cudaStreamCreateWithPriority(&ctx->xstream, cudaStreamNonBlocking, greatest), "exchange stream");
+        }
         while (ctx->xev.size() < G + 1) {
             cudaEvent_t e;
             PA_CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event create");
@@ -1563,7 +1577,7 @@ extern "C" int pa_cuda_attn_noalloc(const pa_cuda_shape *shape, const uint16_t *
     mp.rows_per_set = rows_all;
     mp.n_sets = 1;
     mp.fold = 0;
-    if ((shape->hd == 128 ? launch_merge<128>(mp, st) : launch_merge<256>(mp, st)) != cudaSuccess)
+    if ((shape->hd == 128 ? launch_merge<128>(mp, st, n_sm) : launch_merge<256>(mp, st, n_sm)) != cudaSuccess)
         return na_fail(why, PA_CUDA_ECUDA, "merge kernel launch failed");
     if (cudaStreamSynchronize(st) != cudaSuccess) return na_fail(why, PA_CUDA_ECUDA, "stream synchronize failed");
     int h = 0;

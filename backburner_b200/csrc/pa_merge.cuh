@@ -6,7 +6,8 @@
 //     (O, M, L) as one more part.
 //   merge_partial (phone-attn/phone-attn.h:231-239): a part with l <= 0 contributes nothing.
 //   attn_core's normalisation (phone-attn/phone-attn.h:651-655): O/l rounded to f16, lse = m + log l (-inf if l == 0).
-// One warp per output row; each lane owns hd/32 consecutive head dims (float4 loads).
+// merge_kernel: one warp per output row (or 8 for calls with few rows and many parts); each lane owns hd/32
+// consecutive head dims (float4 loads).
 #pragma once
 #include "pa_common.cuh"
 
@@ -25,36 +26,59 @@ struct Params {
     int fold;                    // 1: (O, M, L) already hold a partial to fold in
 };
 
-template <int HD>
+// SPLIT warps per output row (1: 8 rows per 256-thread block; 8: one row per block, for calls with few rows and many
+// parts, where one warp walking every part of its row would leave the GPU idle). The row's parts are dealt out to its
+// warps; each warp takes the maxima of its parts with its lanes in parallel, the row maximum M is agreed through shared
+// memory, and every warp accumulates sum_c w_c O_c, sum_c w_c l_c against that same M, so the warps' sums simply add.
+// Weights are computed 32 parts at a time (one per lane) and broadcast; the O loads of a batch do not depend on one
+// another, and a part with l <= 0 (no keys) gets weight 0 and its O is not used.
+template <int HD, int SPLIT>
 __global__ void __launch_bounds__(256) merge_kernel(const Params p) {
-    constexpr int V = HD / 32;   // floats per lane
-    const uint64_t gw = (uint64_t) blockIdx.x * 8 + threadIdx.x / 32;
-    const uint32_t lane = threadIdx.x % 32;
-    if (gw >= (uint64_t) p.n_sets * p.rows_per_set) return;
-    const uint32_t s = (uint32_t) (gw / p.rows_per_set);
-    const uint64_t R = gw % p.rows_per_set;
-    const uint32_t c0 = p.c_range ? p.c_range[s] : 0, c1 = p.c_range ? p.c_range[s + 1] : p.n_parts;
+    constexpr int V = HD / 32;          // floats per lane
+    constexpr int RPB = 8 / SPLIT;      // rows per block
+    __shared__ float s_m[8];
+    __shared__ float s_l[8];
+    __shared__ __align__(16) float s_acc[SPLIT > 1 ? 8 * HD : 4];
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32, sw = warp % SPLIT;
+    const uint64_t gw = (uint64_t) blockIdx.x * RPB + warp / SPLIT;
+    const bool active = gw < (uint64_t) p.n_sets * p.rows_per_set;
+    const uint32_t s = active ? (uint32_t) (gw / p.rows_per_set) : 0;
+    const uint64_t R = active ? gw % p.rows_per_set : 0;
+    const uint32_t c0 = !active ? 0 : p.c_range ? p.c_range[s] : 0;
+    const uint32_t c1 = !active ? 0 : p.c_range ? p.c_range[s + 1] : p.n_parts;
     const uint64_t orow = (uint64_t) s * p.rows_per_set + R;
+    const uint64_t rr = (uint64_t) s * p.set_rows + R;
 
-    float M = -INFINITY;
+    // ---- the row maximum over the parts with keys (and the partial already in O, M, L when folding)
     float m_in = -INFINITY, l_in = 0.f;
-    if (p.fold) {
+    const bool fold = active && p.fold && sw == 0;
+    if (fold) {
         m_in = p.M[orow];
         l_in = p.L[orow];
-        if (l_in > 0.f) M = m_in;
     }
-    const uint64_t rr = (uint64_t) s * p.set_rows + R;
-    for (uint32_t c = c0; c < c1; c++) {
+    float M = (fold && l_in > 0.f) ? m_in : -INFINITY;
+    for (uint32_t c = c0 + sw + SPLIT * lane; c < c1; c += 32 * SPLIT) {
         const uint64_t pr = (uint64_t) c * p.ml_stride + rr;
         if (p.Lp[pr] > 0.f) M = fmaxf(M, p.Mp[pr]);
     }
+#pragma unroll
+    for (int x = 16; x > 0; x >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, x));
+    if (SPLIT > 1) {
+        if (lane == 0) s_m[warp] = M;
+        __syncthreads();
+        const uint32_t w0 = (warp / SPLIT) * SPLIT;
+#pragma unroll
+        for (int w = 0; w < SPLIT; w++) M = fmaxf(M, s_m[w0 + w]);
+    }
+
+    // ---- sum_c w_c O_c and sum_c w_c l_c against M
     float acc[V];
-    float L = 0.f;
 #pragma unroll
     for (int i = 0; i < V; i++) acc[i] = 0.f;
-    if (p.fold && l_in > 0.f) {
+    float Ls = 0.f;   // this lane's share of the weighted l
+    if (fold && l_in > 0.f) {
         const float w = ex2((m_in - M) * LOG2E);
-        L = w * l_in;
+        if (lane == 0) Ls = w * l_in;
         const float4 *src = reinterpret_cast<const float4 *>(p.O + orow * HD + lane * V);
 #pragma unroll
         for (int i = 0; i < V / 4; i++) {
@@ -62,28 +86,62 @@ __global__ void __launch_bounds__(256) merge_kernel(const Params p) {
             acc[4 * i] = w * x.x; acc[4 * i + 1] = w * x.y; acc[4 * i + 2] = w * x.z; acc[4 * i + 3] = w * x.w;
         }
     }
-    for (uint32_t c = c0; c < c1; c++) {
-        const uint64_t pr = (uint64_t) c * p.ml_stride + rr;
-        const float lc = p.Lp[pr];
-        if (!(lc > 0.f)) continue;
-        const float w = ex2((p.Mp[pr] - M) * LOG2E);
-        L = fmaf(w, lc, L);
-        const float4 *src = reinterpret_cast<const float4 *>(p.Op + (uint64_t) c * p.op_stride + rr * HD + lane * V);
+    for (uint32_t cb = c0 + sw; cb < c1; cb += 32 * SPLIT) {
+        const uint32_t c = cb + SPLIT * lane;
+        float w = 0.f;
+        if (c < c1) {
+            const uint64_t pr = (uint64_t) c * p.ml_stride + rr;
+            const float lc = p.Lp[pr];
+            if (lc > 0.f) {
+                w = ex2((p.Mp[pr] - M) * LOG2E);
+                Ls = fmaf(w, lc, Ls);
+            }
+        }
+        const uint32_t nb = min(32u, (c1 - cb + SPLIT - 1) / SPLIT);
+#pragma unroll 4
+        for (uint32_t j = 0; j < nb; j++) {
+            const float wj = __shfl_sync(0xffffffffu, w, j);
+            const float4 *src =
+                reinterpret_cast<const float4 *>(p.Op + (uint64_t) (cb + SPLIT * j) * p.op_stride + rr * HD + lane * V);
 #pragma unroll
-        for (int i = 0; i < V / 4; i++) {
-            const float4 x = src[i];
-            acc[4 * i] = fmaf(w, x.x, acc[4 * i]);
-            acc[4 * i + 1] = fmaf(w, x.y, acc[4 * i + 1]);
-            acc[4 * i + 2] = fmaf(w, x.z, acc[4 * i + 2]);
-            acc[4 * i + 3] = fmaf(w, x.w, acc[4 * i + 3]);
+            for (int i = 0; i < V / 4; i++) {
+                const float4 x = src[i];
+                if (wj != 0.f) {   // a part without keys (l <= 0) may hold anything in O
+                    acc[4 * i] = fmaf(wj, x.x, acc[4 * i]);
+                    acc[4 * i + 1] = fmaf(wj, x.y, acc[4 * i + 1]);
+                    acc[4 * i + 2] = fmaf(wj, x.z, acc[4 * i + 2]);
+                    acc[4 * i + 3] = fmaf(wj, x.w, acc[4 * i + 3]);
+                }
+            }
         }
     }
+#pragma unroll
+    for (int x = 16; x > 0; x >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, x);
+    if (SPLIT > 1) {
+        // the row's warps add their sums through shared memory; the row's first warp writes the result
+        float4 *mine = reinterpret_cast<float4 *>(s_acc + warp * HD + lane * V);
+#pragma unroll
+        for (int i = 0; i < V / 4; i++) mine[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+        if (lane == 0) s_l[warp] = Ls;
+        __syncthreads();
+        if (sw != 0) return;
+        for (int w = 1; w < SPLIT; w++) {
+            const float4 *o = reinterpret_cast<const float4 *>(s_acc + (warp + w) * HD + lane * V);
+#pragma unroll
+            for (int i = 0; i < V / 4; i++) {
+                const float4 x = o[i];
+                acc[4 * i] += x.x; acc[4 * i + 1] += x.y; acc[4 * i + 2] += x.z; acc[4 * i + 3] += x.w;
+            }
+            Ls += s_l[warp + w];
+        }
+    }
+    if (!active) return;
     float4 *dst = reinterpret_cast<float4 *>(p.O + orow * HD + lane * V);
 #pragma unroll
     for (int i = 0; i < V / 4; i++) dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
     if (lane == 0) {
-        p.M[orow] = L > 0.f ? M : -INFINITY;
-        p.L[orow] = L;
+        p.M[orow] = Ls > 0.f ? M : -INFINITY;
+        p.L[orow] = Ls;
     }
 }
 

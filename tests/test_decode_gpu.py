@@ -218,6 +218,43 @@ def test_merge_kernel_matches_oracle(ctx, hd):
     np.testing.assert_allclose(out[2].cpu().numpy(), lc, rtol=2e-5)
 
 
+@pytest.mark.parametrize("hd,n,rows", [(128, 100, 24), (256, 257, 6), (128, 9, 40), (256, 33, 3000)])
+def test_merge_many_parts_matches_oracle(ctx, hd, n, rows):
+    """Few rows with many parts (the merge deals a row's parts out to 8 warps) and many rows (one warp per row): empty
+    parts (l = 0) whose O holds NaN must add nothing, as merge_partial skips them; the fold takes one more part."""
+    import torch
+    rng = np.random.default_rng(hd + n + rows)
+    Op = rng.standard_normal((n, rows, hd)).astype(np.float32)
+    mp = (rng.standard_normal((n, rows)) * 4).astype(np.float32)
+    lp = (np.abs(rng.standard_normal((n, rows))) + 0.1).astype(np.float32)
+    empty = rng.random((n, rows)) < 0.2
+    lp[empty] = 0.0
+    mp[empty] = -np.inf
+    Op[empty] = np.nan
+    lp[:, 1] = 0.0
+    mp[:, 1] = -np.inf           # a row with no keys anywhere
+    Op[:, 1] = np.nan
+    O, m, l = pa.merge(ctx, hd, _dev(Op), _dev(mp), _dev(lp))
+    torch.cuda.synchronize()
+    Or, mr, lr = orc.merge_slots(np.where(np.isnan(Op), 0, Op), mp, lp)
+    np.testing.assert_allclose(O.cpu().numpy(), Or, rtol=3e-5, atol=3e-5)
+    np.testing.assert_allclose(l.cpu().numpy(), lr, rtol=3e-5)
+    np.testing.assert_array_equal(m.cpu().numpy()[lr > 0], mr[lr > 0])
+    assert np.isneginf(m.cpu().numpy()[1]) and l.cpu().numpy()[1] == 0 and np.all(O.cpu().numpy()[1] == 0)
+    O0 = rng.standard_normal((rows, hd)).astype(np.float32)
+    m0 = rng.standard_normal(rows).astype(np.float32)
+    l0 = (np.abs(rng.standard_normal(rows)) + 0.1).astype(np.float32)
+    out = (_dev(O0), _dev(m0), _dev(l0))
+    pa.merge(ctx, hd, _dev(Op), _dev(mp), _dev(lp), out=out, fold=True)
+    torch.cuda.synchronize()
+    Oc, mc, lc = O0.copy(), m0.copy(), l0.copy()
+    Om = np.where(np.isnan(Op), 0, Op)
+    for c in range(n):
+        orc.merge_partial(Oc, mc, lc, Om[c], mp[c], lp[c])
+    np.testing.assert_allclose(out[0].cpu().numpy(), Oc, rtol=3e-5, atol=3e-5)
+    np.testing.assert_allclose(out[2].cpu().numpy(), lc, rtol=3e-5)
+
+
 def test_normalize_matches_attn_core(ctx):
     import torch
     rng = np.random.default_rng(2)
