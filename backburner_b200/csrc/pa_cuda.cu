@@ -37,6 +37,11 @@ constexpr uint32_t kPrefillMinRows128 = 24, kPrefillMinRows256 = 32;
 // filled tile. Measured (8 KV heads x 4 layers x 65,536 Q8_0 keys, TFLOP/s single vs pair): 256 rows 676 vs 558,
 // 320 510 vs 549, 384 608 vs 643, 448 667 vs 694, 512 751 vs 784
 constexpr uint32_t kPairMinRows = 257;
+// Per-job overhead of the decode kernel in keys, for the job-size model of pa_cuda_plan_create. Fitted on B200 to
+// config-1 runs of the current kernel (kernel ms, 64 layers): 131,072 keys per layer as 2,048-key jobs 3.618, 4,096
+// 3.600, 8,192 3.708, 14,592 3.684; 16,384 keys per layer (an 8-way shard) as 1,024 0.491, 1,856 0.487, 2,048 0.535,
+// 4,096 0.532. (A persistent variant, each CTA taking several jobs through one stage stream, measured no better.)
+constexpr uint32_t kDecodeJobOverhead = 48;
 
 struct Plan;
 
@@ -105,7 +110,7 @@ struct pa_cuda_plan {
     float *d_op = nullptr, *d_mp = nullptr, *d_lp = nullptr;
     size_t scratch = 0;
     // decode launch shape
-    uint32_t hg = 1, rgc = 1, n_rg = 1, pw = 1, n_consumers = 1, row = 0, gs = 0, grid_y = 1, w = 8;
+    uint32_t hg = 1, rgc = 1, n_rg = 1, n_consumers = 1, row = 0, gs = 0, grid_y = 1, w = 8;
     size_t smem = 0;
     // tcgen05 path (many query rows per KV head, hd 128): tiles of NT x 128 rows (NT x 256 on a CTA pair), tensor
     // maps of the K/V segments
@@ -183,9 +188,7 @@ int plan_decode_shape(pa_cuda_ctx *ctx, pa_cuda_plan *p) {
     p->hg = hg;
     p->rgc = std::min(p->n_rg, maxw / hg);
     const uint32_t S = hg * p->rgc;
-    // two warps per stream split a stage's tiles; with one tile per stage each stream has one warp
-    p->pw = (pa::dec::stage_keys((int) sh.hd) / pa::dec::TILE_KEYS >= 2 && 2 * S <= maxw) ? 2 : 1;
-    p->n_consumers = S * p->pw;
+    p->n_consumers = S;   // one warp per (head, row group) stream
     p->grid_y = (sh.nkv / hg) * ((p->n_rg + p->rgc - 1) / p->rgc);
     p->row = (uint32_t) (hg * sh.hb);                  // a multiple of 16 by the choice of hg
     p->gs = pair_stride(p->row);
@@ -267,12 +270,13 @@ cudaError_t launch_prefill_pair(const pa_cuda_plan *p, uint32_t nj, const CUtens
     return e != cudaSuccess ? e : cudaGetLastError();
 }
 
+// grid x: CTAs along the jobs (each takes jobs x, x + grid_x, ...; at most prm.n_jobs)
 template <int HD, int Q, int W>
-cudaError_t launch_decode(const pa_cuda_plan *p, uint32_t nj, const pa::dec::Params &prm, cudaStream_t st) {
+cudaError_t launch_decode(const pa_cuda_plan *p, uint32_t grid_x, const pa::dec::Params &prm, cudaStream_t st) {
     auto kern = pa::dec::decode_kernel<HD, Q, W>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) p->smem);
     if (e != cudaSuccess) return e;
-    dim3 grid(nj, p->grid_y);
+    dim3 grid(grid_x, p->grid_y);
     kern<<<grid, 32 * p->n_consumers, p->smem, st>>>(prm);
     return cudaGetLastError();
 }
@@ -386,7 +390,7 @@ int run_plan_sets(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float
         prm.n_rg = p->n_rg;
         prm.row = p->row;
         prm.gs = p->gs;
-        prm.pw = p->pw;
+        prm.n_jobs = nj;
         prm.n_consumers = p->n_consumers;
         prm.timeout_ns = ctx->timeout_ns;
         prm.stall = ctx->stall_test;
@@ -701,10 +705,10 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
         const uint64_t jobs_wanted = std::max<uint64_t>(1, ((uint64_t) ctx->n_sm * 4 + ctas_per_job - 1) / ctas_per_job);
         chunk = (uint32_t) std::max<uint64_t>(1024, (total + jobs_wanted - 1) / jobs_wanted);
     } else if (chunk == 0) {
-        // The job size that minimises the modelled time: waves x (keys per job + a per-job overhead worth ~150 keys,
-        // fitted on B200 from config-1 runs: 1M keys took 3,233 GB/s as 448-key jobs, 3,898 as 1,024, 4,142 as 3,584
-        // and 3,682 as 8,192, the last being less than one wave). Waves count the CTAs that fit the SMs at once.
+        // The job size that minimises the modelled time: waves x (keys per job + kDecodeJobOverhead). Waves count the
+        // CTAs that fit all SMs at once.
         const uint32_t slots = (uint32_t) ctx->n_sm * (uint32_t) decode_ctas_per_sm(p);
+        const uint32_t overhead = kDecodeJobOverhead;
         uint64_t best = ~0ull;
         for (uint32_t c = 128; c <= 16384; c += 64) {
             uint64_t jobs = 0, cmax = 0;
@@ -716,7 +720,7 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
                 cmax = std::max<uint64_t>(cmax, cj);
             }
             const uint64_t waves = (jobs * p->grid_y + slots - 1) / slots;
-            const uint64_t cost = waves * (cmax + 150);
+            const uint64_t cost = waves * (cmax + overhead);
             if (cost <= best) { best = cost; chunk = c; }
         }
         if (!chunk) chunk = 128;
@@ -1554,7 +1558,7 @@ extern "C" int pa_cuda_attn_noalloc(const pa_cuda_shape *shape, const uint16_t *
         prm.n_rg = p.n_rg;
         prm.row = p.row;
         prm.gs = p.gs;
-        prm.pw = p.pw;
+        prm.n_jobs = n_jobs;
         prm.n_consumers = p.n_consumers;
         prm.timeout_ns = 2000000000ull;
         prm.stall = 0;

@@ -68,7 +68,7 @@ struct Params {
     uint32_t n_rg;        // 8-row groups in total = ceil(rows / 8)
     uint32_t row;         // bytes of one key row in shared memory (= hg * hb, a multiple of 16)
     uint32_t gs;          // shared-memory stride of a pair of key rows (multiple of 16, odd number of 16-byte units)
-    uint32_t pw;          // consumer warps per (head, row group): 1 or 2 (they split the 16-key tiles)
+    uint32_t n_jobs;      // jobs of the launch: CTA x takes jobs x, x + gridDim.x, ...
     uint32_t n_consumers; // warps per CTA (launch shape)
     uint64_t timeout_ns;
     int stall;            // test hook: consumers first wait on a barrier that nothing completes (bounded)
@@ -136,6 +136,11 @@ __device__ __forceinline__ void q4_word(uint32_t w, uint32_t s2, uint32_t &l02, 
 }
 
 // ---------------------------------------------------------------- the kernel
+// CTA x of the launch takes jobs x, x + gridDim.x, x + 2 gridDim.x, ... of p.jobs[0, p.n_jobs); the plans launch one
+// CTA per job (measured faster than fewer CTAs taking several jobs each: the block scheduler balances the jobs). The
+// stages of a CTA's jobs, in order, are one stream g = 0, 1, 2, ... through the ring: stage g lands in buffer
+// g % NSTAGE, so the copies of a next job's first stages are in flight while the previous job's last stages are
+// computed and its partial written.
 template <int HD, int QUANT, int W>
 __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const Params p) {
     constexpr int NMT = HD / 16;   // k-steps of QK^T = m-tiles of P.V
@@ -143,6 +148,7 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
     constexpr int NSTAGE = nstage(HD);
     constexpr int GB = q_group_bytes(QUANT);
     constexpr int PAIR = 2 * GB;   // bytes of an aligned pair of quant blocks
+    static_assert(STAGE_KEYS == TILE_KEYS, "a stage is one MMA tile of keys");
 
     extern __shared__ __align__(128) uint8_t smem[];
     const uint32_t row = p.row, gs = p.gs;
@@ -151,65 +157,73 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
     // shared-memory offset of key k of a stage (keys in pairs)
     auto kofs = [&](uint32_t k) -> uint32_t { return (k / 2) * gs + (k % 2) * row; };
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + NSTAGE * stage_bytes + SMEM_SLACK);
-    uint64_t *done = full + NSTAGE;    // every active warp is past the pipeline (stage memory is free)
-    uint64_t *xchg = done + 1;         // the second warp of each (head, row group) pair has published its partial
-    uint64_t *never = xchg + 1;        // completed by nobody: the stall test hook waits on it
+    uint64_t *never = full + NSTAGE;   // completed by nobody: the stall test hook waits on it
     uint32_t *released = reinterpret_cast<uint32_t *>(never + 1);   // per buffer: warps done with it, ever
-    uint32_t *issued = released + NSTAGE;                            // per buffer: the last stage issued into it
+    uint32_t *issued = released + NSTAGE;                            // per buffer: the last stream stage issued into it
     volatile int *abort_flag = reinterpret_cast<volatile int *>(issued + NSTAGE);
 
-    const Job job = p.jobs[blockIdx.x];
     const uint32_t n_hgroups = p.nkv / p.hg;
     const uint32_t hgi = blockIdx.y % n_hgroups, rbi = blockIdx.y / n_hgroups;
     const uint32_t h0 = hgi * p.hg;
     const uint32_t rg0 = rbi * p.rgc;
     const uint32_t nrg = min(p.rgc, p.n_rg - rg0);
-    const uint32_t S = p.hg * nrg;                // (head, row group) streams in this CTA
-    const uint32_t n_active = S * p.pw;           // warps with work
+    const uint32_t n_active = p.hg * nrg;         // warps with work: one per (head, row group) stream
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const uint32_t n_stages = (job.nk + STAGE_KEYS - 1) / STAGE_KEYS;
     const uint32_t copy_bytes = (uint32_t) (p.hg * p.hb);
-    const uint8_t *kb = job.k + (uint64_t) job.key0 * p.rs + h0 * p.hb;
-    const uint8_t *vb = job.v + (uint64_t) job.key0 * p.rs + h0 * p.hb;
+    constexpr uint32_t NEVER = 0xFFFFFFFFu;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < NSTAGE; s++) { mbar_init(&full[s], 1); released[s] = 0; issued[s] = 0; }
-        mbar_init(done, n_active);
-        mbar_init(xchg, S);
+        for (int s = 0; s < NSTAGE; s++) { mbar_init(&full[s], 1); released[s] = 0; issued[s] = NEVER; }
         mbar_init(never, 1);
         // a CTA started after another one gave up a wait does no work (a systematic failure ends in one timeout)
         *abort_flag = *(volatile int *) p.status != ST_OK;
         fence_mbar_init();
     }
     __syncthreads();
-    if (*abort_flag || warp >= n_active) return;
+    if (*abort_flag || warp >= n_active || blockIdx.x >= p.n_jobs) return;
 
-    // stage `it` into buffer it % NSTAGE: K rows then V rows, one bulk copy per key row (warp-collective)
-    auto issue = [&](uint32_t it) {
-        const uint32_t s = it % NSTAGE;
-        const uint32_t valid = min((uint32_t) STAGE_KEYS, job.nk - it * STAGE_KEYS);
+    auto stages_of = [&](uint32_t jn) -> uint32_t { return (p.jobs[jn].nk + STAGE_KEYS - 1) / STAGE_KEYS; };
+    // stage `it` of job `jn` as stream stage g, into buffer g % NSTAGE: K rows then V rows, one bulk copy per pair of
+    // key rows (warp-collective)
+    auto issue = [&](uint32_t jn, uint32_t it, uint32_t g) {
+        const Job jb = p.jobs[jn];
+        const uint32_t s = g % NSTAGE;
+        const uint32_t valid = min((uint32_t) STAGE_KEYS, jb.nk - it * STAGE_KEYS);
         if (lane == 0) {
-            issued[s] = it;
+            issued[s] = g;
             mbar_arrive_expect_tx(&full[s], 2u * valid * copy_bytes);
         }
         __syncwarp();
         if (2 * lane < valid) {   // lane copies keys 2*lane, 2*lane+1 (one row if the stage ends there)
-            const uint64_t off = (uint64_t) (it * STAGE_KEYS + 2 * lane) * p.rs;
+            const uint64_t off = (uint64_t) (jb.key0 + it * STAGE_KEYS + 2 * lane) * p.rs + h0 * p.hb;
+            const uint8_t *kb = jb.k + off, *vb = jb.v + off;
             const bool two = 2 * lane + 1 < valid;
             uint8_t *dst = smem + s * stage_bytes + lane * gs;
             if (p.rs == copy_bytes) {   // the head group is the whole position: the pair is one contiguous range
                 const uint32_t bytes = (two ? 2u : 1u) * copy_bytes;
-                bulk_g2s(dst, kb + off, bytes, &full[s]);
-                bulk_g2s(dst + half_stage, vb + off, bytes, &full[s]);
+                bulk_g2s(dst, kb, bytes, &full[s]);
+                bulk_g2s(dst + half_stage, vb, bytes, &full[s]);
             } else {                    // a head group of a wider (or padded) position: one copy per row
-                bulk_g2s(dst, kb + off, copy_bytes, &full[s]);
-                bulk_g2s(dst + half_stage, vb + off, copy_bytes, &full[s]);
+                bulk_g2s(dst, kb, copy_bytes, &full[s]);
+                bulk_g2s(dst + half_stage, vb, copy_bytes, &full[s]);
                 if (two) {
-                    bulk_g2s(dst + row, kb + off + p.rs, copy_bytes, &full[s]);
-                    bulk_g2s(dst + half_stage + row, vb + off + p.rs, copy_bytes, &full[s]);
+                    bulk_g2s(dst + row, kb + p.rs, copy_bytes, &full[s]);
+                    bulk_g2s(dst + half_stage + row, vb + p.rs, copy_bytes, &full[s]);
                 }
             }
         }
+    };
+    // stream stage g + NSTAGE, found from the caller's place in the stream (job jc, which starts at stream stage g0 and
+    // has nc stages): later in job jc, or in one of the CTA's next jobs (each has at least one stage)
+    auto issue_ahead = [&](uint32_t jc, uint32_t g0, uint32_t nc, uint32_t g) {
+        uint32_t target = g + NSTAGE - g0, jn = jc, n = nc;
+        while (target >= n) {
+            target -= n;
+            jn += gridDim.x;
+            if (jn >= p.n_jobs) return;
+            n = stages_of(jn);
+        }
+        issue(jn, target, g + NSTAGE);
     };
     // after a wait gave up: every copy issued so far lands before the CTA exits (warp 0 waits for them, bounded)
     auto abort_and_drain = [&]() {
@@ -219,22 +233,40 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
         }
         if (warp == 0 && lane == 0) {
             const uint64_t drain_ns = p.timeout_ns > DRAIN_NS ? p.timeout_ns : DRAIN_NS;
-            for (int s = 0; s < NSTAGE && s < (int) n_stages; s++) {
-                const uint32_t it = ((volatile uint32_t *) issued)[s];
-                if (!mbar_wait_bounded(&full[s], (it / NSTAGE) & 1, drain_ns, nullptr))
+            for (int s = 0; s < NSTAGE; s++) {
+                const uint32_t gi = ((volatile uint32_t *) issued)[s];
+                if (gi == NEVER) continue;
+                if (!mbar_wait_bounded(&full[s], (gi / NSTAGE) & 1, drain_ns, nullptr))
                     atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
             }
         }
     };
-    if (warp == 0)
-        for (uint32_t it = 0; it < NSTAGE && it < n_stages; it++) issue(it);
+    if (warp == 0) {   // the first NSTAGE stream stages
+        uint32_t jn = blockIdx.x, it = 0, n = stages_of(jn);
+        for (uint32_t g = 0; g < NSTAGE; g++) {
+            issue(jn, it, g);
+            if (++it == n) {
+                it = 0;
+                jn += gridDim.x;
+                if (jn >= p.n_jobs) break;
+                n = stages_of(jn);
+            }
+        }
+    }
 
     // ------------------------------------------------ consumer warps
-    const uint32_t stream = warp % S, par = warp / S;
-    const uint32_t hl = stream % p.hg, rgl = stream / p.hg;
+    const uint32_t hl = warp % p.hg, rgl = warp / p.hg;
     const uint32_t h = h0 + hl, rg = rg0 + rgl;
     const uint32_t g = lane / 4, t = lane % 4;
     const uint32_t hoff = hl * (uint32_t) p.hb;
+    bool ok = true;
+    if (p.stall && !mbar_wait_bounded(never, 0, p.timeout_ns, abort_flag)) ok = false;
+
+    uint32_t gst = 0;   // stream stage
+    for (uint32_t jc = blockIdx.x; ok && jc < p.n_jobs; jc += gridDim.x) {
+    const Job job = p.jobs[jc];
+    const uint32_t n_stages = (job.nk + STAGE_KEYS - 1) / STAGE_KEYS;
+    const uint32_t g0 = gst;
 
     // Q fragments (B operand of S^T = K.Q^T): row n = g of this row group, k values permuted as dK
     uint32_t qf[NMT][2];
@@ -257,23 +289,19 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
     float m0 = M_EMPTY, m1 = M_EMPTY, l0 = 0.f, l1 = 0.f;   // rows 2t, 2t+1 of the 8-row group
     // Lazy running max: P is taken against a reference max mb (log2 units) that moves only when a score exceeds it by
     // more than LAZY_T (P <= 2^LAZY_T, well inside f16), so most tiles skip the cross-lane max and the O rescale. The
-    // exact maximum (ml, lane-local then reduced) is restored at the end: O and l are rescaled to it once.
+    // exact maximum (ml, lane-local then reduced) is restored at the end of the job: O and l are rescaled to it once.
     constexpr float LAZY_T = 8.f;
     float mb0 = M_EMPTY * LOG2E, mb1 = M_EMPTY * LOG2E;
     float th0 = M_EMPTY, th1 = M_EMPTY;        // scores (natural units) above these move mb
     float ml0 = -INFINITY, ml1 = -INFINITY;    // lane-local maxima of the scores
-    bool ok = true;
-    if (p.stall && !mbar_wait_bounded(never, 0, p.timeout_ns, abort_flag)) ok = false;
 
-    for (uint32_t it = 0; ok && it < n_stages; it++) {
-        const uint32_t s = it % NSTAGE;
-        if (!mbar_wait_bounded(&full[s], (it / NSTAGE) & 1, p.timeout_ns, abort_flag)) { ok = false; break; }
+    for (uint32_t it = 0; it < n_stages; it++, gst++) {
+        const uint32_t s = gst % NSTAGE;
+        if (!mbar_wait_bounded(&full[s], (gst / NSTAGE) & 1, p.timeout_ns, abort_flag)) { ok = false; break; }
         const uint32_t valid = min((uint32_t) STAGE_KEYS, job.nk - it * STAGE_KEYS);
         const uint32_t kbase = smem_u32(smem + s * stage_bytes) + hoff;
         const uint32_t vbase = kbase + half_stage;
-        // one tile per stage (hd 128: the host sets one warp per stream) or the stream's warps split the stage's tiles
-        constexpr bool ONE_TILE = STAGE_KEYS == TILE_KEYS;
-        for (uint32_t tt = ONE_TILE ? 0u : par; tt < STAGE_KEYS / TILE_KEYS; tt += ONE_TILE ? 1u : p.pw) {
+        for (uint32_t tt = 0; tt < STAGE_KEYS / TILE_KEYS; tt++) {
             const int tvalid = (int) valid - (int) tt * TILE_KEYS;
             if (tvalid <= 0) break;
             const uint32_t tk = kbase + tt * (TILE_KEYS / 2) * gs;   // the tile's 8 pairs
@@ -471,7 +499,7 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
                 }
             }
         }
-        // release the buffer; the last warp to do so refills it with stage it + NSTAGE
+        // release the buffer; the last warp to do so refills it with stream stage gst + NSTAGE
         __syncwarp();
         uint32_t last = 0;
         if (lane == 0) {
@@ -479,16 +507,13 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
             last = (atomicAdd(&released[s], 1u) + 1u) % n_active == 0;
         }
         last = __shfl_sync(0xffffffffu, last, 0);
-        if (last && it + NSTAGE < n_stages) {
+        if (last) {
             __threadfence_block();
             fence_proxy_async();     // ... and before the bulk copies (async proxy) that overwrite it
-            issue(it + NSTAGE);
+            issue_ahead(jc, g0, n_stages, gst);
         }
     }
-    if (!ok) {
-        abort_and_drain();
-        return;
-    }
+    if (!ok) break;
 
     // ---- report the exact maximum of each row: rescale O and l from the lazy reference max to it (an empty row keeps
     // m = M_EMPTY, l = 0)
@@ -507,63 +532,14 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
         m0 = ml0 > -INFINITY ? ml0 : M_EMPTY;
         m1 = ml1 > -INFINITY ? ml1 : M_EMPTY;
     }
-
-    // ---- finish: l summed over the lanes of a row (keys g), then the partner warp (if any) folded in
+    // l summed over the lanes of a row (keys g)
 #pragma unroll
     for (int x = 4; x < 32; x <<= 1) {
         l0 += __shfl_xor_sync(0xffffffffu, l0, x);
         l1 += __shfl_xor_sync(0xffffffffu, l1, x);
     }
-    if (p.pw == 2) {
-        // the pair's second warp publishes its partial through stage memory once every consumer is past the pipeline;
-        // both waits are bounded, so a consumer that gave up cannot leave the others waiting
-        __syncwarp();
-        if (lane == 0) mbar_arrive(done);
-        float *xb = reinterpret_cast<float *>(smem) + (size_t) stream * (NMT * 4 + 4) * 32;
-        if (par == 1) {
-            bool w = true;
-            if (lane == 0) w = mbar_wait_bounded(done, 0, p.timeout_ns, abort_flag);
-            if (!__shfl_sync(0xffffffffu, w, 0)) {
-                abort_and_drain();
-                return;
-            }
-#pragma unroll
-            for (int mt = 0; mt < NMT; mt++)
-#pragma unroll
-                for (int j = 0; j < 4; j++) xb[(mt * 4 + j) * 32 + lane] = o[mt][j];
-            xb[(NMT * 4 + 0) * 32 + lane] = m0;
-            xb[(NMT * 4 + 1) * 32 + lane] = m1;
-            xb[(NMT * 4 + 2) * 32 + lane] = l0;
-            xb[(NMT * 4 + 3) * 32 + lane] = l1;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(xchg);   // release: the writes above are visible to the waiter
-            return;
-        }
-        bool w = true;
-        if (lane == 0) w = mbar_wait_bounded(xchg, 0, p.timeout_ns, abort_flag);
-        if (!__shfl_sync(0xffffffffu, w, 0)) {
-            abort_and_drain();
-            return;
-        }
-        const float pm0 = xb[(NMT * 4 + 0) * 32 + lane], pm1 = xb[(NMT * 4 + 1) * 32 + lane];
-        const float pl0 = xb[(NMT * 4 + 2) * 32 + lane], pl1 = xb[(NMT * 4 + 3) * 32 + lane];
-        const float M0 = fmaxf(m0, pm0), M1 = fmaxf(m1, pm1);
-        const float a0 = ex2((m0 - M0) * LOG2E), a1 = ex2((m1 - M1) * LOG2E);
-        const float c0 = ex2((pm0 - M0) * LOG2E), c1 = ex2((pm1 - M1) * LOG2E);
-#pragma unroll
-        for (int mt = 0; mt < NMT; mt++) {
-            o[mt][0] = o[mt][0] * a0 + xb[(mt * 4 + 0) * 32 + lane] * c0;
-            o[mt][1] = o[mt][1] * a1 + xb[(mt * 4 + 1) * 32 + lane] * c1;
-            o[mt][2] = o[mt][2] * a0 + xb[(mt * 4 + 2) * 32 + lane] * c0;
-            o[mt][3] = o[mt][3] * a1 + xb[(mt * 4 + 3) * 32 + lane] * c1;
-        }
-        l0 = l0 * a0 + pl0 * c0;
-        l1 = l1 * a1 + pl1 * c1;
-        m0 = M0;
-        m1 = M1;
-    }
 
-    // ---- write the slot partial
+    // ---- write the job's slot partial
     const uint64_t rbase = ((uint64_t) job.slot * p.nkv + h) * p.rows;
     const uint32_t r0 = rg * 8 + 2 * t, r1 = r0 + 1;
 #pragma unroll
@@ -582,6 +558,8 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
         if (r0 < p.rows) { p.Mp[rbase + r0] = l0 > 0.f ? m0 : -INFINITY; p.Lp[rbase + r0] = l0; }
         if (r1 < p.rows) { p.Mp[rbase + r1] = l1 > 0.f ? m1 : -INFINITY; p.Lp[rbase + r1] = l1; }
     }
+    }   // jobs
+    if (!ok) abort_and_drain();
 }
 
 }  // namespace dec
