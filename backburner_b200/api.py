@@ -79,6 +79,7 @@ _SIGS = {
     "pa_cuda_nccl_comm_destroy": (None, [_P]),
     "pa_cuda_shard_attn_allgather_merge": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P]),
     "pa_cuda_set_shard_exchange": (None, [_P, ctypes.c_int]),
+    "pa_cuda_shard_last": (None, [_P, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "pa_cuda_set_shard_groups": (None, [_P, ctypes.c_int]),
     "pa_cuda_set_shard_timeout_ms": (None, [_P, ctypes.c_uint32]),
     "pa_cuda_nccl_wait": (ctypes.c_int, [_P, _P, _P, ctypes.c_uint32]),
@@ -210,11 +211,18 @@ class Context:
         return int(lib().pa_cuda_launch_count(self._h))
 
     # exchange of the position-shard call (shard_attn_allgather_merge) for calls made afterwards
-    EXCHANGE_AUTO, EXCHANGE_ALLGATHER, EXCHANGE_ALLREDUCE = 0, 1, 2
+    EXCHANGE_AUTO, EXCHANGE_ALLGATHER, EXCHANGE_ALLREDUCE, EXCHANGE_PEER = 0, 1, 2, 3
 
     def set_shard_exchange(self, mode: int):
-        """0: by size; 1: all-gather of every rank's packed (O, m, l) and the fold; 2: max / sum all-reduces."""
+        """0: by size; 1: all-gather of every rank's packed (O, m, l) and the fold; 2: max / sum all-reduces; 3: peer
+        stores over NVLink."""
         lib().pa_cuda_set_shard_exchange(self._h, int(mode))
+
+    def shard_last(self):
+        """(exchange, set groups) the last shard call of this context used."""
+        e, g = ctypes.c_int(), ctypes.c_int()
+        lib().pa_cuda_shard_last(self._h, ctypes.byref(e), ctypes.byref(g))
+        return int(e.value), int(g.value)
 
     def set_shard_groups(self, groups: int):
         """Output-set groups whose exchange overlaps the next group's kernels (0: by size, 1: none)."""

@@ -7,7 +7,8 @@
 namespace pa {
 
 // error codes written to the device status word (the host reads it after the stream is synchronised)
-enum : int { ST_OK = 0, ST_TIMEOUT_FULL = 1, ST_TIMEOUT_EMPTY = 2, ST_TIMEOUT_DRAIN = 3, ST_BAD_ARGS = 4 };
+enum : int { ST_OK = 0, ST_TIMEOUT_FULL = 1, ST_TIMEOUT_EMPTY = 2, ST_TIMEOUT_DRAIN = 3, ST_BAD_ARGS = 4,
+             ST_TIMEOUT_PEER = 5 };   // a rank's partial did not arrive in time (peer-store exchange)
 
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;

@@ -95,6 +95,7 @@ struct pa_cuda_ctx {
     size_t d_shard_bytes = 0, d_gathered_bytes = 0;
     int shard_exchange = 0;          // 0 by size, 1 all-gather + fold, 2 max / sum all-reduces
     int shard_groups = 0;            // 0 by size; else output-set groups whose exchange overlaps the next group's kernels
+    int shard_last_mode = 0, shard_last_groups = 0;   // what the last shard call used
     uint32_t shard_timeout_ms = 0;   // > 0: the shard call waits for its exchange, bounded (abort on overrun)
     cudaStream_t xstream = nullptr;  // exchange stream of the pipelined shard call
     std::vector<cudaEvent_t> xev;    // [group] the group's partial is packed; back: the exchange finished
@@ -328,8 +329,7 @@ cudaError_t launch_merge(const pa::mrg::Params &mp, cudaStream_t st, int n_sm) {
 // The plan's output sets [s0, s1): the attention kernel over their jobs (jobs are grouped by set, so they are the
 // contiguous range [crange[s0], crange[s1])) and the merge of their slots into O, m, l, which point at set s0's rows.
 // Qs is the whole call's Q (the kernels address it by each job's absolute set).
-int run_plan_sets(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, cudaStream_t st, uint32_t s0,
-                  uint32_t s1) {
+int run_attention_sets(pa_cuda_plan *p, const uint16_t *Qs, cudaStream_t st, uint32_t s0, uint32_t s1) {
     pa_cuda_ctx *ctx = p->ctx;
     const pa_cuda_shape &sh = p->sh;
     const uint32_t j0 = p->crange[s0], nj = p->crange[s1] - j0;
@@ -405,6 +405,14 @@ int run_plan_sets(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float
         }
         ctx->launches++;
     }
+    return PA_CUDA_OK;
+}
+int run_plan_sets(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, cudaStream_t st, uint32_t s0,
+                  uint32_t s1) {
+    pa_cuda_ctx *ctx = p->ctx;
+    const pa_cuda_shape &sh = p->sh;
+    int rc = run_attention_sets(p, Qs, st, s0, s1);
+    if (rc) return rc;
     pa::mrg::Params mp{};
     mp.Op = p->d_op;
     mp.Mp = p->d_mp;
@@ -501,9 +509,20 @@ int nccl_fail(pa_cuda_ctx *ctx, const NcclApi *api, ncclResult_t r, const char *
 // a shard communicator: NCCL's, plus whether it was aborted (after which NCCL has freed it)
 struct ShardComm {
     ncclComm_t nc = nullptr;
-    int rank = 0, world = 1;
+    int rank = 0, world = 1, device = 0;
     bool dead = false;
+    // peer-store exchange: every rank holds one buffer, mapped into every other rank with CUDA IPC: flags
+    // [world source ranks][blocks_cap] (u64: the call number a source's block last published), then the receive area
+    // [2 halves by call parity][world source ranks][cap floats]
+    int p2p_state = 0;                        // 0 not set up, 1 ready, -1 unavailable on some rank (all fall back)
+    uint8_t *p2p_buf = nullptr;
+    size_t p2p_cap = 0, p2p_blocks = 0, p2p_head = 0;   // floats of a part, blocks of a call, bytes of the flags
+    std::vector<uint8_t *> p2p_peer;          // each rank's buffer as mapped here (this rank's own: p2p_buf)
+    float **d_push = nullptr;                 // device [world]: rank r's receive area, slot of this rank, half 0
+    unsigned long long **d_pflag = nullptr;   // device [world]: rank r's flags of source = this rank
+    unsigned long long p2p_calls = 0;         // peer-store calls so far (the epoch of the next is p2p_calls + 1)
 };
+constexpr uint32_t kSetupWaitMs = 60000;   // bound on the set-up collectives of the peer-store exchange
 // exchange choices by size: the two-all-reduce exchange from this many bytes of one rank's partial (with more than 2
 // ranks), and set groups whose exchange overlaps the next group's kernels from this many
 constexpr size_t kShardReduceBytes = 8u << 20;
@@ -549,6 +568,106 @@ int shard_wait(pa_cuda_ctx *ctx, const NcclApi *api, ShardComm *sc, cudaStream_t
         std::this_thread::sleep_for(std::chrono::microseconds(200));
     cudaGetLastError();
     return fail(ctx, code, why + "; communicator aborted");
+}
+
+void p2p_release(ShardComm *sc) {
+    cudaSetDevice(sc->device);
+    for (int r = 0; r < (int) sc->p2p_peer.size(); r++)
+        if (r != sc->rank && sc->p2p_peer[r]) cudaIpcCloseMemHandle(sc->p2p_peer[r]);
+    sc->p2p_peer.clear();
+    if (sc->p2p_buf) cudaFree(sc->p2p_buf);
+    if (sc->d_push) cudaFree(sc->d_push);
+    if (sc->d_pflag) cudaFree(sc->d_pflag);
+    sc->p2p_buf = nullptr;
+    sc->d_push = nullptr;
+    sc->d_pflag = nullptr;
+    sc->p2p_cap = sc->p2p_blocks = sc->p2p_head = 0;
+    cudaGetLastError();
+}
+
+// every rank's answer to "did this step work here" (an all-gather of one byte each); the ranks act on the same answer
+bool all_ranks_ok(pa_cuda_ctx *ctx, const NcclApi *api, ShardComm *sc, bool ok, cudaStream_t st) {
+    uint8_t *d = nullptr;
+    std::vector<uint8_t> h((size_t) sc->world, 0);
+    bool all = cudaMalloc((void **) &d, (size_t) sc->world) == cudaSuccess;
+    const uint8_t mine = ok ? 1 : 0;
+    if (all) all = cudaMemcpy(d + sc->rank, &mine, 1, cudaMemcpyHostToDevice) == cudaSuccess;
+    // the all-gather runs on every rank whatever happened here, so that no rank waits for another forever
+    const ncclResult_t r = api->all_gather(all ? d + sc->rank : nullptr, d, 1, ncclUint8, sc->nc, st);
+    all = all && r == ncclSuccess && shard_wait(ctx, api, sc, st, kSetupWaitMs) == PA_CUDA_OK &&
+          cudaMemcpy(h.data(), d, (size_t) sc->world, cudaMemcpyDeviceToHost) == cudaSuccess;
+    if (d) cudaFree(d);
+    for (int i = 0; all && i < sc->world; i++) all = h[(size_t) i] == 1;
+    return all;
+}
+
+// Sets up (collectively: every rank calls it at the same point) the peer-store buffers for parts of `part` floats: each
+// rank allocates its buffer, the IPC handles go round with one all-gather, and each rank maps the others'. If any
+// rank fails at any step every rank drops the exchange (state -1) and the shard call uses NCCL instead.
+void p2p_setup(pa_cuda_ctx *ctx, const NcclApi *api, ShardComm *sc, size_t part, size_t blocks, cudaStream_t st) {
+    if (sc->p2p_state == 1 && sc->p2p_cap >= part && sc->p2p_blocks >= blocks) return;
+    if (sc->p2p_state == -1) return;
+    p2p_release(sc);
+    const int W = sc->world;
+    const size_t head = ((size_t) W * blocks * 8 + 255) / 256 * 256;
+    const size_t bytes = head + 2 * (size_t) W * part * sizeof(float);
+    bool ok = cudaMalloc((void **) &sc->p2p_buf, bytes) == cudaSuccess &&
+              cudaMemset(sc->p2p_buf, 0, head) == cudaSuccess;
+    cudaIpcMemHandle_t mine{};
+    if (ok) ok = cudaIpcGetMemHandle(&mine, sc->p2p_buf) == cudaSuccess;
+    // the handles (plus a success byte) of every rank
+    constexpr size_t HB = sizeof(cudaIpcMemHandle_t) + 8;
+    uint8_t *d = nullptr;
+    std::vector<uint8_t> h((size_t) W * HB, 0);
+    const bool dev_ok = cudaMalloc((void **) &d, (size_t) W * HB) == cudaSuccess;
+    if (dev_ok) {
+        std::vector<uint8_t> me(HB, 0);
+        memcpy(me.data(), &mine, sizeof mine);
+        me[sizeof mine] = ok ? 1 : 0;
+        cudaMemcpy(d + (size_t) sc->rank * HB, me.data(), HB, cudaMemcpyHostToDevice);
+    }
+    const ncclResult_t r = api->all_gather(dev_ok ? d + (size_t) sc->rank * HB : nullptr, d, HB, ncclUint8, sc->nc, st);
+    ok = ok && dev_ok && r == ncclSuccess && shard_wait(ctx, api, sc, st, kSetupWaitMs) == PA_CUDA_OK &&
+         cudaMemcpy(h.data(), d, h.size(), cudaMemcpyDeviceToHost) == cudaSuccess;
+    if (d) cudaFree(d);
+    for (int i = 0; ok && i < W; i++) ok = h[(size_t) i * HB + sizeof mine] == 1;
+    // map every other rank's buffer
+    sc->p2p_peer.assign((size_t) W, nullptr);
+    sc->p2p_peer[(size_t) sc->rank] = sc->p2p_buf;
+    for (int i = 0; ok && i < W; i++) {
+        if (i == sc->rank) continue;
+        cudaIpcMemHandle_t hi;
+        memcpy(&hi, h.data() + (size_t) i * HB, sizeof hi);
+        void *ptr = nullptr;
+        ok = cudaIpcOpenMemHandle(&ptr, hi, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+        sc->p2p_peer[(size_t) i] = (uint8_t *) ptr;
+    }
+    cudaGetLastError();
+    // device tables: where this rank's part goes in each rank, and its counter there
+    if (ok) {
+        std::vector<float *> push((size_t) W);
+        std::vector<unsigned long long *> flag((size_t) W);
+        for (int i = 0; i < W; i++) {
+            push[(size_t) i] = (float *) (sc->p2p_peer[(size_t) i] + head) + (size_t) sc->rank * part;
+            flag[(size_t) i] = (unsigned long long *) sc->p2p_peer[(size_t) i] + (size_t) sc->rank * blocks;
+        }
+        ok = cudaMalloc((void **) &sc->d_push, W * sizeof(float *)) == cudaSuccess &&
+             cudaMalloc((void **) &sc->d_pflag, W * sizeof(unsigned long long *)) == cudaSuccess &&
+             cudaMemcpy(sc->d_push, push.data(), W * sizeof(float *), cudaMemcpyHostToDevice) == cudaSuccess &&
+             cudaMemcpy(sc->d_pflag, flag.data(), W * sizeof(unsigned long long *), cudaMemcpyHostToDevice) == cudaSuccess;
+    }
+    // the same decision on every rank
+    ok = all_ranks_ok(ctx, api, sc, ok, st);
+    if (!ok) {
+        p2p_release(sc);
+        sc->p2p_state = -1;
+        return;
+    }
+    sc->p2p_state = 1;
+    sc->p2p_cap = part;
+    sc->p2p_blocks = blocks;
+    sc->p2p_head = head;
+    sc->p2p_calls = 0;
 }
 
 }  // namespace
@@ -1017,6 +1136,7 @@ int pa_cuda_nccl_comm_create(pa_cuda_ctx *ctx, const void *id, int rank, int wor
     sc->nc = c;
     sc->rank = rank;
     sc->world = world;
+    sc->device = ctx->device;
     *comm = sc;
     return PA_CUDA_OK;
 }
@@ -1025,18 +1145,26 @@ void pa_cuda_nccl_comm_destroy(void *comm) {
     auto *sc = (ShardComm *) comm;
     if (!sc) return;
     const NcclApi *api = nccl_api();
+    // the peer-store buffers: mapped by the other ranks too, so destroy after they stopped calling (as with NCCL)
+    cudaSetDevice(sc->device);
+    cudaDeviceSynchronize();
+    p2p_release(sc);
     if (api && sc->nc && !sc->dead) api->comm_destroy(sc->nc);
     delete sc;
 }
 
 void pa_cuda_set_shard_exchange(pa_cuda_ctx *ctx, int mode) {
-    if (ctx) ctx->shard_exchange = (mode >= 0 && mode <= 2) ? mode : 0;
+    if (ctx) ctx->shard_exchange = (mode >= 0 && mode <= 3) ? mode : 0;
 }
 void pa_cuda_set_shard_groups(pa_cuda_ctx *ctx, int groups) {
     if (ctx) ctx->shard_groups = groups > 0 ? groups : 0;
 }
 void pa_cuda_set_shard_timeout_ms(pa_cuda_ctx *ctx, uint32_t ms) {
     if (ctx) ctx->shard_timeout_ms = ms;
+}
+void pa_cuda_shard_last(const pa_cuda_ctx *ctx, int *exchange, int *groups) {
+    if (exchange) *exchange = ctx ? ctx->shard_last_mode : 0;
+    if (groups) *groups = ctx ? ctx->shard_last_groups : 0;
 }
 
 int pa_cuda_nccl_wait(pa_cuda_ctx *ctx, void *comm, void *stream, uint32_t timeout_ms) {
@@ -1061,13 +1189,65 @@ int pa_cuda_shard_attn_allgather_merge(pa_cuda_plan *p, const uint16_t *Qs, void
     const uint32_t hd = p->sh.hd, ns = p->n_sets;
     const uint64_t rps = (uint64_t) p->sh.nkv * p->sh.rows;            // rows per output set
     const uint64_t rows = (uint64_t) ns * rps, part = rows * (hd + 2);   // floats of one rank's packed partial
-    // exchange: the all-gather moves (N-1) partials into every rank, the two all-reduces ~2(N-1)/N of one
-    const int mode = ctx->shard_exchange ? ctx->shard_exchange
-                   : (world > 2 && part * sizeof(float) >= kShardReduceBytes) ? 2 : 1;
+    // exchange: the peer stores (small partials: no collective launch on the call's path), the all-gather moves N-1
+    // partials into every rank, the two all-reduces ~2(N-1)/N of one
+    const bool big = part * sizeof(float) >= kShardReduceBytes;
+    int mode = ctx->shard_exchange ? ctx->shard_exchange : big ? (world > 2 ? 2 : 1) : 3;
+    cudaStream_t st0 = pick(ctx, stream);
+    if (mode == 3) {
+        p2p_setup(ctx, api, sc, part, (rows + 7) / 8, st0);   // collective the first time (and when more room is needed)
+        if (sc->dead) return fail(ctx, PA_CUDA_ENCCL, "the communicator was aborted while setting up the peer stores");
+        if (sc->p2p_state != 1) mode = (big && world > 2) ? 2 : 1;
+    }
+    ctx->shard_last_mode = mode;
+    if (mode == 3) {
+        // the attention kernel, then one exchange kernel: its blocks merge this rank's rows, store them into every
+        // rank's receive area (the half of this call's parity) and publish them, then fold every rank's rows
+        const unsigned long long epoch = ++sc->p2p_calls;
+        int rc = run_attention_sets(p, Qs, st0, 0, ns);
+        if (rc) return rc;
+        pa::mrg::XParams x{};
+        x.Op = p->d_op;
+        x.Mp = p->d_mp;
+        x.Lp = p->d_lp;
+        x.c_range = p->d_crange;
+        x.op_stride = (uint64_t) p->sh.nkv * p->sh.rows * hd;
+        x.ml_stride = (uint64_t) p->sh.nkv * p->sh.rows;
+        x.rows_per_set = rps;
+        x.n_sets = ns;
+        x.push = sc->d_push;
+        x.push_off = (epoch & 1) * (uint64_t) world * sc->p2p_cap;
+        x.push_flag = sc->d_pflag;
+        x.recv = (const float *) (sc->p2p_buf + sc->p2p_head) + (epoch & 1) * (uint64_t) world * sc->p2p_cap;
+        x.flags = (const unsigned long long *) sc->p2p_buf;
+        x.cap = sc->p2p_cap;
+        x.blocks_cap = sc->p2p_blocks;
+        x.epoch = epoch;
+        x.world = (uint32_t) world;
+        x.O = O;
+        x.M = m;
+        x.L = l;
+        x.status = ctx->d_status;
+        x.timeout_ns = ctx->timeout_ns;
+        const unsigned blocks = (unsigned) ((rows + 7) / 8);
+        if (blocks) {
+            if (hd == 128) pa::mrg::shard_exchange_kernel<128><<<blocks, 256, 0, st0>>>(x);
+            else pa::mrg::shard_exchange_kernel<256><<<blocks, 256, 0, st0>>>(x);
+            PA_CK(cudaGetLastError(), "exchange kernel launch");
+            ctx->launches++;
+        }
+        ctx->shard_last_groups = 1;
+        if (ctx->shard_timeout_ms) {
+            if ((rc = shard_wait(ctx, api, sc, st0, ctx->shard_timeout_ms))) return rc;
+            return pa_cuda_status(ctx, st0);
+        }
+        return PA_CUDA_OK;
+    }
     // set groups: each group's exchange overlaps the next group's kernels
     uint32_t G = ctx->shard_groups ? (uint32_t) ctx->shard_groups
                : (part * sizeof(float) >= kShardGroupBytes ? kShardGroups : 1u);
     G = std::max(1u, std::min(G, std::max(1u, ns)));
+    ctx->shard_last_groups = (int) G;
     int rc = ensure_dev(ctx, ctx->d_shard, ctx->d_shard_bytes, part * sizeof(float));
     if (!rc && mode == 1) rc = ensure_dev(ctx, ctx->d_gathered, ctx->d_gathered_bytes, (size_t) world * part * sizeof(float));
     if (rc) return rc;

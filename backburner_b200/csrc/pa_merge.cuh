@@ -145,6 +145,146 @@ __global__ void __launch_bounds__(256) merge_kernel(const Params p) {
     }
 }
 
+// One warp's merge of parts [c0, c1) of one row: part c's row at Op + c * op_stride + rr * HD, its m and l at
+// Mp / Lp + c * ml_stride + rr. Returns sum_c w_c O_c (this lane's HD/32 dims), M and sum_c w_c l_c, w_c =
+// exp(m_c - M), parts with l <= 0 skipped (M = -inf, L = 0 when none has keys). As merge_kernel's one-warp path.
+template <int HD>
+__device__ __forceinline__ void merge_row(const float *Op, const float *Mp, const float *Lp, uint64_t op_stride,
+                                          uint64_t ml_stride, uint64_t rr, uint32_t c0, uint32_t c1, uint32_t lane,
+                                          float (&acc)[HD / 32], float &M, float &L) {
+    constexpr int V = HD / 32;
+    M = -INFINITY;
+    for (uint32_t c = c0 + lane; c < c1; c += 32) {
+        const uint64_t pr = (uint64_t) c * ml_stride + rr;
+        if (Lp[pr] > 0.f) M = fmaxf(M, Mp[pr]);
+    }
+#pragma unroll
+    for (int x = 16; x > 0; x >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, x));
+#pragma unroll
+    for (int i = 0; i < V; i++) acc[i] = 0.f;
+    float Ls = 0.f;
+    for (uint32_t cb = c0; cb < c1; cb += 32) {
+        const uint32_t c = cb + lane;
+        float w = 0.f;
+        if (c < c1) {
+            const uint64_t pr = (uint64_t) c * ml_stride + rr;
+            const float lc = Lp[pr];
+            if (lc > 0.f) {
+                w = ex2((Mp[pr] - M) * LOG2E);
+                Ls = fmaf(w, lc, Ls);
+            }
+        }
+        const uint32_t nb = min(32u, c1 - cb);
+#pragma unroll 4
+        for (uint32_t j = 0; j < nb; j++) {
+            const float wj = __shfl_sync(0xffffffffu, w, j);
+            const float4 *src = reinterpret_cast<const float4 *>(Op + (uint64_t) (cb + j) * op_stride + rr * HD + lane * V);
+#pragma unroll
+            for (int i = 0; i < V / 4; i++) {
+                const float4 x = src[i];
+                if (wj != 0.f) {
+                    acc[4 * i] = fmaf(wj, x.x, acc[4 * i]);
+                    acc[4 * i + 1] = fmaf(wj, x.y, acc[4 * i + 1]);
+                    acc[4 * i + 2] = fmaf(wj, x.z, acc[4 * i + 2]);
+                    acc[4 * i + 3] = fmaf(wj, x.w, acc[4 * i + 3]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int x = 16; x > 0; x >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, x);
+    L = Ls;
+}
+
+// ---------------------------------------------------------------- the peer-store exchange of position shards
+// One kernel per call on every rank (one process per GPU): block b merges rows [8b, 8b+8) of this rank's chunk partials
+// (the plan's slots), stores them into every rank's receive area over NVLink (packed as one rank's part: O [rows][HD],
+// m [rows], l [rows]), publishes `epoch` in each rank's flag for (this rank, block b) with a system-scope release, waits
+// (bounded) until every rank has published block b of this call in this rank's flags, and folds the ranks' rows into
+// O, M, L. Blocks store before they wait, so a block waits only for blocks that store first on the other GPUs.
+struct XParams {
+    const float *Op, *Mp, *Lp;          // this rank's chunk partials (plan slots), as merge_kernel's Params
+    const uint32_t *c_range;            // [n_sets + 1]
+    uint64_t op_stride, ml_stride, rows_per_set;
+    uint32_t n_sets;
+    float *const *push;                 // [world]: rank r's receive area, this rank's part (half 0)
+    uint64_t push_off;                  // floats from half 0 to this call's half
+    unsigned long long *const *push_flag;   // [world]: rank r's flags of source = this rank, [blocks]
+    const float *recv;                  // this rank's receive area, this call's half: rank r's part at recv + r * cap
+    const unsigned long long *flags;    // this rank's flags [world][blocks_cap]
+    uint64_t cap, blocks_cap;
+    unsigned long long epoch;           // this call's number (1, 2, ...)
+    uint32_t world;
+    float *O, *M, *L;
+    int *status;
+    uint64_t timeout_ns;
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256) shard_exchange_kernel(const XParams p) {
+    constexpr int V = HD / 32;
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint64_t rows = (uint64_t) p.n_sets * p.rows_per_set;
+    const uint64_t row = (uint64_t) blockIdx.x * 8 + warp;
+    const bool active = row < rows;
+    float acc[V], M = -INFINITY, L = 0.f;
+    if (active) {
+        const uint32_t s = (uint32_t) (row / p.rows_per_set);
+        merge_row<HD>(p.Op, p.Mp, p.Lp, p.op_stride, p.ml_stride, row % p.rows_per_set, p.c_range[s], p.c_range[s + 1],
+                      lane, acc, M, L);
+        for (uint32_t r = 0; r < p.world; r++) {
+            float *base = p.push[r] + p.push_off;
+            float4 *dst = reinterpret_cast<float4 *>(base + row * HD + lane * V);
+#pragma unroll
+            for (int i = 0; i < V / 4; i++) dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+            if (lane == 0) {
+                base[rows * HD + row] = L > 0.f ? M : -INFINITY;
+                base[rows * HD + rows + row] = L;
+            }
+        }
+    }
+    __syncthreads();   // the block's stores, then (cumulative system-scope fence) its flag in every rank
+    if (threadIdx.x < p.world) {
+        __threadfence_system();
+        st_release_sys(p.push_flag[threadIdx.x] + blockIdx.x, p.epoch);
+    }
+    __shared__ int s_go;
+    if (threadIdx.x == 0) {
+        bool go = *(volatile int *) p.status == ST_OK;   // a call that already failed waits no further
+        const uint64_t t0 = globaltimer_ns();
+        for (uint32_t r = 0; go && r < p.world; r++) {
+            const unsigned long long *f = p.flags + (uint64_t) r * p.blocks_cap + blockIdx.x;
+            for (uint32_t it = 0; ld_acquire_sys(f) < p.epoch; it++) {
+                if ((it & 63) == 63 && globaltimer_ns() - t0 > p.timeout_ns) {
+                    atomicCAS(p.status, ST_OK, ST_TIMEOUT_PEER);
+                    go = false;
+                    break;
+                }
+            }
+        }
+        s_go = go;
+    }
+    __syncthreads();
+    if (!s_go || !active) return;
+    merge_row<HD>(p.recv, p.recv + rows * HD, p.recv + rows * HD + rows, p.cap, p.cap, row, 0, p.world, lane, acc, M, L);
+    float4 *dst = reinterpret_cast<float4 *>(p.O + row * HD + lane * V);
+#pragma unroll
+    for (int i = 0; i < V / 4; i++) dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+    if (lane == 0) {
+        p.M[row] = L > 0.f ? M : -INFINITY;
+        p.L[row] = L;
+    }
+}
+
 // O/l -> f16, lse = m + log(l); rows with l == 0 give O = 0, lse = -inf
 template <int HD>
 __global__ void __launch_bounds__(256) normalize_kernel(const float *O, const float *M, const float *L, uint64_t n_rows,

@@ -342,7 +342,7 @@ class Leg:
         per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
         ms = self.max_over_ranks(ev[0].elapsed_time(ev[-1]))
         kern = self.max_over_ranks(kern_total / steps)
-        res = {"ms": ms, "kernel_ms": kern, "launches": launches, "clocks": clk.summary(),
+        res = {"ms": ms, "kernel_ms": kern, "launches": launches, "clocks": clk.summary(), "exchange": self.ctx.shard_last(),
                "step_ms": {"min": round(min(per), 4), "median": round(statistics.median(per), 4),
                            "max": round(max(per), 4)}}
         if plan_only_steps > 0 and self.world > 1:
@@ -379,10 +379,13 @@ def breakdown(r: dict, steps: int) -> dict:
     return b
 
 
-def exchange_name(world: int, mode: int, groups: int) -> str:
+def exchange_name(world: int, used) -> str:
+    """The exchange the library's shard call used (pa_cuda_shard_last): mode, set groups."""
     if world == 1:
         return "none (one GPU)"
-    kind = {1: "NCCL all-gather of (O,m,l) + LSE fold", 2: "NCCL all-reduce MAX of m + SUM of rescaled (O,l)"}[mode]
+    mode, groups = used
+    kind = {1: "NCCL all-gather of (O,m,l) + LSE fold", 2: "NCCL all-reduce MAX of m + SUM of rescaled (O,l)",
+            3: "peer stores of the merged (O,m,l) over NVLink into every rank + bounded-wait LSE fold"}.get(mode, "?")
     return kind + (f", {groups} set groups overlapped with the kernels" if groups > 1 else "")
 
 
@@ -452,9 +455,8 @@ def bench_prefill(torch, dist, pa, ctx, comm, device, stream, world, rank, local
     mask, all `layers` layers per step in one plan (the tcgen05 CTA-pair kernel: 2,560 rows per KV head); the positions
     sharded over the ranks like the decode workload (each rank 65,536/N of every layer)."""
     rows = PF_TOKENS * GQA
-    mode = 2 if world > 2 else 1
     leg = Leg(torch, dist, pa, ctx, comm, device, stream, world, rank, local, layers, PF_KEYS, rows, pa.Q8_0,
-              1000, exchange=mode, groups=8)
+              1000)
     g = torch.Generator(device=device)
     g.manual_seed(SEED + 11)
     Qs = (torch.randn((layers, NKV, rows, HD), generator=g, device=device) / HD ** 0.5).to(torch.float16)
@@ -477,7 +479,7 @@ def bench_prefill(torch, dist, pa, ctx, comm, device, stream, world, rank, local
     return {"metric": "prefill attn TFLOP/s (config 2: 512 tokens x 65536 Q8_0 keys, 40q/8kv, d128)",
             "value": round(flops / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "ms_per_step": round(ms, 3),
             "layers": layers, "steps": steps, "keys_per_gpu": leg.nk,
-            "exchange": exchange_name(world, mode, 8),
+            "exchange": exchange_name(world, r["exchange"]),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "peak_kind": kind,
                          "frac_of_sustained": round(achieved / peak_s, 4),
@@ -505,9 +507,8 @@ def bench_verify(torch, dist, pa, ctx, comm, device, stream, world, rank, local,
     mask. Fresh seeded Q per step. Roofline: the slower of HBM (quantised K/V bytes) and tensor (4 n_tok q_heads d keys
     flops) for this rank's launch."""
     rows = VF_TOKENS * GQA
-    mode = 2 if world > 2 else 1
     leg = Leg(torch, dist, pa, ctx, comm, device, stream, world, rank, local, layers, VF_KEYS, rows, pa.Q4_0,
-              3000, exchange=mode, groups=1)
+              3000)
     Qs = make_q(torch, steps + 3, layers, rows, device, SEED + 13)
     r = leg.timed(lambda i: Qs[i % Qs.shape[0]], steps, 3, plan_only_steps=min(steps, 20))
     ms = r["ms"] / steps
@@ -533,7 +534,7 @@ def bench_verify(torch, dist, pa, ctx, comm, device, stream, world, rank, local,
     return {"metric": "verify KV-attn GB/s (config 3: 16 tokens x 196608 Q4_0 keys, 40q/8kv, d128, 64 layers)",
             "value": round(lb / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
             "ms_per_step": round(ms, 4), "layers": layers, "steps": steps, "keys_per_gpu": nk,
-            "exchange": exchange_name(world, mode, 1),
+            "exchange": exchange_name(world, r["exchange"]),
             "roofline": {"bound": bound, "unit": "TFLOP/s" if bound == "tensor" else "GB/s",
                          "achieved": round((fl_launch / kt / 1e12) if bound == "tensor" else (lb_launch / kt / 1e9), 1),
                          "peak": ten if bound == "tensor" else hbm,
@@ -635,7 +636,7 @@ def main():
     decode = None
     if args.only in ("all", "decode"):
         leg = Leg(torch, dist, pa, ctx, comm, device, stream, world, rank, local, L, args.keys, GQA, pa.Q8_0, 0,
-                  exchange=1, groups=1, chunk_keys=args.chunk_keys)
+                  chunk_keys=args.chunk_keys)
         total_steps = args.warmup + args.steps
         Qs = make_q(torch, total_steps, L, GQA, device, SEED + 7)      # [steps][L][NKV][GQA][HD]
         r = leg.timed(lambda i: Qs[i], args.steps, args.warmup, plan_only_steps=min(args.steps, 64))
@@ -735,7 +736,8 @@ def main():
                            "keys": args.keys, "keys_per_gpu": decode["keys_per_gpu"], "nkv": NKV, "q_heads": Q_HEADS,
                            "hd": HD, "quant": "q8_0",
                            "parallelism": f"sequence shards x{world}" + (
-                               ", pa_cuda_shard_attn_allgather_merge: " + exchange_name(world, 1, 1) if world > 1 else ""),
+                               ", pa_cuda_shard_attn_allgather_merge: " + exchange_name(world, r["exchange"])
+                               if world > 1 else ""),
                            "l2": f"inputs larger than L2 ({decode['bytes_per_step'] / 1e9:.1f} GB of KV per step), "
                                  f"no flush",
                            "bytes_per_step": decode["bytes_per_step"]},

@@ -162,8 +162,14 @@ void pa_cuda_nccl_comm_destroy(void *comm);
 /* Runs this rank's plan (its shard's segments) into a packed (O, m, l), exchanges the ranks' partials on `stream`, and
  * folds them by log-sum-exp into O, m, l, identical on every rank. Every rank calls it, in the same order, with plans of
  * the same n_sets and shape, and the same exchange settings. The exchange (pa_cuda_set_shard_exchange):
+ *   peer stores: the merge of this rank's chunk partials stores its rows straight into every rank's receive buffer over
+ *     NVLink (buffers mapped into every rank with CUDA IPC, set up collectively by the first such call) and counts
+ *     them in on a per-source counter there; each rank's fold waits (bounded by pa_cuda_set_timeout_ns: a missing
+ *     rank's partial makes pa_cuda_status report PA_CUDA_ETIMEOUT) until every rank's rows are in, then merges. No
+ *     NCCL launch on the call's path. The choice by size below 8 MiB of partial per rank (decode, verify); when CUDA
+ *     IPC is not available on every rank, all ranks use the all-gather instead.
  *   all-gather: one ncclAllGather of every rank's packed (O, m, l), then the fold (pa_cuda_merge_gathered): each rank
- *     receives N-1 partials. The choice by size for small partials (decode) and for 2 ranks.
+ *     receives N-1 partials. The choice by size for large partials on 2 ranks.
  *   all-reduce: the rows' maxima over the ranks (ncclAllReduce MAX straight into m), each rank's (O, l) moved to them,
  *     then summed (ncclAllReduce SUM into O and l): ~2(N-1)/N of a partial per rank. The choice by size from 8 MiB of
  *     partial per rank with more than 2 ranks (prefill).
@@ -174,8 +180,10 @@ void pa_cuda_nccl_comm_destroy(void *comm);
 int pa_cuda_shard_attn_allgather_merge(pa_cuda_plan *plan, const uint16_t *Qs, void *comm, float *O, float *m, float *l,
                                        void *stream);
 /* Exchange of pa_cuda_shard_attn_allgather_merge for calls made afterwards: 0 = by size (default), 1 = all-gather and
- * fold, 2 = max / sum all-reduces. */
+ * fold, 2 = max / sum all-reduces, 3 = peer stores (set groups do not apply). */
 void pa_cuda_set_shard_exchange(pa_cuda_ctx *ctx, int mode);
+/* The exchange (1, 2 or 3) and set groups the last pa_cuda_shard_attn_allgather_merge of this context used. */
+void pa_cuda_shard_last(const pa_cuda_ctx *ctx, int *exchange, int *groups);
 /* Output-set groups of pa_cuda_shard_attn_allgather_merge whose exchange overlaps the next group's kernels: 0 = by size
  * (default), 1 = no overlap, G > 1 = G groups (at most n_sets). */
 void pa_cuda_set_shard_groups(pa_cuda_ctx *ctx, int groups);

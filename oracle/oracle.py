@@ -60,6 +60,9 @@ def lib():
         L.orc_partial_f64.argtypes = [ctypes.POINTER(_Shape), _u16p, _u8p, _u8p, ctypes.c_uint32, _f64p, _f64p, _f64p]
         L.orc_partial_f32.argtypes = [ctypes.POINTER(_Shape), _u16p, _u8p, _u8p, ctypes.c_uint32, ctypes.c_int,
                                       ctypes.c_int, ctypes.c_int, _f32p, _f32p, _f32p]
+        L.orc_partial_f32_i8q.restype = ctypes.c_int
+        L.orc_partial_f32_i8q.argtypes = [ctypes.POINTER(_Shape), _u16p, _u8p, _u8p, ctypes.c_uint32, ctypes.c_int,
+                                          ctypes.c_int, ctypes.c_int, _f32p, _f32p, _f32p]
         L.orc_partial_f32_mt.restype = ctypes.c_int
         L.orc_partial_f32_mt.argtypes = [ctypes.POINTER(_Shape), _u16p, _u8p, _u8p, ctypes.c_uint32, ctypes.c_int,
                                          ctypes.c_uint32, _f32p, _f32p, _f32p]
@@ -175,6 +178,21 @@ def partial_f32(sh: _Shape, Qs, K, V, nk: int, bk: int = 512):
     l = np.empty_like(m)
     lib().orc_partial_f32(ctypes.byref(sh), _p(Qs, _u16p), _p(K, _u8p), _p(V, _u8p), nk, bk, 0, sh.nkv, _p(O, _f32p),
                           _p(m, _f32p), _p(l, _f32p))
+    return O, m, l
+
+
+def partial_f32_i8q(sh: _Shape, Qs, K, V, nk: int, bk: int = 512):
+    """orc_partial_f32 with the reference's int8-domain QK (scripts/sme/sme_attn.c:465-508); Q8_0 rows only."""
+    Qs = np.ascontiguousarray(Qs, dtype=np.uint16)
+    K = np.ascontiguousarray(K, dtype=np.uint8)
+    V = np.ascontiguousarray(V, dtype=np.uint8)
+    O = np.empty((sh.nkv, sh.rows, sh.hd), dtype=np.float32)
+    m = np.empty((sh.nkv, sh.rows), dtype=np.float32)
+    l = np.empty_like(m)
+    rc = lib().orc_partial_f32_i8q(ctypes.byref(sh), _p(Qs, _u16p), _p(K, _u8p), _p(V, _u8p), nk, bk, 0, sh.nkv,
+                                   _p(O, _f32p), _p(m, _f32p), _p(l, _f32p))
+    if rc != 0:
+        raise ValueError("the int8-domain QK needs Q8_0 rows")
     return O, m, l
 
 

@@ -322,6 +322,89 @@ void orc_partial_f32(const orc_shape *sh, const uint16_t *Qs, const uint8_t *K, 
     free(kT); free(vb); free(S); free(q); free(Ot); free(alpha);
 }
 
+/* The int8-domain QK of scripts/sme/sme_attn.c:465-508 (sme_qk_i8blk: per 32-block int32 dot products of int8 Q and
+ * q8_0 K; i8_combine: s = sum_b float(T_b) * (dq_b * dk_b)), with Q quantised per 32-block by the Q8_0 rule
+ * (orc_quant_q8_0: d = f16(max|x|/127), q = rint(x / d); the reference leaves Q's rule to its caller), applied to the
+ * f16(q*scale) values the kernels receive. Softmax and P.V as orc_partial_f32 (P and V rounded to f16). Q8_0 rows only;
+ * returns -1 for other formats. */
+int orc_partial_f32_i8q(const orc_shape *sh, const uint16_t *Qs, const uint8_t *K, const uint8_t *V, uint32_t nk,
+                        int bk, int h0, int h1, float *O, float *m, float *l) {
+    if (sh->quant != ORC_Q8_0) return -1;
+    const int hd = sh->hd, R = sh->rows, NB = hd / 32;
+    if (bk <= 0) bk = 512;
+    int8_t *qi = (int8_t *) malloc((size_t) R * hd);
+    float *dq = (float *) malloc(sizeof(float) * (size_t) R * NB);
+    float *vb = (float *) malloc(sizeof(float) * (size_t) bk * hd);
+    float *S = (float *) malloc(sizeof(float) * (size_t) R * bk);
+    float *Ot = (float *) malloc(sizeof(float) * (size_t) R * hd);
+    float *alpha = (float *) malloc(sizeof(float) * R);
+    uint8_t blk[34];
+    for (int h = h0; h < h1; h++) {
+        float *Oh = O + (size_t) h * R * hd, *mh = m + (size_t) h * R, *lh = l + (size_t) h * R;
+        for (int r = 0; r < R; r++)
+            for (int b = 0; b < NB; b++) {
+                float x[32];
+                for (int i = 0; i < 32; i++) x[i] = h2f_fast(Qs[((size_t) h * R + r) * hd + b * 32 + i]);
+                orc_quant_q8_0(x, 1, blk);
+                uint16_t dh;
+                memcpy(&dh, blk, 2);
+                dq[(size_t) r * NB + b] = h2f_fast(dh);
+                for (int i = 0; i < 32; i++) qi[((size_t) r * NB + b) * 32 + i] = (int8_t) blk[2 + i];
+            }
+        for (int r = 0; r < R; r++) { mh[r] = -1e30f; lh[r] = 0; }
+        memset(Oh, 0, sizeof(float) * (size_t) R * hd);
+        for (uint32_t j0 = 0; j0 < nk; j0 += (uint32_t) bk) {
+            const int b = nk - j0 < (uint32_t) bk ? (int) (nk - j0) : bk;
+            for (int j = 0; j < b; j++) {
+                const uint8_t *hp = K + (size_t) (j0 + j) * sh->rs + (size_t) h * sh->hb;
+                for (int r = 0; r < R; r++) {
+                    float acc = 0;
+                    for (int q = 0; q < NB; q++) {
+                        const uint8_t *p = hp + q * 34;
+                        uint16_t dh;
+                        memcpy(&dh, p, 2);
+                        int32_t t = 0;
+                        const int8_t *qr = qi + ((size_t) r * NB + q) * 32;
+                        for (int i = 0; i < 32; i++) t += (int32_t) qr[i] * (int32_t) (int8_t) p[2 + i];
+                        acc = fmaf((float) t, dq[(size_t) r * NB + q] * h2f_fast(dh), acc);
+                    }
+                    S[(size_t) r * bk + j] = acc;
+                }
+            }
+            for (int r = 0; r < R; r++) {
+                float *sr = S + (size_t) r * bk;
+                float mx = -INFINITY;
+                for (int j = 0; j < b; j++) mx = fmaxf(mx, sr[j]);
+                const float mn = fmaxf(mh[r], mx);
+                alpha[r] = expf(mh[r] - mn);
+                mh[r] = mn;
+                float ls = 0;
+                for (int j = 0; j < b; j++) {
+                    const float p = expf(sr[j] - mn);
+                    ls += p;
+                    sr[j] = r16(p);
+                }
+                lh[r] = fmaf(lh[r], alpha[r], ls);
+            }
+            deq_block(sh, V + (size_t) j0 * sh->rs, b, h, vb, 0, hd);
+            for (int r = 0; r < R; r++) {
+                float *ot = Ot + (size_t) r * hd;
+                const float *pr = S + (size_t) r * bk;
+                for (int d = 0; d < hd; d++) ot[d] = 0;
+                for (int j = 0; j < b; j++) {
+                    const float p = pr[j];
+                    const float *vj = vb + (size_t) j * hd;
+                    for (int d = 0; d < hd; d++) ot[d] += p * vj[d];
+                }
+                float *o = Oh + (size_t) r * hd;
+                for (int d = 0; d < hd; d++) o[d] = fmaf(o[d], alpha[r], ot[d]);
+            }
+        }
+    }
+    free(qi); free(dq); free(vb); free(S); free(Ot); free(alpha);
+    return 0;
+}
+
 /* ---------------------------------------------------------------- merges */
 
 void orc_merge_partial(float *O, float *m, float *l, const float *O2, const float *m2, const float *l2, size_t rows,

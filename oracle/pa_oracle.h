@@ -13,6 +13,8 @@
  *   orc_quant_q4_0               BASELINE Q4_0 rule: d = max|x|/7, q = rint(x/d) + 8 in [1,15], byte i = q[i] | q[i+16] << 4
  *   orc_partial_f64              phone-attn/pa-tool.cpp:150-173, scripts/sme/sme_attn.c:641-676 (fp64 reference)
  *   orc_partial_f32              scripts/sme/sme_attn.c:274-306 (block online softmax, f16 K/V/P, fp32 accumulators)
+ *   orc_partial_f32_i8q          the same with the int8-domain QK of scripts/sme/sme_attn.c:465-508 (sme_qk_i8blk,
+ *                                i8_combine), Q quantised per 32-block by the Q8_0 rule
  *   orc_partial_f32_mt           the same over (head x key chunk) threads, chunks folded with orc_merge_partial
  *   orc_merge_partial            phone-attn/phone-attn.h:231-239 (generalised to any head dim)
  *   orc_merge_slots              phone-attn/pa-metal.mm:137-159  (pa_merge: LSE fold of chunk slots)
@@ -69,6 +71,11 @@ void orc_partial_f64(const orc_shape *sh, const uint16_t *Qs, const uint8_t *K, 
  * f16 before P.V, m starts at -1e30 as in the reference. heads [h0, h1) only. */
 void orc_partial_f32(const orc_shape *sh, const uint16_t *Qs, const uint8_t *K, const uint8_t *V, uint32_t nk,
                      int bk, int h0, int h1, float *O, float *m, float *l);
+
+/* The same with the int8-domain QK of scripts/sme/sme_attn.c:465-508: Q quantised per 32-block (Q8_0 rule), per-block
+ * int32 dot products with the q8_0 K integers, s = sum_b float(T_b) * (dq_b * dk_b). Q8_0 rows only (else -1). */
+int orc_partial_f32_i8q(const orc_shape *sh, const uint16_t *Qs, const uint8_t *K, const uint8_t *V, uint32_t nk,
+                        int bk, int h0, int h1, float *O, float *m, float *l);
 
 /* orc_partial_f32 on nthreads pthreads over (head, chunk of chunk_keys) items; chunk partials of a head are
  * folded in key order. Returns 0 on success. */

@@ -211,3 +211,21 @@ def test_reference_pa_tool_gate_passes_on_oracle(env, extra):
     finally:
         srv.kill()
         srv.wait()
+
+
+def test_int8_domain_qk_error_against_fp64():
+    """The reference's int8-domain QK (scripts/sme/sme_attn.c:465-508: sme_qk_i8blk's per-block int32 dot products of
+    int8 Q and q8_0 K, combined by i8_combine as sum_b float(T_b) dq_b dk_b), with Q quantised per 32-block by the Q8_0
+    rule, measured against the fp64 oracle with the reference's check metrics (sme_attn.c:768-772: per-row O/l error,
+    m error, l error). On the BASELINE distributions its O error is ~1e-2: past pa-tool's 5e-3 gate and the 2e-3
+    north-star tolerance, where the f16-domain QK the kernels use stays within both; this is why the CUDA path keeps Q
+    in f16 (the variant is a bench-only kernel in the reference)."""
+    for hd, nkv, rows, nk, seed in [(128, 8, 5, 8192, 1), (256, 4, 48, 4096, 3)]:
+        c = orc.gen_case(seed, hd, nkv, rows, nk, orc.Q8_0)
+        Of, mf, lf = orc.partial_f64(c["shape"], c["Qs"], c["K"], c["V"], nk)
+        O1, m1, l1 = orc.partial_f32(c["shape"], c["Qs"], c["K"], c["V"], nk)
+        O2, m2, l2 = orc.partial_f32_i8q(c["shape"], c["Qs"], c["K"], c["V"], nk)
+        e16, e8 = orc.rel_err(O1, m1, l1, Of, mf, lf), orc.rel_err(O2, m2, l2, Of, mf, lf)
+        assert e16[0] <= 2e-3 and e16[1] <= 2e-3, e16
+        assert e8[0] > 3e-3 and e8[1] > 5e-3, e8
+        assert np.abs(m2 - mf).max() > 1e-2 > np.abs(m1 - mf).max()

@@ -1,7 +1,8 @@
 """pa_cuda_shard_attn_allgather_merge: position shards over NCCL in one call (one process per GPU; each rank's plan covers
 its contiguous range of positions of every output set; the ranks' packed (O, m, l) are exchanged and folded on every
-rank). Both exchanges are covered: the all-gather followed by the fold, and the max / sum all-reduces; with and without
-output-set groups (a group's exchange overlapping the next group's kernels).
+rank). Every exchange is covered: the all-gather followed by the fold, the max / sum all-reduces (with and without
+output-set groups, a group's exchange overlapping the next group's kernels), and the peer stores over NVLink (each rank's
+merged rows stored into every rank's receive buffer, the fold waiting on per-source counters).
 
 A communicator of one rank must give what the plan alone gives; two ranks on two GPUs must agree with each other bit
 for bit and with the oracle over all positions (2e-3, as the other parity tests). A rank that leaves between steps must
@@ -22,7 +23,7 @@ from test_decode_gpu import TOL_REF
 pytestmark = pytest.mark.gpu
 
 HD, NKV, ROWS, NK, SETS = 128, 8, 5, 3000, 4
-MODES = [(1, 1), (1, 3), (2, 1), (2, 3)]   # (exchange: 1 all-gather, 2 all-reduce; set groups)
+MODES = [(1, 1), (1, 3), (2, 1), (2, 3), (3, 1)]   # (exchange: 1 all-gather, 2 all-reduce, 3 peer stores; set groups)
 
 
 def _cases():
@@ -58,9 +59,12 @@ def test_one_rank_equals_the_plan(ctx):
                 O2, m2, l2 = torch.full_like(O1, 7.0), torch.full_like(m1, 7.0), torch.full_like(l1, 7.0)
                 pa.shard_attn_allgather_merge(plan, Qs, comm, O2, m2, l2)
                 ctx.status()
-                np.testing.assert_allclose(O2.cpu().numpy(), O1.cpu().numpy(), rtol=1e-6, atol=1e-7)
+                assert ctx.shard_last()[0] == mode, (mode, ctx.shard_last())
+                # the same arithmetic up to the order of the fp32 sums (merges of different shapes)
+                o1 = O1.cpu().numpy()
+                np.testing.assert_allclose(O2.cpu().numpy(), o1, rtol=1e-5, atol=1e-6 * np.abs(o1).max())
                 np.testing.assert_allclose(m2.cpu().numpy(), m1.cpu().numpy(), rtol=1e-6)
-                np.testing.assert_allclose(l2.cpu().numpy(), l1.cpu().numpy(), rtol=1e-6)
+                np.testing.assert_allclose(l2.cpu().numpy(), l1.cpu().numpy(), rtol=1e-5)
     finally:
         ctx.set_shard_exchange(0)
         ctx.set_shard_groups(0)
@@ -93,6 +97,7 @@ def _rank(rank, world, uid, q):
             for _ in range(2):
                 pa2.shard_attn_allgather_merge(plan, Qs, comm, O, m, l)
                 ctx.status()
+                assert ctx.shard_last()[0] == mode, (mode, ctx.shard_last())
                 out[(mode, groups)].append((O.cpu().numpy(), m.cpu().numpy(), l.cpu().numpy()))
         comm.close()
         plan.close()
