@@ -240,6 +240,7 @@ cudaError_t launch_prefill(const pa_cuda_plan *p, uint32_t nj, const CUtensorMap
                            cudaStream_t st) {
     auto kern = pa::pre::prefill_kernel<Q, NT>;
     constexpr int smem = pa::pre::Smem<Q, NT>::TOTAL + 1024;   // + alignment slack for the 1024-byte operand tiles
+    static_assert(smem <= 227 * 1024, "shared memory of a CTA");
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid(nj * p->sh.nkv * p->n_rt);   // CTA = (row-tile group, head, job), row-tile group fastest

@@ -191,17 +191,21 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int b_mn_major) {
     return (1u << 4) | ((uint32_t) b_mn_major << 16) | ((uint32_t) (N >> 3) << 17) | ((uint32_t) (M >> 4) << 24);
 }
 
-// shared-memory map (all operand tiles 1024-aligned)
-template <int QUANT, int NT>
+// dequantised K and V buffers (a ring) of the single-CTA kernel: 4 with one Q tile (shared memory has room; measured
+// +1% on the config-3 verify batch over 2), 2 with two tiles
+__host__ __device__ constexpr int kv_bufs(int nt) { return nt == 1 ? 4 : 2; }
+
+// shared-memory map (all operand tiles 1024-aligned); KVB dequantised K and V buffers
+template <int QUANT, int NT, int KVB = kv_bufs(NT)>
 struct Smem {
     static constexpr int RAWB = raw_row_bytes(QUANT);
     static constexpr int Q = 0;                                   // NT x [2 atom cols][128 rows][128 B]
-    static constexpr int K = Q + NT * BM * HD * 2;                 // 2 x [2 atom cols][64 keys][128 B]
-    static constexpr int V = K + 2 * BN * HD * 2;                  // 2 x same (read MN-major)
-    static constexpr int RAW = V + 2 * BN * HD * 2;                // NS x (K rows, V rows) x [64][RAWB]
+    static constexpr int K = Q + NT * BM * HD * 2;                 // KVB x [2 atom cols][64 keys][128 B]
+    static constexpr int V = K + KVB * BN * HD * 2;                // KVB x same (read MN-major)
+    static constexpr int RAW = V + KVB * BN * HD * 2;              // NS x (K rows, V rows) x [64][RAWB]
     static constexpr int RAW_STAGE = (2 * BN * RAWB + 1023) / 1024 * 1024;
     static constexpr int BAR = RAW + NS * RAW_STAGE;
-    static constexpr int N_BAR = 1 + 2 * NS + 8 + 7 * NT + 1 + 1;
+    static constexpr int N_BAR = 1 + 2 * NS + 4 * KVB + 7 * NT + 1 + 1;
     static constexpr int TOTAL = BAR + N_BAR * 8 + 32;
 };
 
@@ -211,7 +215,8 @@ __host__ __device__ constexpr int dq_warps(int nt) { return nt == 1 ? 8 : 4; }
 template <int QUANT, int NT>
 __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_kernel(const __grid_constant__ CUtensorMap tq,
                                                                        const Params p) {
-    using L = Smem<QUANT, NT>;
+    constexpr int KVB = kv_bufs(NT);
+    using L = Smem<QUANT, NT, KVB>;
     constexpr int RAWB = L::RAWB;
     constexpr int GB = dec::q_group_bytes(QUANT);
     constexpr uint32_t IDESC_S = idesc_f16(BM, BN, 0);
@@ -227,8 +232,8 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::BAR);
     uint64_t *q_full = bar;
     uint64_t *raw_full = bar + 1, *raw_empty = raw_full + NS;
-    uint64_t *k_full = raw_empty + NS, *k_free = k_full + 2, *v_full = k_free + 2, *v_free = v_full + 2;
-    uint64_t *s_full = v_free + 2;             // [NT]: S of the block in TMEM
+    uint64_t *k_full = raw_empty + NS, *k_free = k_full + KVB, *v_full = k_free + KVB, *v_free = v_full + KVB;
+    uint64_t *s_full = v_free + KVB;           // [NT]: S of the block in TMEM
     uint64_t *s_empty = s_full + NT;           // [NT]: the softmax has read S into registers
     uint64_t *p_full = s_empty + NT;           // [NT][2]: P of the block in P buffer j & 1 (one barrier per buffer, so
                                                // the softmax finishing block j+1 cannot complete block j's phase)
@@ -256,7 +261,7 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
         for (int s = 0; s < NS; s++) { mbar_init(&raw_full[s], 1); mbar_init(&raw_empty[s], NDQ); }
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < KVB; b++) {
             mbar_init(&k_full[b], NDQ); mbar_init(&k_free[b], 1); mbar_init(&v_full[b], NDQ); mbar_init(&v_free[b], 1);
         }
         for (int t = 0; t < NT; t++) {
@@ -344,8 +349,8 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
             const uint64_t dq0 = sdesc(sbase + L::Q, 16, 1024), dk0 = sdesc(sbase + L::K, 16, 1024);
             if (wait(q_full, 0)) {
                 for (uint32_t j = 0; j < nblk && ok; j++) {
-                    const uint32_t b = j & 1;
-                    if (!wait(&k_full[b], (j >> 1) & 1)) break;
+                    const uint32_t b = j % KVB;
+                    if (!wait(&k_full[b], (j / KVB) & 1)) break;
                     const uint64_t dk = dk0 + b * (uint32_t) (BN * HD * 2 / 16);
 #pragma unroll
                     for (int t = 0; t < NT; t++) {
@@ -366,19 +371,20 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
         } else if (lane == 0) {
             const uint64_t dv0 = sdesc(sbase + L::V, BN * 128, 1024);
             for (uint32_t jj = 0; jj < nblk && ok; jj++) {
-                const uint32_t b = jj & 1;
-                if (!wait(&v_full[b], (jj >> 1) & 1)) break;
+                const uint32_t b = jj % KVB;   // V buffer
+                if (!wait(&v_full[b], (jj / KVB) & 1)) break;
                 const uint64_t dv = dv0 + b * (uint32_t) (BN * HD * 2 / 16);
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
-                    if (!wait(&p_full[2 * t + b], (jj >> 1) & 1)) break;
+                    const uint32_t pb = jj & 1;   // P buffer
+                    if (!wait(&p_full[2 * t + pb], (jj >> 1) & 1)) break;
                     tc_fence_after();
                     const uint32_t d = tmem + t * 256 + 128;
-                    const uint32_t pa = tmem + t * 256 + BN + b * (BN / 2);   // P buffer b (f16, two keys per column)
+                    const uint32_t pa = tmem + t * 256 + BN + pb * (BN / 2);   // P buffer pb (f16, two keys per column)
 #pragma unroll
                     for (int ks = 0; ks < BN / 16; ks++)
                         tc_mma_ts(d, pa + ks * 8, dv + (uint32_t) (ks * 2048 / 16), IDESC_PV, (jj > 0 || ks > 0) ? 1u : 0u);
-                    tc_commit(&pv_free[2 * t + b]);   // P buffer b and O (through this block) are settled
+                    tc_commit(&pv_free[2 * t + pb]);   // P buffer pb and O (through this block) are settled
                     if (jj + 1 == nblk) tc_commit(&o_ready[t]);
                 }
                 if (!ok) break;
@@ -479,7 +485,7 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
                     tmem_ld32(tl + 128 + q * 32, o);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int i = 0; i < 32; i++) o[i] *= alpha;
+                    for (int x = 0; x < 32; x++) o[x] *= alpha;
                     tmem_st32(tl + 128 + q * 32, o);
                 }
                 tmem_wait_st();
@@ -527,12 +533,12 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
         const uint32_t w0 = (ds - w16) / 4, shift = 8 * (ds % 4);
         const uint32_t colb = (qblk / 2) * BN * 128;        // atom column of this block's d's
         for (uint32_t j = 0; j < nblk; j++) {
-            const uint32_t st = j % NS, b = j & 1;
+            const uint32_t st = j % NS, b = j % KVB;
             if (!wait(&raw_full[st], (j / NS) & 1)) break;
             const uint32_t raw = sbase + L::RAW + st * L::RAW_STAGE;
 #pragma unroll
             for (int kv = 0; kv < 2; kv++) {
-                if (j >= 2 && !wait(kv == 0 ? &k_free[b] : &v_free[b], ((j - 2) >> 1) & 1)) break;
+                if (j >= KVB && !wait(kv == 0 ? &k_free[b] : &v_free[b], ((j / KVB) - 1) & 1)) break;
                 const uint32_t src = raw + kv * BN * RAWB;
                 const uint32_t dst = sbase + (kv == 0 ? L::K : L::V) + b * BN * HD * 2 + colb;
 #pragma unroll
