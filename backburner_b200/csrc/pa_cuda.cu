@@ -42,6 +42,10 @@ constexpr uint32_t kPairMinRows = 257;
 // 3.600, 8,192 3.708, 14,592 3.684; 16,384 keys per layer (an 8-way shard) as 1,024 0.491, 1,856 0.487, 2,048 0.535,
 // 4,096 0.532. (A persistent variant, each CTA taking several jobs through one stage stream, measured no better.)
 constexpr uint32_t kDecodeJobOverhead = 48;
+// Per-job overhead of the tcgen05 kernels in keys (a CTA's set-up is ~5-10 us, ~64 keys of an hd-256 block a us), for the
+// same model. Measured on the server's 8-token ATTN (hd 256, 4 KV heads, 48 rows, 32,768 keys): 1,024-key jobs 58.6 us
+// (kernel), 2,048-key jobs 51.6 us.
+constexpr uint32_t kPrefillJobOverhead = 512;
 
 struct Plan;
 
@@ -820,10 +824,27 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
     }
     uint32_t chunk = chunk_keys;
     if (chunk == 0 && p->prefill) {
-        // at least ~4 CTAs per SM in total, >= 1024 keys per job
+        // The job size that minimises waves x (keys per job + kPrefillJobOverhead), waves counting the CTAs of all jobs
+        // (every row group and KV head of a job; two per cluster) over one CTA per SM: a small call (the server's
+        // 8-token ATTN over 32k keys) gets about one wave of longer jobs instead of many short CTAs that each pay the
+        // set-up (TMEM, barriers, Q tiles, the ring's first stages); config 2 keeps a 65,536-key segment per job and
+        // the config-3 verify batch two jobs per 196,608-key layer (7 waves of 1,024 CTAs).
         const uint64_t ctas_per_job = (uint64_t) p->grid_y * (p->pair ? 2 : 1);
-        const uint64_t jobs_wanted = std::max<uint64_t>(1, ((uint64_t) ctx->n_sm * 4 + ctas_per_job - 1) / ctas_per_job);
-        chunk = (uint32_t) std::max<uint64_t>(1024, (total + jobs_wanted - 1) / jobs_wanted);
+        uint64_t best = ~0ull;
+        for (uint32_t c = 512; c <= 262144; c += 512) {
+            uint64_t jobs = 0, cmax = 0;
+            for (uint32_t i = 0; i < n_segs; i++) {
+                const uint32_t nk = segs[i].nk;
+                if (!nk) continue;
+                const uint32_t nj = (nk + c - 1) / c, cj = ((nk + nj - 1) / nj + 63) / 64 * 64;
+                jobs += (nk + cj - 1) / cj;
+                cmax = std::max<uint64_t>(cmax, cj);
+            }
+            const uint64_t waves = (jobs * ctas_per_job + ctx->n_sm - 1) / ctx->n_sm;
+            const uint64_t cost = waves * (cmax + kPrefillJobOverhead);
+            if (cost <= best) { best = cost; chunk = c; }
+        }
+        if (!chunk) chunk = 1024;
     } else if (chunk == 0) {
         // The job size that minimises the modelled time: waves x (keys per job + kDecodeJobOverhead). Waves count the
         // CTAs that fit all SMs at once.
