@@ -248,7 +248,7 @@ cudaError_t launch_prefill(const pa_cuda_plan *p, uint32_t nj, const CUtensorMap
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid(nj * p->sh.nkv * p->n_rt);   // CTA = (row-tile group, head, job), row-tile group fastest
-    kern<<<grid, 32 * (4 + 4 * NT + pa::pre::dq_warps(NT)), smem, st>>>(tq, prm);
+    kern<<<grid, 32 * pa::pre::cta_warps(NT), smem, st>>>(tq, prm);
     return cudaGetLastError();
 }
 // the CTA-pair kernel: clusters of 2 CTAs along x, one cluster per job
@@ -344,6 +344,7 @@ int run_attention_sets(pa_cuda_plan *p, const uint16_t *Qs, cudaStream_t st, uin
             return fail(ctx, PA_CUDA_ECUDA, "cuTensorMapEncodeTiled (Q) failed");
         pa::pre::Params prm{};
         prm.jobs = p->d_jobs + j0;
+        prm.Qs = Qs;
         prm.kv_maps = p->d_maps;
         prm.Op = p->d_op;
         prm.Mp = p->d_mp;

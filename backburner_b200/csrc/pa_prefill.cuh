@@ -7,17 +7,18 @@
 // one unnormalised (O, m, l) per chunk of keys. Head dim 128.
 //
 // One CTA = one chunk of keys of one segment x one KV head x NT tiles of 128 query rows. Warp roles:
-//   warp 0             TMA: the Q tiles once (128-byte swizzle, the UMMA operand layout), then per 64-key block the
-//                      raw quantised rows of this head (a 16-byte-aligned window of each key row, one 2-D tensor copy
-//                      for K and one for V; keys past the end read as zeros)
-//   warps 1, 2         warp 1 allocates TMEM (per tile: S 64 columns, two P buffers of 32, O 128); one thread of warp 1
-//                      issues the S_t = Q_t K^T MMAs (M=128, N=64) into S, one of warp 2 the O_t += P_t V MMAs (M=128,
-//                      N=128, A = P read from TMEM, B = V read MN-major) into O
+//   warp 0             TMA: with two tiles the Q tiles once (128-byte swizzle, the UMMA operand layout), then per
+//                      64-key block the raw quantised rows of this head (a 16-byte-aligned window of each key row, one
+//                      2-D tensor copy for K and one for V; keys past the end read as zeros)
+//   warps 1, 2         warp 1 allocates TMEM (two tiles, per tile: S 64 columns, two P buffers of 32, O 128; one tile:
+//                      two S buffers, four P buffers, O and the Q tile, 512 columns); one thread of warp 1 issues the
+//                      S_t = Q_t K^T MMAs (M=128, N=64; A = Q from shared or, one tile, tensor memory) into S, one of
+//                      warp 2 the O_t += P_t V MMAs (M=128, N=128, A = P read from TMEM, B = V read MN-major) into O
 //   warps 4 .. 4+4NT   one warpgroup per Q tile: thread = query row = TMEM lane. Reads its row of S (64 keys; S is
 //                      free again once read), masks tail keys, online softmax in the log2 domain with lazy rescaling (the
 //                      running max moves only when a block's max exceeds it by more than 8, so O in TMEM is rescaled
 //                      rarely), writes P as packed f16 into the block's P buffer: the softmax never waits for a P.V
-//                      except to rescale
+//                      except to rescale. With one tile the warpgroup also writes the Q tile into tensor memory
 //   last 8 (NT = 1) or  dequantise each raw K and V block into f16 operand tiles (f16(d * q), 128-byte swizzle)
 //   4 (NT = 2) warps
 // All waits are bounded; a wait that runs out records a status, and every role still reaches the final barrier so
@@ -34,7 +35,7 @@ namespace pre {
 constexpr int HD = 128;
 constexpr int BM = 128;   // query rows per tile = TMEM lanes
 constexpr int BN = 64;    // keys per block
-constexpr int NS = 3;     // raw stages
+constexpr int NS = 3;     // raw stages of the CTA-pair kernel's TMA ring
 
 // bytes of the 16-byte-aligned window that holds one head of a key row: the head (hd/32 blocks of 34 B for Q8_0, 18 B
 // for Q4_0) plus its offset inside the window (head h starts at h * hb: offset 0 or 8 when hb % 16 == 8, else 0),
@@ -45,6 +46,7 @@ __host__ __device__ constexpr int raw_row_bytes(int quant, int hd = 128) {
 
 struct Params {
     const dec::Job *jobs;
+    const uint16_t *Qs;           // f16(q*scale) [n_sets][nkv][rows][HD] (the one-tile kernel reads its rows directly)
     const CUtensorMap *kv_maps;   // [2*seg] K rows, [2*seg+1] V rows: 16-bit elements {rs/2, nk}, box {raw_row_bytes/2,
                                   // keys per copy} (16-bit elements keep a 272-byte window within TMA's 256-element box)
     float *Op, *Mp, *Lp;          // slot partials [slot][nkv][rows][HD], [slot][nkv][rows]
@@ -194,26 +196,40 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int b_mn_major) {
 // dequantised K and V buffers (a ring) of the single-CTA kernel: 4 with one Q tile (shared memory has room; measured
 // +1% on the config-3 verify batch over 2), 2 with two tiles
 __host__ __device__ constexpr int kv_bufs(int nt) { return nt == 1 ? 4 : 2; }
+// raw (quantised) K/V stages of the single-CTA kernel's TMA ring
+__host__ __device__ constexpr int raw_stages(int quant, int nt) { return 3; }
+// dequant warps of the single-CTA kernel: 8 with one Q tile (the dequant is the larger cost per row there), 4 with two
+__host__ __device__ constexpr int dq_warps(int nt) { return nt == 1 ? 8 : 4; }
+// warps of a CTA: TMA + MMA warpgroup, one softmax warpgroup per Q tile, dequant
+__host__ __device__ constexpr int cta_warps(int nt) { return 4 + 4 * nt + dq_warps(nt); }
+// S accumulators per Q tile in tensor memory: two with one tile (the S MMA of block j+1 runs while the softmax still
+// works on block j; a CTA has the SM's 512 columns to itself), one with two tiles (each tile's S, P and O fill 256)
+__host__ __device__ constexpr int s_bufs(int nt) { return nt == 1 ? 2 : 1; }
+// Q in tensor memory: the one-tile kernel keeps its Q tile in TMEM (64 columns) as the A operand of S = Q K^T, so an S
+// MMA reads only its K slice from shared memory (from shared memory, each N = 64 MMA re-read a 4 KB Q slice: twice the
+// K bytes it multiplies); with two tiles tensor memory is full and Q stays in shared memory
+__host__ __device__ constexpr bool q_in_tmem(int nt) { return nt == 1; }
+// P buffers per Q tile in tensor memory: four with one tile (the softmax writes P of block j once P.V of block j-4 is
+// done, so a P.V queued behind S MMAs in the tensor pipe does not hold the softmax up), two with two tiles
+__host__ __device__ constexpr int p_bufs(int nt) { return nt == 1 ? 4 : 2; }
 
 // shared-memory map (all operand tiles 1024-aligned); KVB dequantised K and V buffers
 template <int QUANT, int NT, int KVB = kv_bufs(NT)>
 struct Smem {
     static constexpr int RAWB = raw_row_bytes(QUANT);
-    static constexpr int Q = 0;                                   // NT x [2 atom cols][128 rows][128 B]
-    static constexpr int K = Q + NT * BM * HD * 2;                 // KVB x [2 atom cols][64 keys][128 B]
+    static constexpr int Q = 0;                                   // NT x [2 atom cols][128 rows][128 B] (or none)
+    static constexpr int K = Q + (q_in_tmem(NT) ? 0 : NT * BM * HD * 2);   // KVB x [2 atom cols][64 keys][128 B]
     static constexpr int V = K + KVB * BN * HD * 2;                // KVB x same (read MN-major)
-    static constexpr int RAW = V + KVB * BN * HD * 2;              // NS x (K rows, V rows) x [64][RAWB]
+    static constexpr int NRS = raw_stages(QUANT, NT);
+    static constexpr int RAW = V + KVB * BN * HD * 2;              // NRS x (K rows, V rows) x [64][RAWB]
     static constexpr int RAW_STAGE = (2 * BN * RAWB + 1023) / 1024 * 1024;
-    static constexpr int BAR = RAW + NS * RAW_STAGE;
-    static constexpr int N_BAR = 1 + 2 * NS + 4 * KVB + 7 * NT + 1 + 1;
+    static constexpr int BAR = RAW + NRS * RAW_STAGE;
+    static constexpr int N_BAR = 1 + 2 * NRS + 4 * KVB + (2 * s_bufs(NT) + 2 * p_bufs(NT) + 1) * NT + 1 + 1;
     static constexpr int TOTAL = BAR + N_BAR * 8 + 32;
 };
 
-// dequant warps of the single-CTA kernel: 8 with one Q tile (the dequant is the larger cost per row there), 4 with two
-__host__ __device__ constexpr int dq_warps(int nt) { return nt == 1 ? 8 : 4; }
-
 template <int QUANT, int NT>
-__global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_kernel(const __grid_constant__ CUtensorMap tq,
+__global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __grid_constant__ CUtensorMap tq,
                                                                        const Params p) {
     constexpr int KVB = kv_bufs(NT);
     using L = Smem<QUANT, NT, KVB>;
@@ -221,24 +237,36 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
     constexpr int GB = dec::q_group_bytes(QUANT);
     constexpr uint32_t IDESC_S = idesc_f16(BM, BN, 0);
     constexpr uint32_t IDESC_PV = idesc_f16(BM, HD, 1);
-    // warpgroups: 0 = TMA (warp 0) + MMA (warp 1) + 2 idle warps, 1..NT = softmax of tile t, last = dequant
+    // warpgroups: 0 = TMA (warp 0) + MMA (warps 1, 2) + 1 idle warp, 1..NT = softmax of tile t, last = dequant
     constexpr int SM0 = 4, DQ0 = 4 + 4 * NT;   // first softmax warp, first dequant warp
     constexpr int NDQ = dq_warps(NT);
+    // tensor memory of tile t from column t * 256: S (64 columns), two P buffers (32 columns each, f16 packed two keys
+    // per column), O (128 columns); with one tile its second S buffer sits at column 256, where a second tile's S
+    // would, so every accumulator keeps the alignment of the two-tile layout, and P buffers 2 and 3 at 320 and 352
+    constexpr int NSB = s_bufs(NT), NPB = p_bufs(NT);
+    constexpr bool QT = q_in_tmem(NT);
+    constexpr uint32_t T_P = BN, T_O = 2 * BN, TCOLS = NSB == 2 ? 512 : 256 * NT;
+    constexpr uint32_t T_Q = 384;   // Q (one tile): row = lane, column c = f16 elements 2c, 2c + 1
+    static_assert(!QT || (NT == 1 && NSB == 2 && NPB == 4), "Q in TMEM sits after P buffers 2, 3 of the one-tile layout");
+    static_assert(NPB == 2 || (NT == 1 && NSB == 2), "P buffers 2, 3 live in the one-tile 512-column layout");
+    // column of P buffer i (relative to the tile)
+    auto p_col = [](uint32_t i) -> uint32_t { return i < 2 ? T_P + i * (BN / 2) : 256 + BN + (i - 2) * (BN / 2); };
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // operand tiles need 1024-byte alignment (128-byte swizzle atoms): align the dynamic base explicitly
     uint8_t *smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
     const uint32_t sbase = smem_u32(smem);
     uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L::BAR);
-    uint64_t *q_full = bar;
-    uint64_t *raw_full = bar + 1, *raw_empty = raw_full + NS;
-    uint64_t *k_full = raw_empty + NS, *k_free = k_full + KVB, *v_full = k_free + KVB, *v_free = v_full + KVB;
-    uint64_t *s_full = v_free + KVB;           // [NT]: S of the block in TMEM
-    uint64_t *s_empty = s_full + NT;           // [NT]: the softmax has read S into registers
-    uint64_t *p_full = s_empty + NT;           // [NT][2]: P of the block in P buffer j & 1 (one barrier per buffer, so
-                                               // the softmax finishing block j+1 cannot complete block j's phase)
-    uint64_t *pv_free = p_full + 2 * NT;       // [NT][2]: P.V of a block with P buffer b completed
-    uint64_t *o_ready = pv_free + 2 * NT;      // [NT]: the last P.V completed (once)
+    uint64_t *q_full = bar;   // Q tile(s) in shared memory (TMA) or, one tile, in tensor memory (the softmax warps)
+    constexpr int NRS = L::NRS;
+    uint64_t *raw_full = bar + 1, *raw_empty = raw_full + NRS;
+    uint64_t *k_full = raw_empty + NRS, *k_free = k_full + KVB, *v_full = k_free + KVB, *v_free = v_full + KVB;
+    uint64_t *s_full = v_free + KVB;           // [NT][NSB]: S of the block in S buffer j % NSB of the tile
+    uint64_t *s_empty = s_full + NT * NSB;     // [NT][NSB]: the softmax has read that S into registers
+    uint64_t *p_full = s_empty + NT * NSB;     // [NT][NPB]: P of the block in P buffer j % NPB (one barrier per buffer,
+                                               // so the softmax finishing a later block cannot complete block j's phase)
+    uint64_t *pv_free = p_full + NPB * NT;     // [NT][NPB]: P.V of a block with P buffer i completed
+    uint64_t *o_ready = pv_free + NPB * NT;    // [NT]: the last P.V completed (once)
     uint64_t *mma_done = o_ready + NT;         // every MMA this CTA issued has completed (before TMEM is freed)
     uint64_t *never = mma_done + 1;            // completed by nobody: the stall test hook waits on it
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + L::N_BAR);
@@ -259,18 +287,25 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
     bool ok = true;
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
-        for (int s = 0; s < NS; s++) { mbar_init(&raw_full[s], 1); mbar_init(&raw_empty[s], NDQ); }
+        // Q in tensor memory: one arrival per softmax warp with a real row (see below), else the TMA thread's
+        mbar_init(q_full, QT ? min(4u, (p.rows - row0 + 31) / 32) : 1u);
+        for (int s = 0; s < NRS; s++) { mbar_init(&raw_full[s], 1); mbar_init(&raw_empty[s], NDQ); }
         for (int b = 0; b < KVB; b++) {
             mbar_init(&k_full[b], NDQ); mbar_init(&k_free[b], 1); mbar_init(&v_full[b], NDQ); mbar_init(&v_free[b], 1);
         }
         for (int t = 0; t < NT; t++) {
-            mbar_init(&s_full[t], 1);
-            mbar_init(&s_empty[t], 4);
-            mbar_init(&p_full[2 * t], 4);
-            mbar_init(&p_full[2 * t + 1], 4);
-            mbar_init(&pv_free[2 * t], 1);
-            mbar_init(&pv_free[2 * t + 1], 1);
+            // softmax warps that take part: those with a real row (a lane quarter wholly past the call's rows sits out;
+            // NT = 1 only, see the softmax role)
+            const uint32_t first = row0 + t * BM;
+            const uint32_t nq = NT == 1 ? min(4u, (p.rows - first + 31) / 32) : 4u;
+            for (int sb = 0; sb < NSB; sb++) {
+                mbar_init(&s_full[t * NSB + sb], 1);
+                mbar_init(&s_empty[t * NSB + sb], nq);
+            }
+            for (int i = 0; i < NPB; i++) {
+                mbar_init(&p_full[t * NPB + i], nq);
+                mbar_init(&pv_free[t * NPB + i], 1);
+            }
             mbar_init(&o_ready[t], 1);
         }
         mbar_init(mma_done, 2);
@@ -281,9 +316,9 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
     }
     __syncthreads();
     if (*abort_flag) return;   // uniform: before TMEM is allocated
-    if (warp == 1) {   // TMEM: per tile S x2 (64 columns each) + O (128 columns)
+    if (warp == 1) {   // TMEM: per tile S, two P buffers and O; one tile: a second S
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(256 * NT)
+                     "r"(TCOLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -308,20 +343,22 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
     if (warp < 4) {
       // 16 warps launched with 128 registers each at NT = 1 and 2; each warpgroup resizes its share (NT = 1: control 160,
       // softmax 168, two dequant warpgroups 88: 128 x (160 + 168 + 88 + 88) = 64,512 <= 65,536)
-      if (NT == 1) asm volatile("setmaxnreg.inc.sync.aligned.u32 160;");
+      if constexpr (NT == 1) asm volatile("setmaxnreg.inc.sync.aligned.u32 160;");
       if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
-            const int qrow = (int) (((uint64_t) job.set * p.nkv + h) * p.rows + row0);
-            mbar_arrive_expect_tx(q_full, NT * BM * HD * 2);
-            for (int t = 0; t < NT; t++)
-                for (int c = 0; c < 2; c++)
-                    tma_2d(smem + L::Q + t * BM * HD * 2 + c * BM * 128, &tq, c * 64, qrow + t * BM, q_full);
+            if constexpr (!QT) {
+                const int qrow = (int) (((uint64_t) job.set * p.nkv + h) * p.rows + row0);
+                mbar_arrive_expect_tx(q_full, NT * BM * HD * 2);
+                for (int t = 0; t < NT; t++)
+                    for (int c = 0; c < 2; c++)
+                        tma_2d(smem + L::Q + t * BM * HD * 2 + c * BM * 128, &tq, c * 64, qrow + t * BM, q_full);
+            }
             const CUtensorMap *km = p.kv_maps + 2 * job.seg, *vm = km + 1;
             uint32_t issued = 0;
             for (uint32_t j = 0; j < nblk; j++) {
-                const uint32_t st = j % NS;
-                if (j >= NS && !wait(&raw_empty[st], ((j / NS) - 1) & 1)) break;
+                const uint32_t st = j % NRS;
+                if (j >= NRS && !wait(&raw_empty[st], ((j / NRS) - 1) & 1)) break;
                 mbar_arrive_expect_tx(&raw_full[st], 2 * BN * RAWB);
                 uint8_t *dst = smem + L::RAW + st * L::RAW_STAGE;
                 tma_2d(dst, km, hx / 2, (int) (job.key0 + j * BN), &raw_full[st]);
@@ -331,10 +368,10 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
             // on an abort, every issued copy lands before the CTA exits
             if (!ok) {
                 const uint64_t drain = tmo > dec::DRAIN_NS ? tmo : dec::DRAIN_NS;
-                if (!mbar_wait_bounded(q_full, 0, drain, nullptr)) atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
-                const uint32_t first = issued > NS ? issued - NS : 0;
+                if (!QT && !mbar_wait_bounded(q_full, 0, drain, nullptr)) atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
+                const uint32_t first = issued > NRS ? issued - NRS : 0;
                 for (uint32_t j = first; j < issued; j++)
-                    if (!mbar_wait_bounded(&raw_full[j % NS], (j / NS) & 1, drain, nullptr))
+                    if (!mbar_wait_bounded(&raw_full[j % NRS], (j / NRS) & 1, drain, nullptr))
                         atomicCAS(p.status, ST_OK, ST_TIMEOUT_DRAIN);
             }
         }
@@ -354,15 +391,21 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
                     const uint64_t dk = dk0 + b * (uint32_t) (BN * HD * 2 / 16);
 #pragma unroll
                     for (int t = 0; t < NT; t++) {
-                        if (j >= 1 && !wait(&s_empty[t], (j - 1) & 1)) break;
+                        const uint32_t sb = t * NSB + j % NSB;   // the block's S buffer
+                        if (j >= NSB && !wait(&s_empty[sb], ((j / NSB) - 1) & 1)) break;
                         tc_fence_after();
-                        const uint32_t d = tmem + t * 256;
+                        const uint32_t d = tmem + t * 256 + (j % NSB) * 256;
                         const uint64_t dq = dq0 + (uint32_t) (t * BM * HD * 2 / 16);
 #pragma unroll
-                        for (int kk = 0; kk < HD / 16; kk++)
-                            tc_mma(d, dq + (uint32_t) (((kk / 4) * BM * 128 + (kk % 4) * 32) / 16),
-                                   dk + (uint32_t) (((kk / 4) * BN * 128 + (kk % 4) * 32) / 16), IDESC_S, kk > 0 ? 1u : 0u);
-                        tc_commit(&s_full[t]);
+                        for (int kk = 0; kk < HD / 16; kk++) {
+                            const uint64_t bk = dk + (uint32_t) (((kk / 4) * BN * 128 + (kk % 4) * 32) / 16);
+                            if constexpr (QT)   // A = Q from tensor memory: 8 columns (16 f16) per k-step
+                                tc_mma_ts(d, tmem + t * 256 + T_Q + kk * 8, bk, IDESC_S, kk > 0 ? 1u : 0u);
+                            else
+                                tc_mma(d, dq + (uint32_t) (((kk / 4) * BM * 128 + (kk % 4) * 32) / 16), bk, IDESC_S,
+                                       kk > 0 ? 1u : 0u);
+                        }
+                        tc_commit(&s_full[sb]);
                     }
                     if (!ok) break;
                     tc_commit(&k_free[b]);
@@ -376,15 +419,15 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
                 const uint64_t dv = dv0 + b * (uint32_t) (BN * HD * 2 / 16);
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
-                    const uint32_t pb = jj & 1;   // P buffer
-                    if (!wait(&p_full[2 * t + pb], (jj >> 1) & 1)) break;
+                    const uint32_t pb = jj % NPB;   // P buffer
+                    if (!wait(&p_full[t * NPB + pb], (jj / NPB) & 1)) break;
                     tc_fence_after();
-                    const uint32_t d = tmem + t * 256 + 128;
-                    const uint32_t pa = tmem + t * 256 + BN + pb * (BN / 2);   // P buffer pb (f16, two keys per column)
+                    const uint32_t d = tmem + t * 256 + T_O;
+                    const uint32_t pa = tmem + t * 256 + p_col(pb);   // P buffer pb (f16, two keys per column)
 #pragma unroll
                     for (int ks = 0; ks < BN / 16; ks++)
                         tc_mma_ts(d, pa + ks * 8, dv + (uint32_t) (ks * 2048 / 16), IDESC_PV, (jj > 0 || ks > 0) ? 1u : 0u);
-                    tc_commit(&pv_free[2 * t + pb]);   // P buffer pb and O (through this block) are settled
+                    tc_commit(&pv_free[t * NPB + pb]);   // P buffer pb and O (through this block) are settled
                     if (jj + 1 == nblk) tc_commit(&o_ready[t]);
                 }
                 if (!ok) break;
@@ -401,41 +444,65 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
       }   // warp 3: idle
     } else if (warp < (uint32_t) DQ0) {
         // ------------------------------------------------ softmax warpgroup of tile t
-        if (NT == 2) asm volatile("setmaxnreg.inc.sync.aligned.u32 152;");
+        if constexpr (NT == 2) asm volatile("setmaxnreg.inc.sync.aligned.u32 152;");
         else asm volatile("setmaxnreg.inc.sync.aligned.u32 168;");
         if (p.stall) wait(never, 0);                       // runs out: records the timeout, every role unwinds
         const int t = (int) (warp - SM0) / 4;
         const uint32_t wq = warp % 4;                      // TMEM lane quarter of this warp
         const uint32_t r = wq * 32 + lane;                 // row of the tile = TMEM lane
         const uint32_t tl = tmem + ((wq * 32) << 16) + t * 256;
-        // a warp whose 32 rows are all past the call's rows (a partly filled tile) only keeps the barrier protocol: its
-        // rows' O is never written and MMA rows are independent, so its P may stay as it is. (Its p_full arrival for
-        // block j + 2 needs S of j + 2, which needs every warp's s_empty of j + 1, after their p_full of j.)
-        // (NT = 1 only: the small-row calls; the two-tile softmax has no registers to spare for it)
+        // a warp whose 32 rows are all past the call's rows (a partly filled tile; NT = 1 only) sits the blocks out: the
+        // S, P and Q barriers count only the warps with a real row, its rows' O is never written and MMA rows are
+        // independent, so its S, P and Q may stay as they are. (It must not arrive at all: with two S buffers a warp that
+        // did no work could arrive for block j + 2 before the real warps wrote P of block j.)
         const bool pad = NT == 1 && row0 + t * BM + wq * 32 >= p.rows;
+        // Q in tensor memory: each warp with a real row writes its lanes' Q rows (rows past the call's rows as zeros)
+        // into the Q columns, then arrives on q_full, which the S issuer waits for
+        if constexpr (QT) {
+            if (!pad && ok) {
+                uint32_t qv[HD / 2];
+                const uint32_t row = row0 + r;
+                if (row < p.rows) {
+                    const uint4 *src =
+                        reinterpret_cast<const uint4 *>(p.Qs + (((uint64_t) job.set * p.nkv + h) * p.rows + row) * HD);
+#pragma unroll
+                    for (int i = 0; i < HD / 8; i++) {
+                        const uint4 v = __ldg(src + i);
+                        qv[4 * i] = v.x; qv[4 * i + 1] = v.y; qv[4 * i + 2] = v.z; qv[4 * i + 3] = v.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < HD / 2; i++) qv[i] = 0u;
+                }
+#pragma unroll
+                for (int c = 0; c < HD / 64; c++)
+                    tmem_st32u(tl + T_Q + 32 * c, *reinterpret_cast<const uint32_t(*)[32]>(qv + 32 * c));
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(q_full);
+            }
+        }
         float m_used = -INFINITY, l = 0.f;
         float m_row = -INFINITY;   // the row's exact maximum (log2 units); O and l are reported against it
-        for (uint32_t j = 0; j < nblk; j++) {
-            const uint32_t b = j & 1;
-            if (!wait(&s_full[t], j & 1)) break;
-            if (pad) {
-                __syncwarp();
-                if (lane == 0) { mbar_arrive(&s_empty[t]); mbar_arrive(&p_full[2 * t + b]); }
-                continue;
-            }
+        for (uint32_t j = 0; j < nblk && !pad; j++) {
+            const uint32_t b = j % NPB;                    // the block's P buffer
+            const uint32_t sb = t * NSB + j % NSB;         // the block's S buffer
+            if (!wait(&s_full[sb], (j / NSB) & 1)) break;
             tc_fence_after();
-            float s[64];
+            const uint32_t ts = tl + (j % NSB) * 256;
+            float s[BN];
             {
                 float a[32], c[32];
-                tmem_ld32(tl, a);
-                tmem_ld32(tl + 32, c);
+                tmem_ld32(ts, a);
+                tmem_ld32(ts + 32, c);
                 tmem_wait_ld();
 #pragma unroll
                 for (int i = 0; i < 32; i++) { s[i] = a[i]; s[32 + i] = c[i]; }
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[t]);
+            if (lane == 0) mbar_arrive(&s_empty[sb]);
             const int nvalid = (int) (job.nk - j * BN);
             if (nvalid < BN) {
 #pragma unroll
@@ -459,9 +526,9 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
             // p = 2^(s*log2e - m): scale-and-shift and the row sum on fp32 pairs (fma/add .f32x2)
             const uint64_t l2e2 = pack_f2(LOG2E, LOG2E), nm2 = pack_f2(-m_used, -m_used);
             uint64_t acc = pack_f2(0.f, 0.f);
-            uint32_t ph[32];
+            uint32_t ph[BN / 2];
 #pragma unroll
-            for (int i = 0; i < 32; i++) {
+            for (int i = 0; i < BN / 2; i++) {
                 float t0, t1;
                 unpack_f2(fma_f2(pack_f2(s[2 * i], s[2 * i + 1]), l2e2, nm2), t0, t1);
                 const float p0 = ex2(t0), p1 = ex2(t1);
@@ -469,33 +536,32 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
                 acc = add_f2(acc, pp);
                 ph[i] = pack_h2(p0, p1);
             }
-            float sa, sb;
-            unpack_f2(acc, sa, sb);
-            const float sum = sa + sb;
-            l = fmaf(l, alpha, sum);
+            float sum_a, sum_b;
+            unpack_f2(acc, sum_a, sum_b);
+            l = fmaf(l, alpha, sum_a + sum_b);
             // O is rescaled (rarely: the lazy max moved) once P.V of block j-1 has completed; P buffer b is free once
-            // P.V of block j-2 (its last reader) has. Each buffer's barrier completes once per P.V on that buffer, and
-            // P.V of block j cannot start before this P is written, so each wait names exactly one completion.
+            // P.V of block j-NPB (its last reader) has. Each buffer's barrier completes once per P.V on that buffer,
+            // and P.V of block j cannot start before this P is written, so each wait names exactly one completion.
             if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
-                if (!wait(&pv_free[2 * t + (b ^ 1)], ((j - 1) >> 1) & 1)) break;
+                if (!wait(&pv_free[t * NPB + (j - 1) % NPB], ((j - 1) / NPB) & 1)) break;
                 tc_fence_after();
 #pragma unroll
                 for (int q = 0; q < HD / 32; q++) {
                     float o[32];
-                    tmem_ld32(tl + 128 + q * 32, o);
+                    tmem_ld32(tl + T_O + q * 32, o);
                     tmem_wait_ld();
 #pragma unroll
                     for (int x = 0; x < 32; x++) o[x] *= alpha;
-                    tmem_st32(tl + 128 + q * 32, o);
+                    tmem_st32(tl + T_O + q * 32, o);
                 }
                 tmem_wait_st();
             }
-            if (j >= 2 && !wait(&pv_free[2 * t + b], ((j - 2) >> 1) & 1)) break;
-            tmem_st32u(tl + BN + b * (BN / 2), ph);   // P, two keys per column, into P buffer b
+            if (j >= NPB && !wait(&pv_free[t * NPB + b], ((j / NPB) - 1) & 1)) break;
+            tmem_st32u(tl + p_col(b), ph);   // P, two keys per column, into P buffer b
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[2 * t + b]);
+            if (lane == 0) mbar_arrive(&p_full[t * NPB + b]);
         }
         // final: O from TMEM to the slot partial, moved from the lazy reference max m_used to the row's exact maximum
         // (m = max_j s_j, as sme_attn_partial reports it): one factor 2^(m_used - m_row) in (2^-8, 1] on O and l
@@ -507,7 +573,7 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
 #pragma unroll
             for (int q = 0; q < HD / 32; q++) {
                 float o[32];
-                tmem_ld32(tl + 128 + q * 32, o);
+                tmem_ld32(tl + T_O + q * 32, o);
                 tmem_wait_ld();
                 if (row < p.rows) {
                     float4 *dst = reinterpret_cast<float4 *>(p.Op + orow * HD + q * 32);
@@ -533,8 +599,8 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
         const uint32_t w0 = (ds - w16) / 4, shift = 8 * (ds % 4);
         const uint32_t colb = (qblk / 2) * BN * 128;        // atom column of this block's d's
         for (uint32_t j = 0; j < nblk; j++) {
-            const uint32_t st = j % NS, b = j % KVB;
-            if (!wait(&raw_full[st], (j / NS) & 1)) break;
+            const uint32_t st = j % NRS, b = j % KVB;
+            if (!wait(&raw_full[st], (j / NRS) & 1)) break;
             const uint32_t raw = sbase + L::RAW + st * L::RAW_STAGE;
 #pragma unroll
             for (int kv = 0; kv < 2; kv++) {
@@ -615,7 +681,7 @@ __global__ void __launch_bounds__(32 * (4 + 4 * NT + dq_warps(NT)), 1) prefill_k
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256 * NT) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
     }
 }
 
