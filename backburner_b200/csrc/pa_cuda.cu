@@ -37,6 +37,9 @@ constexpr uint32_t kPrefillMinRows128 = 24, kPrefillMinRows256 = 32;
 // filled tile. Measured (8 KV heads x 4 layers x 65,536 Q8_0 keys, TFLOP/s single vs pair): 256 rows 676 vs 558,
 // 320 510 vs 549, 384 608 vs 643, 448 667 vs 694, 512 751 vs 784
 constexpr uint32_t kPairMinRows = 257;
+// ... and up to which hd-256 calls run on the single-CTA kernel with one 128-row tile (its CTAs hold half the rows of a
+// pair's, so a small call spreads over twice the jobs in one wave); above, on CTA pairs
+constexpr uint32_t kSingle256MaxRows = 128;
 // Per-job overhead of the decode kernel in keys, for the job-size model of pa_cuda_plan_create. Fitted on B200 to
 // config-1 runs of the current kernel (kernel ms, 64 layers): 131,072 keys per layer as 2,048-key jobs 3.618, 4,096
 // 3.600, 8,192 3.708, 14,592 3.684; 16,384 keys per layer (an 8-way shard) as 1,024 0.491, 1,856 0.487, 2,048 0.535,
@@ -239,11 +242,11 @@ bool map_q(CUtensorMap *m, const void *Qs, uint64_t n_rows, uint32_t hd) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int Q, int NT>
+template <int Q, int NT, int D = 128>
 cudaError_t launch_prefill(const pa_cuda_plan *p, uint32_t nj, const CUtensorMap &tq, const pa::pre::Params &prm,
                            cudaStream_t st) {
-    auto kern = pa::pre::prefill_kernel<Q, NT>;
-    constexpr int smem = pa::pre::Smem<Q, NT>::TOTAL + 1024;   // + alignment slack for the 1024-byte operand tiles
+    auto kern = pa::pre::prefill_kernel<Q, NT, D>;
+    constexpr int smem = pa::pre::Smem<Q, NT, D>::TOTAL + 1024;   // + alignment slack for the 1024-byte operand tiles
     static_assert(smem <= 227 * 1024, "shared memory of a CTA");
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -368,6 +371,9 @@ int run_attention_sets(pa_cuda_plan *p, const uint16_t *Qs, cudaStream_t st, uin
                 e = p->nt == 2 ? launch_prefill_pair<1, 2, 128>(p, nj, tq, prm, st) : launch_prefill_pair<1, 1, 128>(p, nj, tq, prm, st);
             else
                 e = p->nt == 2 ? launch_prefill_pair<2, 2, 128>(p, nj, tq, prm, st) : launch_prefill_pair<2, 1, 128>(p, nj, tq, prm, st);
+        } else if (sh.hd == 256) {   // one Q tile of 128 rows per CTA
+            e = sh.quant == PA_CUDA_Q8_0 ? launch_prefill<1, 1, 256>(p, nj, tq, prm, st)
+                                         : launch_prefill<2, 1, 256>(p, nj, tq, prm, st);
         } else if (sh.quant == PA_CUDA_Q8_0) {
             e = p->nt == 2 ? launch_prefill<1, 2>(p, nj, tq, prm, st) : launch_prefill<1, 1>(p, nj, tq, prm, st);
         } else {
@@ -793,21 +799,22 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
     if ((rc = plan_decode_shape(ctx, p))) { delete p; return rc; }
     // the tcgen05 kernel takes calls with many query rows per KV head (prefill, ATTN_BIG, long verify batches), the
     // split-K kernel the decode-sized ones (as the reference engine switches kernels by rows, pa-metal.mm:818-835)
-    // (hd 256, the reference server's wire geometry, runs on the CTA-pair kernel only)
-    const bool tc_ok = (shape->hd == 128 || (shape->hd == 256 && ctx->kernel_choice != 2)) &&
-                       shape->quant != PA_CUDA_F16 && encode_fn() != nullptr;
+    // (hd 256, the reference server's wire geometry: one 128-row tile per CTA up to kSingle256MaxRows rows per KV head,
+    // CTA pairs above)
+    const bool tc_ok = (shape->hd == 128 || shape->hd == 256) && shape->quant != PA_CUDA_F16 && encode_fn() != nullptr;
     const uint32_t min_rows = shape->hd == 128 ? kPrefillMinRows128 : kPrefillMinRows256;
     p->prefill = tc_ok && (ctx->kernel_choice >= 2 || (ctx->kernel_choice == 0 && shape->rows >= min_rows));
     if (ctx->kernel_choice >= 2 && !tc_ok) {
         delete p;
         return fail(ctx, PA_CUDA_EUNSUPPORTED,
-                    "tcgen05 kernels need quantised (Q8_0 / Q4_0) rows and hd 128 (single CTA) or 128 / 256 (CTA pairs)");
+                    "tcgen05 kernels need quantised (Q8_0 / Q4_0) rows and hd 128 or 256");
     }
     if (p->prefill) {
         // PA_CUDA_TC_TILES=1|2: Q tiles of 128 rows per CTA (default: 2 when there are more than 128 rows)
         static const int tiles_env = getenv("PA_CUDA_TC_TILES") ? atoi(getenv("PA_CUDA_TC_TILES")) : 0;
         // CTA pairs (2-SM MMAs, half of each K/V block dequantised per SM) from kPairMinRows rows per KV head
-        p->pair = shape->hd == 256 || ctx->kernel_choice == 3 || (ctx->kernel_choice == 0 && shape->rows >= kPairMinRows);
+        p->pair = ctx->kernel_choice == 3 ||
+                  (ctx->kernel_choice == 0 && shape->rows >= (shape->hd == 256 ? kSingle256MaxRows + 1 : kPairMinRows));
         const uint32_t tile_rows = (uint32_t) pa::pre::BM * (p->pair ? 2u : 1u);
         p->nt = shape->hd == 256 ? 1 : (tiles_env == 1 || tiles_env == 2) ? tiles_env : (shape->rows > tile_rows ? 2 : 1);
         p->n_rt = (shape->rows + tile_rows * p->nt - 1) / (tile_rows * p->nt);
@@ -943,14 +950,17 @@ const char *pa_cuda_plan_kernel(const pa_cuda_plan *p) {
     if (!p) return "";
     const uint32_t q = p->sh.quant;
     if (p->prefill) {
-        static const char *names[3][2][2] = {
+        static const char *names[4][2][2] = {
             {{"pa::pre::prefill_kernel<1,1>", "pa::pre::prefill_kernel<1,2>"},
              {"pa::pre::prefill_kernel<2,1>", "pa::pre::prefill_kernel<2,2>"}},
             {{"pa::pre::prefill_pair_kernel<1,1,128>", "pa::pre::prefill_pair_kernel<1,2,128>"},
              {"pa::pre::prefill_pair_kernel<2,1,128>", "pa::pre::prefill_pair_kernel<2,2,128>"}},
             {{"pa::pre::prefill_pair_kernel<1,1,256>", "pa::pre::prefill_pair_kernel<1,1,256>"},
-             {"pa::pre::prefill_pair_kernel<2,1,256>", "pa::pre::prefill_pair_kernel<2,1,256>"}}};
-        return names[!p->pair ? 0 : p->sh.hd == 256 ? 2 : 1][q == PA_CUDA_Q8_0 ? 0 : 1][p->nt == 2 ? 1 : 0];
+             {"pa::pre::prefill_pair_kernel<2,1,256>", "pa::pre::prefill_pair_kernel<2,1,256>"}},
+            {{"pa::pre::prefill_kernel<1,1,256>", "pa::pre::prefill_kernel<1,1,256>"},
+             {"pa::pre::prefill_kernel<2,1,256>", "pa::pre::prefill_kernel<2,1,256>"}}};
+        const int k = !p->pair ? (p->sh.hd == 256 ? 3 : 0) : p->sh.hd == 256 ? 2 : 1;
+        return names[k][q == PA_CUDA_Q8_0 ? 0 : 1][p->nt == 2 ? 1 : 0];
     }
     static const char *dec[3][3] = {
         {"pa::dec::decode_kernel<128,0,8>", "pa::dec::decode_kernel<128,1,8>", "pa::dec::decode_kernel<128,2,8>"},

@@ -193,61 +193,69 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int b_mn_major) {
     return (1u << 4) | ((uint32_t) b_mn_major << 16) | ((uint32_t) (N >> 3) << 17) | ((uint32_t) (M >> 4) << 24);
 }
 
-// dequantised K and V buffers (a ring) of the single-CTA kernel: 4 with one Q tile (shared memory has room; measured
-// +1% on the config-3 verify batch over 2), 2 with two tiles
-__host__ __device__ constexpr int kv_bufs(int nt) { return nt == 1 ? 4 : 2; }
-// raw (quantised) K/V stages of the single-CTA kernel's TMA ring
-__host__ __device__ constexpr int raw_stages(int quant, int nt) { return 3; }
+// The single-CTA kernel's layout depends on the tile count NT and the head dim D (D = 256: one tile only, the reference
+// server's wire geometry).
+// dequantised K and V buffers (a ring): 4 with one Q tile at D = 128 (shared memory has room; measured +1% on the
+// config-3 verify batch over 2), else 2 (D = 256: 32 KB per buffer)
+__host__ __device__ constexpr int kv_bufs(int nt, int d = 128) { return nt == 1 && d == 128 ? 4 : 2; }
+// raw (quantised) K/V stages of the TMA ring: 3, or 2 at D = 256 (a stage of Q8_0 rows is 34 KB there)
+__host__ __device__ constexpr int raw_stages(int quant, int nt, int d = 128) { return d == 128 ? 3 : 2; }
 // dequant warps of the single-CTA kernel: 8 with one Q tile (the dequant is the larger cost per row there), 4 with two
 __host__ __device__ constexpr int dq_warps(int nt) { return nt == 1 ? 8 : 4; }
 // warps of a CTA: TMA + MMA warpgroup, one softmax warpgroup per Q tile, dequant
 __host__ __device__ constexpr int cta_warps(int nt) { return 4 + 4 * nt + dq_warps(nt); }
-// S accumulators per Q tile in tensor memory: two with one tile (the S MMA of block j+1 runs while the softmax still
-// works on block j; a CTA has the SM's 512 columns to itself), one with two tiles (each tile's S, P and O fill 256)
-__host__ __device__ constexpr int s_bufs(int nt) { return nt == 1 ? 2 : 1; }
-// Q in tensor memory: the one-tile kernel keeps its Q tile in TMEM (64 columns) as the A operand of S = Q K^T, so an S
+// S accumulators per Q tile in tensor memory: two with one tile at D = 128 (the S MMA of block j+1 runs while the
+// softmax still works on block j; a CTA has the SM's 512 columns to itself), else one (two tiles: each tile's S, P and
+// O fill 256 columns; D = 256: O takes 256 and Q 128)
+__host__ __device__ constexpr int s_bufs(int nt, int d = 128) { return nt == 1 && d == 128 ? 2 : 1; }
+// Q in tensor memory: the one-tile kernel keeps its Q tile in TMEM (D / 2 columns) as the A operand of S = Q K^T, so an S
 // MMA reads only its K slice from shared memory (from shared memory, each N = 64 MMA re-read a 4 KB Q slice: twice the
 // K bytes it multiplies); with two tiles tensor memory is full and Q stays in shared memory
 __host__ __device__ constexpr bool q_in_tmem(int nt) { return nt == 1; }
-// P buffers per Q tile in tensor memory: four with one tile (the softmax writes P of block j once P.V of block j-4 is
-// done, so a P.V queued behind S MMAs in the tensor pipe does not hold the softmax up), two with two tiles
-__host__ __device__ constexpr int p_bufs(int nt) { return nt == 1 ? 4 : 2; }
+// P buffers per Q tile in tensor memory: four with one tile at D = 128 (the softmax writes P of block j once P.V of
+// block j-4 is done, so a P.V queued behind S MMAs in the tensor pipe does not hold the softmax up), else two
+__host__ __device__ constexpr int p_bufs(int nt, int d = 128) { return nt == 1 && d == 128 ? 4 : 2; }
 
 // shared-memory map (all operand tiles 1024-aligned); KVB dequantised K and V buffers
-template <int QUANT, int NT, int KVB = kv_bufs(NT)>
+template <int QUANT, int NT, int D = 128>
 struct Smem {
-    static constexpr int RAWB = raw_row_bytes(QUANT);
-    static constexpr int Q = 0;                                   // NT x [2 atom cols][128 rows][128 B] (or none)
-    static constexpr int K = Q + (q_in_tmem(NT) ? 0 : NT * BM * HD * 2);   // KVB x [2 atom cols][64 keys][128 B]
-    static constexpr int V = K + KVB * BN * HD * 2;                // KVB x same (read MN-major)
-    static constexpr int NRS = raw_stages(QUANT, NT);
-    static constexpr int RAW = V + KVB * BN * HD * 2;              // NRS x (K rows, V rows) x [64][RAWB]
+    static_assert(D == 128 || (D == 256 && NT == 1), "head dim 256 takes one Q tile");
+    static constexpr int KVB = kv_bufs(NT, D);
+    static constexpr int RAWB = raw_row_bytes(QUANT, D);
+    static constexpr int Q = 0;                                   // NT x [D/64 atom cols][128 rows][128 B] (or none)
+    static constexpr int K = Q + (q_in_tmem(NT) ? 0 : NT * BM * D * 2);   // KVB x [D/64 atom cols][64 keys][128 B]
+    static constexpr int V = K + KVB * BN * D * 2;                 // KVB x same (read MN-major)
+    static constexpr int NRS = raw_stages(QUANT, NT, D);
+    static constexpr int RAW = V + KVB * BN * D * 2;               // NRS x (K rows, V rows) x [64][RAWB]
     static constexpr int RAW_STAGE = (2 * BN * RAWB + 1023) / 1024 * 1024;
     static constexpr int BAR = RAW + NRS * RAW_STAGE;
-    static constexpr int N_BAR = 1 + 2 * NRS + 4 * KVB + (2 * s_bufs(NT) + 2 * p_bufs(NT) + 1) * NT + 1 + 1;
+    static constexpr int N_BAR = 1 + 2 * NRS + 4 * KVB + (2 * s_bufs(NT, D) + 2 * p_bufs(NT, D) + 1) * NT + 1 + 1;
     static constexpr int TOTAL = BAR + N_BAR * 8 + 32;
 };
 
-template <int QUANT, int NT>
+template <int QUANT, int NT, int D = 128>
 __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __grid_constant__ CUtensorMap tq,
                                                                        const Params p) {
-    constexpr int KVB = kv_bufs(NT);
-    using L = Smem<QUANT, NT, KVB>;
+    using L = Smem<QUANT, NT, D>;
+    constexpr int KVB = L::KVB;
     constexpr int RAWB = L::RAWB;
     constexpr int GB = dec::q_group_bytes(QUANT);
     constexpr uint32_t IDESC_S = idesc_f16(BM, BN, 0);
-    constexpr uint32_t IDESC_PV = idesc_f16(BM, HD, 1);
+    constexpr uint32_t IDESC_PV = idesc_f16(BM, D, 1);
     // warpgroups: 0 = TMA (warp 0) + MMA (warps 1, 2) + 1 idle warp, 1..NT = softmax of tile t, last = dequant
     constexpr int SM0 = 4, DQ0 = 4 + 4 * NT;   // first softmax warp, first dequant warp
     constexpr int NDQ = dq_warps(NT);
-    // tensor memory of tile t from column t * 256: S (64 columns), two P buffers (32 columns each, f16 packed two keys
-    // per column), O (128 columns); with one tile its second S buffer sits at column 256, where a second tile's S
-    // would, so every accumulator keeps the alignment of the two-tile layout, and P buffers 2 and 3 at 320 and 352
-    constexpr int NSB = s_bufs(NT), NPB = p_bufs(NT);
+    // tensor memory (512 columns) of tile t from column t * 256: S (64 columns), two P buffers (32 columns each, f16
+    // packed two keys per column), O (D columns); D = 128 with one tile: the second S buffer at column 256, where a
+    // second tile's S would, so every accumulator keeps the alignment of the two-tile layout, P buffers 2 and 3 at 320
+    // and 352, Q at 384; D = 256 (one tile): O at 128-383, Q at 384-511
+    constexpr int NSB = s_bufs(NT, D), NPB = p_bufs(NT, D);
     constexpr bool QT = q_in_tmem(NT);
-    constexpr uint32_t T_P = BN, T_O = 2 * BN, TCOLS = NSB == 2 ? 512 : 256 * NT;
+    constexpr uint32_t T_P = BN, T_O = 2 * BN, TCOLS = 512;
     constexpr uint32_t T_Q = 384;   // Q (one tile): row = lane, column c = f16 elements 2c, 2c + 1
-    static_assert(!QT || (NT == 1 && NSB == 2 && NPB == 4), "Q in TMEM sits after P buffers 2, 3 of the one-tile layout");
+    static_assert(T_O + D <= (NSB == 2 || NPB > 2 ? 256u : T_Q) && T_Q + (QT ? D / 2 : 0) <= TCOLS,
+                  "one-tile tensor memory layout");
+    static_assert(!QT || NT == 1, "Q in tensor memory with one tile only");
     static_assert(NPB == 2 || (NT == 1 && NSB == 2), "P buffers 2, 3 live in the one-tile 512-column layout");
     // column of P buffer i (relative to the tile)
     auto p_col = [](uint32_t i) -> uint32_t { return i < 2 ? T_P + i * (BN / 2) : 256 + BN + (i - 2) * (BN / 2); };
@@ -349,10 +357,10 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
         if (lane == 0) {
             if constexpr (!QT) {
                 const int qrow = (int) (((uint64_t) job.set * p.nkv + h) * p.rows + row0);
-                mbar_arrive_expect_tx(q_full, NT * BM * HD * 2);
+                mbar_arrive_expect_tx(q_full, NT * BM * D * 2);
                 for (int t = 0; t < NT; t++)
-                    for (int c = 0; c < 2; c++)
-                        tma_2d(smem + L::Q + t * BM * HD * 2 + c * BM * 128, &tq, c * 64, qrow + t * BM, q_full);
+                    for (int c = 0; c < D / 64; c++)
+                        tma_2d(smem + L::Q + t * BM * D * 2 + c * BM * 128, &tq, c * 64, qrow + t * BM, q_full);
             }
             const CUtensorMap *km = p.kv_maps + 2 * job.seg, *vm = km + 1;
             uint32_t issued = 0;
@@ -388,16 +396,16 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
                 for (uint32_t j = 0; j < nblk && ok; j++) {
                     const uint32_t b = j % KVB;
                     if (!wait(&k_full[b], (j / KVB) & 1)) break;
-                    const uint64_t dk = dk0 + b * (uint32_t) (BN * HD * 2 / 16);
+                    const uint64_t dk = dk0 + b * (uint32_t) (BN * D * 2 / 16);
 #pragma unroll
                     for (int t = 0; t < NT; t++) {
                         const uint32_t sb = t * NSB + j % NSB;   // the block's S buffer
                         if (j >= NSB && !wait(&s_empty[sb], ((j / NSB) - 1) & 1)) break;
                         tc_fence_after();
                         const uint32_t d = tmem + t * 256 + (j % NSB) * 256;
-                        const uint64_t dq = dq0 + (uint32_t) (t * BM * HD * 2 / 16);
+                        const uint64_t dq = dq0 + (uint32_t) (t * BM * D * 2 / 16);
 #pragma unroll
-                        for (int kk = 0; kk < HD / 16; kk++) {
+                        for (int kk = 0; kk < D / 16; kk++) {
                             const uint64_t bk = dk + (uint32_t) (((kk / 4) * BN * 128 + (kk % 4) * 32) / 16);
                             if constexpr (QT)   // A = Q from tensor memory: 8 columns (16 f16) per k-step
                                 tc_mma_ts(d, tmem + t * 256 + T_Q + kk * 8, bk, IDESC_S, kk > 0 ? 1u : 0u);
@@ -416,7 +424,7 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
             for (uint32_t jj = 0; jj < nblk && ok; jj++) {
                 const uint32_t b = jj % KVB;   // V buffer
                 if (!wait(&v_full[b], (jj / KVB) & 1)) break;
-                const uint64_t dv = dv0 + b * (uint32_t) (BN * HD * 2 / 16);
+                const uint64_t dv = dv0 + b * (uint32_t) (BN * D * 2 / 16);
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
                     const uint32_t pb = jj % NPB;   // P buffer
@@ -460,23 +468,19 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
         // into the Q columns, then arrives on q_full, which the S issuer waits for
         if constexpr (QT) {
             if (!pad && ok) {
-                uint32_t qv[HD / 2];
                 const uint32_t row = row0 + r;
-                if (row < p.rows) {
-                    const uint4 *src =
-                        reinterpret_cast<const uint4 *>(p.Qs + (((uint64_t) job.set * p.nkv + h) * p.rows + row) * HD);
+                const uint4 *src =
+                    reinterpret_cast<const uint4 *>(p.Qs + (((uint64_t) job.set * p.nkv + h) * p.rows + row) * D);
 #pragma unroll
-                    for (int i = 0; i < HD / 8; i++) {
-                        const uint4 v = __ldg(src + i);
+                for (int c = 0; c < D / 64; c++) {   // 64 dims (32 columns) at a time
+                    uint32_t qv[32];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const uint4 v = row < p.rows ? __ldg(src + 8 * c + i) : make_uint4(0u, 0u, 0u, 0u);
                         qv[4 * i] = v.x; qv[4 * i + 1] = v.y; qv[4 * i + 2] = v.z; qv[4 * i + 3] = v.w;
                     }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < HD / 2; i++) qv[i] = 0u;
+                    tmem_st32u(tl + T_Q + 32 * c, qv);
                 }
-#pragma unroll
-                for (int c = 0; c < HD / 64; c++)
-                    tmem_st32u(tl + T_Q + 32 * c, *reinterpret_cast<const uint32_t(*)[32]>(qv + 32 * c));
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
@@ -546,7 +550,7 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
                 if (!wait(&pv_free[t * NPB + (j - 1) % NPB], ((j - 1) / NPB) & 1)) break;
                 tc_fence_after();
 #pragma unroll
-                for (int q = 0; q < HD / 32; q++) {
+                for (int q = 0; q < D / 32; q++) {
                     float o[32];
                     tmem_ld32(tl + T_O + q * 32, o);
                     tmem_wait_ld();
@@ -571,12 +575,12 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
             const uint64_t orow = ((uint64_t) job.slot * p.nkv + h) * p.rows + row;
             const float fix = m_row > -INFINITY ? ex2(m_used - m_row) : 1.f;
 #pragma unroll
-            for (int q = 0; q < HD / 32; q++) {
+            for (int q = 0; q < D / 32; q++) {
                 float o[32];
                 tmem_ld32(tl + T_O + q * 32, o);
                 tmem_wait_ld();
                 if (row < p.rows) {
-                    float4 *dst = reinterpret_cast<float4 *>(p.Op + orow * HD + q * 32);
+                    float4 *dst = reinterpret_cast<float4 *>(p.Op + orow * D + q * 32);
 #pragma unroll
                     for (int i = 0; i < 8; i++)
                         dst[i] = make_float4(o[4 * i] * fix, o[4 * i + 1] * fix, o[4 * i + 2] * fix, o[4 * i + 3] * fix);
@@ -588,16 +592,11 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
             }
         }
     } else {
-        // ------------------------------------------------ dequantisers: warp dw owns quant block dw % 4 of every key
-        // (4 warps: both 32-key halves of a block; 8 warps, NT = 1: key half dw / 4)
+        // ------------------------------------------------ dequantisers: warp dw owns quant blocks dw % 4 (+ 4 at
+        // D = 256) of every key (4 warps: both 32-key halves of a block; 8 warps, NT = 1: key half dw / 4)
         if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 80;");
         else asm volatile("setmaxnreg.dec.sync.aligned.u32 88;");
-        const uint32_t dw = warp - DQ0, qblk = dw % 4;
-        const uint32_t bo = hoff + GB * qblk;               // block start inside the raw window row
-        const uint32_t w16 = bo & ~15u;                     // 16-byte aligned start of the words covering it
-        const uint32_t ds = bo + 2;                         // first data byte
-        const uint32_t w0 = (ds - w16) / 4, shift = 8 * (ds % 4);
-        const uint32_t colb = (qblk / 2) * BN * 128;        // atom column of this block's d's
+        const uint32_t dw = warp - DQ0;
         for (uint32_t j = 0; j < nblk; j++) {
             const uint32_t st = j % NRS, b = j % KVB;
             if (!wait(&raw_full[st], (j / NRS) & 1)) break;
@@ -606,9 +605,16 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
             for (int kv = 0; kv < 2; kv++) {
                 if (j >= KVB && !wait(kv == 0 ? &k_free[b] : &v_free[b], ((j / KVB) - 1) & 1)) break;
                 const uint32_t src = raw + kv * BN * RAWB;
-                const uint32_t dst = sbase + (kv == 0 ? L::K : L::V) + b * BN * HD * 2 + colb;
 #pragma unroll
-                for (int pass = 0; pass < 8 / NDQ; pass++) {
+                for (int it = 0; it < (8 / NDQ) * (D / 128); it++) {
+                    const int pass = it % (8 / NDQ);
+                    const uint32_t qblk = dw % 4 + 4 * (uint32_t) (it / (8 / NDQ));
+                    const uint32_t bo = hoff + GB * qblk;               // block start inside the raw window row
+                    const uint32_t w16 = bo & ~15u;                     // 16-byte aligned start of the words covering it
+                    const uint32_t ds = bo + 2;                         // first data byte
+                    const uint32_t w0 = (ds - w16) / 4, shift = 8 * (ds % 4);
+                    // atom column of this block's d's
+                    const uint32_t dst = sbase + (kv == 0 ? L::K : L::V) + b * BN * D * 2 + (qblk / 2) * BN * 128;
                     const uint32_t key = (NDQ == 8 ? dw / 4 : (uint32_t) pass) * 32 + lane;
                     const uint32_t rb = src + key * RAWB;
                     const uint32_t s2 = lds16(rb + bo);

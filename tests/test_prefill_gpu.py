@@ -49,38 +49,45 @@ def test_tcgen05_pair_kernel_parity(ctx, rows, nk, quant):
 
 
 # head dim 256 (the reference server's wire geometry: HD 256, 48 rows per group, phone-attn.h:79-80) on the pair
-# kernel, chosen by default from 32 rows per KV head: ATTN_BIG groups (rows = 48 ng), an 8-token ATTN (48 rows), ragged
-# keys, Q4_0
+# kernel (the default above 128 rows per KV head; forced here for every size): ATTN_BIG groups (rows = 48 ng), an
+# 8-token ATTN (48 rows), ragged keys, Q4_0
 @pytest.mark.parametrize("rows,nk,quant", [
     (96, 2048, orc.Q8_0), (144, 4096, orc.Q8_0), (256, 1500, orc.Q4_0), (512, 777, orc.Q8_0), (300, 65, orc.Q8_0),
     (64, 1, orc.Q4_0), (768, 3000, orc.Q8_0), (48, 2500, orc.Q8_0), (32, 999, orc.Q4_0)])
 def test_tcgen05_pair_kernel_hd256_parity(ctx, rows, nk, quant):
     c = orc.gen_case(7000 + rows + nk + quant, 256, 8, rows, nk, quant)
-    O, m, l = _run_kernel(ctx, c, 0)
+    O, m, l = _run_kernel(ctx, c, 3)
     _check(c, O, m, l, nk)
 
 
-def test_hd256_plans_pick_the_pair_kernel(ctx):
+# head dim 256 on the single-CTA kernel with one 128-row tile (the default from 32 to 128 rows per KV head): an 8-token
+# ATTN (48 rows), two groups (96), a full tile, ragged keys, Q4_0, and more rows than one tile (forced: several tiles
+# per head as separate CTAs)
+@pytest.mark.parametrize("rows,nk,quant", [
+    (48, 2500, orc.Q8_0), (96, 2048, orc.Q8_0), (128, 4096, orc.Q8_0), (32, 999, orc.Q4_0), (64, 1, orc.Q4_0),
+    (80, 65, orc.Q8_0), (200, 777, orc.Q8_0)])
+def test_tcgen05_kernel_hd256_parity(ctx, rows, nk, quant):
+    c = orc.gen_case(7500 + rows + nk + quant, 256, 8, rows, nk, quant)
+    O, m, l = _run_kernel(ctx, c, 0 if rows <= 128 else 2)
+    _check(c, O, m, l, nk)
+
+
+def test_hd256_plans_pick_their_kernels(ctx):
     import torch
-    for rows, want in [(24, "pa::dec::decode_kernel<256,1,8>"), (48, "pa::pre::prefill_pair_kernel<1,1,256>")]:
+    for rows, want in [(24, "pa::dec::decode_kernel<256,1,8>"), (48, "pa::pre::prefill_kernel<1,1,256>"),
+                       (128, "pa::pre::prefill_kernel<1,1,256>"), (144, "pa::pre::prefill_pair_kernel<1,1,256>")]:
         shape = pa.shape_for(256, 8, rows, pa.Q8_0)
         K = torch.zeros((128, shape.rs), dtype=torch.uint8, device="cuda")
         plan = pa.Plan(ctx, shape, 1, [pa.Seg(K.data_ptr(), K.data_ptr(), 128, 0)])
         assert plan.kernel == want
         plan.close()
-    ctx.set_kernel(2)
-    try:
-        with pytest.raises(pa.PaCudaError):
-            pa.Plan(ctx, pa.shape_for(256, 8, 96, pa.Q8_0), 1, [pa.Seg(K.data_ptr(), K.data_ptr(), 128, 0)])
-    finally:
-        ctx.set_kernel(0)
 
 
-@pytest.mark.parametrize("hd,rows,nk", [(128, 80, 3000), (128, 256, 2000), (256, 192, 2500)])
+@pytest.mark.parametrize("hd,rows,nk", [(128, 80, 3000), (128, 256, 2000), (256, 192, 2500), (256, 48, 3000)])
 def test_tcgen05_matches_split_k_kernel(ctx, hd, rows, nk):
     c = orc.gen_case(77 + rows, hd, 8, rows, nk, orc.Q8_0)
     O1, m1, l1 = _run_kernel(ctx, c, 1)
-    for which in ((2, 3) if hd == 128 else (3,)):
+    for which in (2, 3):
         O2, m2, l2 = _run_kernel(ctx, c, which)
         e = orc.rel_err(O2, m2, l2, O1.astype(np.float64), m1.astype(np.float64), l1.astype(np.float64))
         assert e[0] <= 1e-3 and e[1] <= 1e-3, (which, e)
@@ -120,9 +127,9 @@ def test_tcgen05_student_t_values(ctx, which):
     _check(c, O, m, l, 3000)
 
 
-@pytest.mark.parametrize("which,hd,rows", [(2, 128, 256), (3, 128, 512), (3, 256, 96)])
+@pytest.mark.parametrize("which,hd,rows", [(2, 128, 256), (3, 128, 512), (3, 256, 96), (2, 256, 96)])
 def test_tcgen05_bounded_wait_reports_and_context_recovers(ctx, which, hd, rows):
-    """Failure detection without a GPU fault, on the tcgen05 kernels (single CTA; CTA pair at hd 128 and 256): with the
+    """Failure detection without a GPU fault, on the tcgen05 kernels (single CTA and CTA pair, hd 128 and 256): with the
     stall hook on, the softmax warps wait on a barrier that nothing completes; after the 1 ms limit the kernel records
     the timeout, every role of both CTAs of a pair unwinds through its bounded waits, TMEM is freed, the host reads
     ETIMEOUT, and the next call on the same context is correct."""
