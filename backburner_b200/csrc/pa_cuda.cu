@@ -30,15 +30,17 @@ namespace {
 constexpr int kMaxSmem = 227 * 1024;
 // query rows per KV head from which the tcgen05 kernels are used: they dequantise each key block once for all rows,
 // where the split-K kernel repeats it per 8-row group. Measured crossover (8 KV heads, Q8_0, GB/s split-K vs tcgen05):
-// hd 128: 16 rows 2,337 vs 2,024, 24 rows 1,578 vs 2,021, 40 rows 944 vs 1,942; hd 256 (pair kernel): 24 rows 1,642
-// vs 1,454, 32 rows 1,242 vs 1,468, 48 rows 848 vs 1,464
-constexpr uint32_t kPrefillMinRows128 = 24, kPrefillMinRows256 = 32;
+// hd 128: 16 rows 2,337 vs 2,024, 24 rows 1,578 vs 2,021, 40 rows 944 vs 1,942; hd 256 (4 layers x 32,768 keys,
+// single-CTA kernel): 8 rows 4,267 vs 3,547, 12 rows 2,259 vs 3,535, 16 rows 2,177 vs 3,545 (4 KV heads: 8 rows 3,463
+// vs 3,247, 12 rows 2,230 vs 3,238): one 8-row group stays on the split-K kernel
+constexpr uint32_t kPrefillMinRows128 = 24, kPrefillMinRows256 = 9;
 // ... and from which the hd-128 calls run on CTA pairs: past 256 rows the single-CTA kernel starts a second, partly
 // filled tile. Measured (8 KV heads x 4 layers x 65,536 Q8_0 keys, TFLOP/s single vs pair): 256 rows 676 vs 558,
 // 320 510 vs 549, 384 608 vs 643, 448 667 vs 694, 512 751 vs 784
 constexpr uint32_t kPairMinRows = 257;
-// ... and up to which hd-256 calls run on the single-CTA kernel with one 128-row tile (its CTAs hold half the rows of a
-// pair's, so a small call spreads over twice the jobs in one wave); above, on CTA pairs
+// ... and up to which hd-256 calls run on the single-CTA kernel with one 128-row tile; above, on CTA pairs. Measured
+// (8 KV heads x 4 layers x 32,768 Q8_0 keys, us single vs pair): 48 rows 166 vs 305, 128 rows 174 vs 305, 144 rows 327
+// vs 311, 256 rows 335 vs 317
 constexpr uint32_t kSingle256MaxRows = 128;
 // Per-job overhead of the decode kernel in keys, for the job-size model of pa_cuda_plan_create. Fitted on B200 to
 // config-1 runs of the current kernel (kernel ms, 64 layers): 131,072 keys per layer as 2,048-key jobs 3.618, 4,096

@@ -195,11 +195,19 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int b_mn_major) {
 
 // The single-CTA kernel's layout depends on the tile count NT and the head dim D (D = 256: one tile only, the reference
 // server's wire geometry).
-// dequantised K and V buffers (a ring): 4 with one Q tile at D = 128 (shared memory has room; measured +1% on the
-// config-3 verify batch over 2), else 2 (D = 256: 32 KB per buffer)
-__host__ __device__ constexpr int kv_bufs(int nt, int d = 128) { return nt == 1 && d == 128 ? 4 : 2; }
-// raw (quantised) K/V stages of the TMA ring: 3, or 2 at D = 256 (a stage of Q8_0 rows is 34 KB there)
-__host__ __device__ constexpr int raw_stages(int quant, int nt, int d = 128) { return d == 128 ? 3 : 2; }
+// keys per block: 128 with one tile at D = 128 (a block's hand-offs between the roles cost about the same whatever its
+// size, so larger blocks amortise them), else 64
+__host__ __device__ constexpr int block_keys(int nt, int d = 128) { return nt == 1 && d == 128 ? 128 : 64; }
+// the 64-key one-tile layout at D = 128 (two S buffers, four P buffers, a 4-deep K/V ring); every other one has 512 or
+// fewer columns of tensor memory for one S and two P buffers, and 32 KB K/V buffers in a 2-deep ring
+__host__ __device__ constexpr bool small_one_tile(int nt, int d) { return nt == 1 && d == 128 && block_keys(nt, d) == 64; }
+// dequantised K and V buffers (a ring): 4 in the 64-key one-tile layout (measured +1% on the config-3 verify batch over
+// 2), else 2
+__host__ __device__ constexpr int kv_bufs(int nt, int d = 128) { return small_one_tile(nt, d) ? 4 : 2; }
+// raw (quantised) K/V stages of the TMA ring: 3 with 64-key blocks at D = 128, else 2 (a stage of Q8_0 rows is 34-36 KB)
+__host__ __device__ constexpr int raw_stages(int quant, int nt, int d = 128) {
+    return d == 128 && block_keys(nt, d) == 64 ? 3 : 2;
+}
 // dequant warps of the single-CTA kernel: 8 with one Q tile (the dequant is the larger cost per row there), 4 with two
 __host__ __device__ constexpr int dq_warps(int nt) { return nt == 1 ? 8 : 4; }
 // warps of a CTA: TMA + MMA warpgroup, one softmax warpgroup per Q tile, dequant
@@ -207,27 +215,28 @@ __host__ __device__ constexpr int cta_warps(int nt) { return 4 + 4 * nt + dq_war
 // S accumulators per Q tile in tensor memory: two with one tile at D = 128 (the S MMA of block j+1 runs while the
 // softmax still works on block j; a CTA has the SM's 512 columns to itself), else one (two tiles: each tile's S, P and
 // O fill 256 columns; D = 256: O takes 256 and Q 128)
-__host__ __device__ constexpr int s_bufs(int nt, int d = 128) { return nt == 1 && d == 128 ? 2 : 1; }
+__host__ __device__ constexpr int s_bufs(int nt, int d = 128) { return small_one_tile(nt, d) ? 2 : 1; }
 // Q in tensor memory: the one-tile kernel keeps its Q tile in TMEM (D / 2 columns) as the A operand of S = Q K^T, so an S
 // MMA reads only its K slice from shared memory (from shared memory, each N = 64 MMA re-read a 4 KB Q slice: twice the
 // K bytes it multiplies); with two tiles tensor memory is full and Q stays in shared memory
 __host__ __device__ constexpr bool q_in_tmem(int nt) { return nt == 1; }
 // P buffers per Q tile in tensor memory: four with one tile at D = 128 (the softmax writes P of block j once P.V of
 // block j-4 is done, so a P.V queued behind S MMAs in the tensor pipe does not hold the softmax up), else two
-__host__ __device__ constexpr int p_bufs(int nt, int d = 128) { return nt == 1 && d == 128 ? 4 : 2; }
+__host__ __device__ constexpr int p_bufs(int nt, int d = 128) { return small_one_tile(nt, d) ? 4 : 2; }
 
 // shared-memory map (all operand tiles 1024-aligned); KVB dequantised K and V buffers
 template <int QUANT, int NT, int D = 128>
 struct Smem {
     static_assert(D == 128 || (D == 256 && NT == 1), "head dim 256 takes one Q tile");
     static constexpr int KVB = kv_bufs(NT, D);
+    static constexpr int B = block_keys(NT, D);                    // keys per block
     static constexpr int RAWB = raw_row_bytes(QUANT, D);
     static constexpr int Q = 0;                                   // NT x [D/64 atom cols][128 rows][128 B] (or none)
-    static constexpr int K = Q + (q_in_tmem(NT) ? 0 : NT * BM * D * 2);   // KVB x [D/64 atom cols][64 keys][128 B]
-    static constexpr int V = K + KVB * BN * D * 2;                 // KVB x same (read MN-major)
+    static constexpr int K = Q + (q_in_tmem(NT) ? 0 : NT * BM * D * 2);   // KVB x [D/64 atom cols][B keys][128 B]
+    static constexpr int V = K + KVB * B * D * 2;                  // KVB x same (read MN-major)
     static constexpr int NRS = raw_stages(QUANT, NT, D);
-    static constexpr int RAW = V + KVB * BN * D * 2;               // NRS x (K rows, V rows) x [64][RAWB]
-    static constexpr int RAW_STAGE = (2 * BN * RAWB + 1023) / 1024 * 1024;
+    static constexpr int RAW = V + KVB * B * D * 2;                // NRS x (K rows, V rows) x [B][RAWB]
+    static constexpr int RAW_STAGE = (2 * B * RAWB + 1023) / 1024 * 1024;
     static constexpr int BAR = RAW + NRS * RAW_STAGE;
     static constexpr int N_BAR = 1 + 2 * NRS + 4 * KVB + (2 * s_bufs(NT, D) + 2 * p_bufs(NT, D) + 1) * NT + 1 + 1;
     static constexpr int TOTAL = BAR + N_BAR * 8 + 32;
@@ -238,27 +247,29 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
                                                                        const Params p) {
     using L = Smem<QUANT, NT, D>;
     constexpr int KVB = L::KVB;
+    constexpr int B = L::B;   // keys per block
     constexpr int RAWB = L::RAWB;
     constexpr int GB = dec::q_group_bytes(QUANT);
-    constexpr uint32_t IDESC_S = idesc_f16(BM, BN, 0);
+    constexpr uint32_t IDESC_S = idesc_f16(BM, B, 0);
     constexpr uint32_t IDESC_PV = idesc_f16(BM, D, 1);
     // warpgroups: 0 = TMA (warp 0) + MMA (warps 1, 2) + 1 idle warp, 1..NT = softmax of tile t, last = dequant
     constexpr int SM0 = 4, DQ0 = 4 + 4 * NT;   // first softmax warp, first dequant warp
     constexpr int NDQ = dq_warps(NT);
-    // tensor memory (512 columns) of tile t from column t * 256: S (64 columns), two P buffers (32 columns each, f16
-    // packed two keys per column), O (D columns); D = 128 with one tile: the second S buffer at column 256, where a
-    // second tile's S would, so every accumulator keeps the alignment of the two-tile layout, P buffers 2 and 3 at 320
-    // and 352, Q at 384; D = 256 (one tile): O at 128-383, Q at 384-511
+    // tensor memory (512 columns) of tile t from column t * 256: S (B columns), two P buffers (B / 2 columns each, f16
+    // packed two keys per column), O (D columns); one tile: Q at 384 (D / 2 columns). 128-key blocks (D = 128): S
+    // 0-127, P 128 / 192, O 256-383; D = 256: S 0-63, P 64 / 96, O 128-383; the 64-key layout at D = 128: the second S
+    // buffer at column 256, where a second tile's S would, so every accumulator keeps the alignment of the two-tile
+    // layout, and P buffers 2 and 3 at 320 and 352
     constexpr int NSB = s_bufs(NT, D), NPB = p_bufs(NT, D);
     constexpr bool QT = q_in_tmem(NT);
-    constexpr uint32_t T_P = BN, T_O = 2 * BN, TCOLS = 512;
+    constexpr uint32_t T_P = B, T_O = 2 * B, TCOLS = 512;
     constexpr uint32_t T_Q = 384;   // Q (one tile): row = lane, column c = f16 elements 2c, 2c + 1
     static_assert(T_O + D <= (NSB == 2 || NPB > 2 ? 256u : T_Q) && T_Q + (QT ? D / 2 : 0) <= TCOLS,
                   "one-tile tensor memory layout");
     static_assert(!QT || NT == 1, "Q in tensor memory with one tile only");
     static_assert(NPB == 2 || (NT == 1 && NSB == 2), "P buffers 2, 3 live in the one-tile 512-column layout");
     // column of P buffer i (relative to the tile)
-    auto p_col = [](uint32_t i) -> uint32_t { return i < 2 ? T_P + i * (BN / 2) : 256 + BN + (i - 2) * (BN / 2); };
+    auto p_col = [](uint32_t i) -> uint32_t { return i < 2 ? T_P + i * (B / 2) : 256 + B + (i - 2) * (B / 2); };
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // operand tiles need 1024-byte alignment (128-byte swizzle atoms): align the dynamic base explicitly
@@ -286,7 +297,7 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
     const uint32_t rt = cid % p.n_rt, h = (cid / p.n_rt) % p.nkv;
     const dec::Job job = p.jobs[cid / (p.n_rt * p.nkv)];
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const uint32_t nblk = (job.nk + BN - 1) / BN;
+    const uint32_t nblk = (job.nk + B - 1) / B;
     const uint32_t hbyte = h * (uint32_t) p.hb;
     const int hx = (int) (hbyte & ~15u);          // window start (16-byte aligned) of this head in a key row
     const uint32_t hoff = hbyte & 15u;            // head start inside the window
@@ -349,9 +360,10 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
     };
 
     if (warp < 4) {
-      // 16 warps launched with 128 registers each at NT = 1 and 2; each warpgroup resizes its share (NT = 1: control 160,
-      // softmax 168, two dequant warpgroups 88: 128 x (160 + 168 + 88 + 88) = 64,512 <= 65,536)
-      if constexpr (NT == 1) asm volatile("setmaxnreg.inc.sync.aligned.u32 160;");
+      // 16 warps launched with 128 registers each at NT = 1 and 2; each warpgroup resizes its share (NT = 1, 64-key
+      // blocks: control 160, softmax 168, two dequant warpgroups 88; 128-key blocks: control 128, softmax 200 (the 128
+      // scores of a row), dequant 88: 128 x (160 + 168 + 88 + 88) or 128 x (128 + 200 + 88 + 88) = 64,512 <= 65,536)
+      if constexpr (NT == 1 && B == 64) asm volatile("setmaxnreg.inc.sync.aligned.u32 160;");
       if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
@@ -367,10 +379,14 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
             for (uint32_t j = 0; j < nblk; j++) {
                 const uint32_t st = j % NRS;
                 if (j >= NRS && !wait(&raw_empty[st], ((j / NRS) - 1) & 1)) break;
-                mbar_arrive_expect_tx(&raw_full[st], 2 * BN * RAWB);
+                mbar_arrive_expect_tx(&raw_full[st], 2 * B * RAWB);
                 uint8_t *dst = smem + L::RAW + st * L::RAW_STAGE;
-                tma_2d(dst, km, hx / 2, (int) (job.key0 + j * BN), &raw_full[st]);
-                tma_2d(dst + BN * RAWB, vm, hx / 2, (int) (job.key0 + j * BN), &raw_full[st]);
+#pragma unroll
+                for (int c = 0; c < B / BN; c++) {   // the tensor maps' boxes hold 64 keys
+                    const int key = (int) (job.key0 + j * B) + c * BN;
+                    tma_2d(dst + c * BN * RAWB, km, hx / 2, key, &raw_full[st]);
+                    tma_2d(dst + (B + c * BN) * RAWB, vm, hx / 2, key, &raw_full[st]);
+                }
                 issued = j + 1;
             }
             // on an abort, every issued copy lands before the CTA exits
@@ -396,7 +412,7 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
                 for (uint32_t j = 0; j < nblk && ok; j++) {
                     const uint32_t b = j % KVB;
                     if (!wait(&k_full[b], (j / KVB) & 1)) break;
-                    const uint64_t dk = dk0 + b * (uint32_t) (BN * D * 2 / 16);
+                    const uint64_t dk = dk0 + b * (uint32_t) (B * D * 2 / 16);
 #pragma unroll
                     for (int t = 0; t < NT; t++) {
                         const uint32_t sb = t * NSB + j % NSB;   // the block's S buffer
@@ -406,7 +422,7 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
                         const uint64_t dq = dq0 + (uint32_t) (t * BM * D * 2 / 16);
 #pragma unroll
                         for (int kk = 0; kk < D / 16; kk++) {
-                            const uint64_t bk = dk + (uint32_t) (((kk / 4) * BN * 128 + (kk % 4) * 32) / 16);
+                            const uint64_t bk = dk + (uint32_t) (((kk / 4) * B * 128 + (kk % 4) * 32) / 16);
                             if constexpr (QT)   // A = Q from tensor memory: 8 columns (16 f16) per k-step
                                 tc_mma_ts(d, tmem + t * 256 + T_Q + kk * 8, bk, IDESC_S, kk > 0 ? 1u : 0u);
                             else
@@ -420,11 +436,11 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
                 }
             }
         } else if (lane == 0) {
-            const uint64_t dv0 = sdesc(sbase + L::V, BN * 128, 1024);
+            const uint64_t dv0 = sdesc(sbase + L::V, B * 128, 1024);
             for (uint32_t jj = 0; jj < nblk && ok; jj++) {
                 const uint32_t b = jj % KVB;   // V buffer
                 if (!wait(&v_full[b], (jj / KVB) & 1)) break;
-                const uint64_t dv = dv0 + b * (uint32_t) (BN * D * 2 / 16);
+                const uint64_t dv = dv0 + b * (uint32_t) (B * D * 2 / 16);
 #pragma unroll
                 for (int t = 0; t < NT; t++) {
                     const uint32_t pb = jj % NPB;   // P buffer
@@ -433,7 +449,7 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
                     const uint32_t d = tmem + t * 256 + T_O;
                     const uint32_t pa = tmem + t * 256 + p_col(pb);   // P buffer pb (f16, two keys per column)
 #pragma unroll
-                    for (int ks = 0; ks < BN / 16; ks++)
+                    for (int ks = 0; ks < B / 16; ks++)
                         tc_mma_ts(d, pa + ks * 8, dv + (uint32_t) (ks * 2048 / 16), IDESC_PV, (jj > 0 || ks > 0) ? 1u : 0u);
                     tc_commit(&pv_free[t * NPB + pb]);   // P buffer pb and O (through this block) are settled
                     if (jj + 1 == nblk) tc_commit(&o_ready[t]);
@@ -453,6 +469,7 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
     } else if (warp < (uint32_t) DQ0) {
         // ------------------------------------------------ softmax warpgroup of tile t
         if constexpr (NT == 2) asm volatile("setmaxnreg.inc.sync.aligned.u32 152;");
+        else if constexpr (B == 128) asm volatile("setmaxnreg.inc.sync.aligned.u32 200;");
         else asm volatile("setmaxnreg.inc.sync.aligned.u32 168;");
         if (p.stall) wait(never, 0);                       // runs out: records the timeout, every role unwinds
         const int t = (int) (warp - SM0) / 4;
@@ -495,28 +512,30 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
             if (!wait(&s_full[sb], (j / NSB) & 1)) break;
             tc_fence_after();
             const uint32_t ts = tl + (j % NSB) * 256;
-            float s[BN];
+            float s[B];   // the row's B scores stay in registers, so S is free as soon as it is read
             {
-                float a[32], c[32];
-                tmem_ld32(ts, a);
-                tmem_ld32(ts + 32, c);
+                float a[B / 32][32];
+#pragma unroll
+                for (int c = 0; c < B / 32; c++) tmem_ld32(ts + 32 * c, a[c]);
                 tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 32; i++) { s[i] = a[i]; s[32 + i] = c[i]; }
+                for (int c = 0; c < B / 32; c++)
+#pragma unroll
+                    for (int i = 0; i < 32; i++) s[32 * c + i] = a[c][i];
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_empty[sb]);
-            const int nvalid = (int) (job.nk - j * BN);
-            if (nvalid < BN) {
+            const int nvalid = (int) (job.nk - j * B);
+            if (nvalid < B) {
 #pragma unroll
-                for (int i = 0; i < BN; i++)
+                for (int i = 0; i < B; i++)
                     if (i >= nvalid) s[i] = -INFINITY;
             }
             float mx = s[0];
 #pragma unroll
-            for (int i = 1; i + 1 < BN; i += 2) mx = max3(mx, s[i], s[i + 1]);
-            mx = fmaxf(mx, s[BN - 1]);
+            for (int i = 1; i + 1 < B; i += 2) mx = max3(mx, s[i], s[i + 1]);
+            mx = fmaxf(mx, s[B - 1]);
             mx *= LOG2E;
             m_row = fmaxf(m_row, mx);
             float alpha = 1.f;
@@ -530,14 +549,13 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
             // p = 2^(s*log2e - m): scale-and-shift and the row sum on fp32 pairs (fma/add .f32x2)
             const uint64_t l2e2 = pack_f2(LOG2E, LOG2E), nm2 = pack_f2(-m_used, -m_used);
             uint64_t acc = pack_f2(0.f, 0.f);
-            uint32_t ph[BN / 2];
+            uint32_t ph[B / 2];
 #pragma unroll
-            for (int i = 0; i < BN / 2; i++) {
+            for (int i = 0; i < B / 2; i++) {
                 float t0, t1;
                 unpack_f2(fma_f2(pack_f2(s[2 * i], s[2 * i + 1]), l2e2, nm2), t0, t1);
                 const float p0 = ex2(t0), p1 = ex2(t1);
-                const uint64_t pp = pack_f2(p0, p1);
-                acc = add_f2(acc, pp);
+                acc = add_f2(acc, pack_f2(p0, p1));
                 ph[i] = pack_h2(p0, p1);
             }
             float sum_a, sum_b;
@@ -561,7 +579,10 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
                 tmem_wait_st();
             }
             if (j >= NPB && !wait(&pv_free[t * NPB + b], ((j / NPB) - 1) & 1)) break;
-            tmem_st32u(tl + p_col(b), ph);   // P, two keys per column, into P buffer b
+            // P, two keys per column, into P buffer b (32 columns at a time)
+#pragma unroll
+            for (int hq = 0; hq < B / 64; hq++)
+                tmem_st32u(tl + p_col(b) + 32 * hq, *reinterpret_cast<const uint32_t(*)[32]>(ph + 32 * hq));
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -593,7 +614,8 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
         }
     } else {
         // ------------------------------------------------ dequantisers: warp dw owns quant blocks dw % 4 (+ 4 at
-        // D = 256) of every key (4 warps: both 32-key halves of a block; 8 warps, NT = 1: key half dw / 4)
+        // D = 256) of every key (4 warps: both 32-key halves of each 64 keys; 8 warps, NT = 1: key half dw / 4 of each
+        // 64 keys)
         if (NT == 2) asm volatile("setmaxnreg.dec.sync.aligned.u32 80;");
         else asm volatile("setmaxnreg.dec.sync.aligned.u32 88;");
         const uint32_t dw = warp - DQ0;
@@ -604,18 +626,19 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
 #pragma unroll
             for (int kv = 0; kv < 2; kv++) {
                 if (j >= KVB && !wait(kv == 0 ? &k_free[b] : &v_free[b], ((j / KVB) - 1) & 1)) break;
-                const uint32_t src = raw + kv * BN * RAWB;
+                const uint32_t src = raw + kv * B * RAWB;
+                // items: 64-key chunk kc of the block, key half (8 warps) or pass (4 warps), quant block of the warp
 #pragma unroll
-                for (int it = 0; it < (8 / NDQ) * (D / 128); it++) {
-                    const int pass = it % (8 / NDQ);
-                    const uint32_t qblk = dw % 4 + 4 * (uint32_t) (it / (8 / NDQ));
+                for (int it = 0; it < (B / 64) * (8 / NDQ) * (D / 128); it++) {
+                    const int pass = it % (8 / NDQ), kc = it / (8 / NDQ) % (B / 64);
+                    const uint32_t qblk = dw % 4 + 4 * (uint32_t) (it / ((8 / NDQ) * (B / 64)));
                     const uint32_t bo = hoff + GB * qblk;               // block start inside the raw window row
                     const uint32_t w16 = bo & ~15u;                     // 16-byte aligned start of the words covering it
                     const uint32_t ds = bo + 2;                         // first data byte
                     const uint32_t w0 = (ds - w16) / 4, shift = 8 * (ds % 4);
                     // atom column of this block's d's
-                    const uint32_t dst = sbase + (kv == 0 ? L::K : L::V) + b * BN * D * 2 + (qblk / 2) * BN * 128;
-                    const uint32_t key = (NDQ == 8 ? dw / 4 : (uint32_t) pass) * 32 + lane;
+                    const uint32_t dst = sbase + (kv == 0 ? L::K : L::V) + b * B * D * 2 + (qblk / 2) * B * 128;
+                    const uint32_t key = 64 * (uint32_t) kc + (NDQ == 8 ? dw / 4 : (uint32_t) pass) * 32 + lane;
                     const uint32_t rb = src + key * RAWB;
                     const uint32_t s2 = lds16(rb + bo);
                     const uint32_t sc2 = s2 | (s2 << 16);
