@@ -29,11 +29,12 @@ namespace {
 
 constexpr int kMaxSmem = 227 * 1024;
 // query rows per KV head from which the tcgen05 kernels are used: they dequantise each key block once for all rows,
-// where the split-K kernel repeats it per 8-row group. Measured crossover (8 KV heads, Q8_0, GB/s split-K vs tcgen05):
-// hd 128: 16 rows 2,337 vs 2,024, 24 rows 1,578 vs 2,021, 40 rows 944 vs 1,942; hd 256 (4 layers x 32,768 keys,
-// single-CTA kernel): 8 rows 4,267 vs 3,547, 12 rows 2,259 vs 3,535, 16 rows 2,177 vs 3,545 (4 KV heads: 8 rows 3,463
-// vs 3,247, 12 rows 2,230 vs 3,238): one 8-row group stays on the split-K kernel
-constexpr uint32_t kPrefillMinRows128 = 24, kPrefillMinRows256 = 9;
+// where the split-K kernel repeats it per 8-row group. Measured crossover (8 KV heads x 4 layers x 32,768 Q8_0 keys,
+// GB/s split-K vs the single-CTA tcgen05 kernel): hd 128: 8 rows 3,636 vs 2,569, 12 rows 2,095 vs 2,558, 16 rows 2,066
+// vs 2,558 (4 KV heads: 8 rows 2,882 vs 2,329, 12 rows 1,910 vs 2,328); hd 256: 8 rows 4,267 vs 3,547, 12 rows 2,259 vs
+// 3,535, 16 rows 2,177 vs 3,545 (4 KV heads: 8 rows 3,463 vs 3,247, 12 rows 2,230 vs 3,238). One 8-row group stays on
+// the split-K kernel.
+constexpr uint32_t kPrefillMinRows128 = 9, kPrefillMinRows256 = 9;
 // ... and from which the hd-128 calls run on CTA pairs: past 256 rows the single-CTA kernel starts a second, partly
 // filled tile. Measured (8 KV heads x 4 layers x 65,536 Q8_0 keys, TFLOP/s single vs pair): 256 rows 676 vs 558,
 // 320 510 vs 549, 384 608 vs 643, 448 667 vs 694, 512 751 vs 784
