@@ -8,13 +8,14 @@
 //
 // One CTA = one chunk of keys of one segment x one KV head x NT tiles of 128 query rows. Warp roles:
 //   warp 0             TMA: with two tiles the Q tiles once (128-byte swizzle, the UMMA operand layout), then per
-//                      64-key block the raw quantised rows of this head (a 16-byte-aligned window of each key row, one
-//                      2-D tensor copy for K and one for V; keys past the end read as zeros)
-//   warps 1, 2         warp 1 allocates TMEM (two tiles, per tile: S 64 columns, two P buffers of 32, O 128; one tile:
-//                      two S buffers, four P buffers, O and the Q tile, 512 columns); one thread of warp 1 issues the
-//                      S_t = Q_t K^T MMAs (M=128, N=64; A = Q from shared or, one tile, tensor memory) into S, one of
-//                      warp 2 the O_t += P_t V MMAs (M=128, N=128, A = P read from TMEM, B = V read MN-major) into O
-//   warps 4 .. 4+4NT   one warpgroup per Q tile: thread = query row = TMEM lane. Reads its row of S (64 keys; S is
+//                      block (B keys: 128 with one tile at head dim 128, else 64) the raw quantised rows of this head (a
+//                      16-byte-aligned window of each key row, 2-D tensor copies of 64 rows for K and for V; keys past
+//                      the end read as zeros)
+//   warps 1, 2         warp 1 allocates TMEM (512 columns: per tile S B columns, two P buffers of B / 2, O D; one tile:
+//                      the Q tile too); one thread of warp 1 issues the S_t = Q_t K^T MMAs (M=128, N=B; A = Q from
+//                      shared or, one tile, tensor memory) into S, one of warp 2 the O_t += P_t V MMAs (M=128, N=D,
+//                      A = P read from TMEM, B = V read MN-major) into O
+//   warps 4 .. 4+4NT   one warpgroup per Q tile: thread = query row = TMEM lane. Reads its row of S (B keys; S is
 //                      free again once read), masks tail keys, online softmax in the log2 domain with lazy rescaling (the
 //                      running max moves only when a block's max exceeds it by more than 8, so O in TMEM is rescaled
 //                      rarely), writes P as packed f16 into the block's P buffer: the softmax never waits for a P.V
@@ -196,15 +197,11 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int b_mn_major) {
 // The single-CTA kernel's layout depends on the tile count NT and the head dim D (D = 256: one tile only, the reference
 // server's wire geometry).
 // keys per block: 128 with one tile at D = 128 (a block's hand-offs between the roles cost about the same whatever its
-// size, so larger blocks amortise them), else 64
+// size, so larger blocks amortise them), else 64 (D = 256: the same bytes per block)
 __host__ __device__ constexpr int block_keys(int nt, int d = 128) { return nt == 1 && d == 128 ? 128 : 64; }
-// the 64-key one-tile layout at D = 128 (two S buffers, four P buffers, a 4-deep K/V ring); every other one has 512 or
-// fewer columns of tensor memory for one S and two P buffers, and 32 KB K/V buffers in a 2-deep ring
-__host__ __device__ constexpr bool small_one_tile(int nt, int d) { return nt == 1 && d == 128 && block_keys(nt, d) == 64; }
-// dequantised K and V buffers (a ring): 4 in the 64-key one-tile layout (measured +1% on the config-3 verify batch over
-// 2), else 2
-__host__ __device__ constexpr int kv_bufs(int nt, int d = 128) { return small_one_tile(nt, d) ? 4 : 2; }
-// raw (quantised) K/V stages of the TMA ring: 3 with 64-key blocks at D = 128, else 2 (a stage of Q8_0 rows is 34-36 KB)
+// dequantised K and V buffers (a ring of 2: 32 KB each with one tile)
+__host__ __device__ constexpr int kv_bufs(int nt, int d = 128) { return 2; }
+// raw (quantised) K/V stages of the TMA ring: 3 with two tiles, else 2 (a stage of Q8_0 rows is 34-36 KB)
 __host__ __device__ constexpr int raw_stages(int quant, int nt, int d = 128) {
     return d == 128 && block_keys(nt, d) == 64 ? 3 : 2;
 }
@@ -212,17 +209,15 @@ __host__ __device__ constexpr int raw_stages(int quant, int nt, int d = 128) {
 __host__ __device__ constexpr int dq_warps(int nt) { return nt == 1 ? 8 : 4; }
 // warps of a CTA: TMA + MMA warpgroup, one softmax warpgroup per Q tile, dequant
 __host__ __device__ constexpr int cta_warps(int nt) { return 4 + 4 * nt + dq_warps(nt); }
-// S accumulators per Q tile in tensor memory: two with one tile at D = 128 (the S MMA of block j+1 runs while the
-// softmax still works on block j; a CTA has the SM's 512 columns to itself), else one (two tiles: each tile's S, P and
-// O fill 256 columns; D = 256: O takes 256 and Q 128)
-__host__ __device__ constexpr int s_bufs(int nt, int d = 128) { return small_one_tile(nt, d) ? 2 : 1; }
+// S accumulators per Q tile in tensor memory: one (each layout fills the 512 columns with S, P, O and Q; with a row's
+// scores in registers S is free as soon as the softmax has read it)
+__host__ __device__ constexpr int s_bufs(int nt, int d = 128) { return 1; }
 // Q in tensor memory: the one-tile kernel keeps its Q tile in TMEM (D / 2 columns) as the A operand of S = Q K^T, so an S
 // MMA reads only its K slice from shared memory (from shared memory, each N = 64 MMA re-read a 4 KB Q slice: twice the
 // K bytes it multiplies); with two tiles tensor memory is full and Q stays in shared memory
 __host__ __device__ constexpr bool q_in_tmem(int nt) { return nt == 1; }
-// P buffers per Q tile in tensor memory: four with one tile at D = 128 (the softmax writes P of block j once P.V of
-// block j-4 is done, so a P.V queued behind S MMAs in the tensor pipe does not hold the softmax up), else two
-__host__ __device__ constexpr int p_bufs(int nt, int d = 128) { return small_one_tile(nt, d) ? 4 : 2; }
+// P buffers per Q tile in tensor memory: two (the softmax writes P of block j once P.V of block j-2 is done)
+__host__ __device__ constexpr int p_bufs(int nt, int d = 128) { return 2; }
 
 // shared-memory map (all operand tiles 1024-aligned); KVB dequantised K and V buffers
 template <int QUANT, int NT, int D = 128>
@@ -256,20 +251,17 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
     constexpr int SM0 = 4, DQ0 = 4 + 4 * NT;   // first softmax warp, first dequant warp
     constexpr int NDQ = dq_warps(NT);
     // tensor memory (512 columns) of tile t from column t * 256: S (B columns), two P buffers (B / 2 columns each, f16
-    // packed two keys per column), O (D columns); one tile: Q at 384 (D / 2 columns). 128-key blocks (D = 128): S
-    // 0-127, P 128 / 192, O 256-383; D = 256: S 0-63, P 64 / 96, O 128-383; the 64-key layout at D = 128: the second S
-    // buffer at column 256, where a second tile's S would, so every accumulator keeps the alignment of the two-tile
-    // layout, and P buffers 2 and 3 at 320 and 352
+    // packed two keys per column), O (D columns); one tile: Q at 384 (D / 2 columns). One tile at D = 128 (128-key
+    // blocks): S 0-127, P 128 / 192, O 256-383; D = 256: S 0-63, P 64 / 96, O 128-383
     constexpr int NSB = s_bufs(NT, D), NPB = p_bufs(NT, D);
     constexpr bool QT = q_in_tmem(NT);
     constexpr uint32_t T_P = B, T_O = 2 * B, TCOLS = 512;
     constexpr uint32_t T_Q = 384;   // Q (one tile): row = lane, column c = f16 elements 2c, 2c + 1
-    static_assert(T_O + D <= (NSB == 2 || NPB > 2 ? 256u : T_Q) && T_Q + (QT ? D / 2 : 0) <= TCOLS,
-                  "one-tile tensor memory layout");
+    static_assert(NSB == 1 && NPB == 2 && T_O + D <= (NT == 1 ? T_Q : 256u) && T_Q + (QT ? D / 2 : 0) <= TCOLS,
+                  "tensor memory layout");
     static_assert(!QT || NT == 1, "Q in tensor memory with one tile only");
-    static_assert(NPB == 2 || (NT == 1 && NSB == 2), "P buffers 2, 3 live in the one-tile 512-column layout");
     // column of P buffer i (relative to the tile)
-    auto p_col = [](uint32_t i) -> uint32_t { return i < 2 ? T_P + i * (B / 2) : 256 + B + (i - 2) * (B / 2); };
+    auto p_col = [](uint32_t i) -> uint32_t { return T_P + i * (B / 2); };
 
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // operand tiles need 1024-byte alignment (128-byte swizzle atoms): align the dynamic base explicitly
@@ -478,8 +470,8 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
         const uint32_t tl = tmem + ((wq * 32) << 16) + t * 256;
         // a warp whose 32 rows are all past the call's rows (a partly filled tile; NT = 1 only) sits the blocks out: the
         // S, P and Q barriers count only the warps with a real row, its rows' O is never written and MMA rows are
-        // independent, so its S, P and Q may stay as they are. (It must not arrive at all: with two S buffers a warp that
-        // did no work could arrive for block j + 2 before the real warps wrote P of block j.)
+        // independent, so its S, P and Q may stay as they are. (It must not arrive at all: a warp that does no work can
+        // run ahead of the real warps, and its arrival for a later block would complete an earlier block's phase.)
         const bool pad = NT == 1 && row0 + t * BM + wq * 32 >= p.rows;
         // Q in tensor memory: each warp with a real row writes its lanes' Q rows (rows past the call's rows as zeros)
         // into the Q columns, then arrives on q_full, which the S issuer waits for

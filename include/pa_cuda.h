@@ -92,10 +92,10 @@ int pa_cuda_status(pa_cuda_ctx *ctx, void *stream);
 /* Bound on every in-kernel wait (default 2 s). */
 void pa_cuda_set_timeout_ns(pa_cuda_ctx *ctx, uint64_t ns);
 /* Kernel selection for plans created afterwards (as the reference engine's PA_BIG_KERNEL / PA_BIG_MIN_NG switches,
- * phone-attn/pa-metal.mm:818-821): 0 = by shape (default, quantised rows: the tcgen05 kernels from 24 query rows per KV
- * head at hd 128 (on CTA pairs above 256 rows) and from 32 at hd 256 (CTA pairs); the split-K mma.sync kernel otherwise),
- * 1 = always the split-K kernel, 2 = the tcgen05 kernel on single CTAs (hd 128), 3 = the tcgen05 kernel on CTA pairs
- * (hd 128 or 256). */
+ * phone-attn/pa-metal.mm:818-821): 0 = by shape (default, quantised rows: the tcgen05 kernels from 9 query rows per KV
+ * head, on single CTAs up to 256 rows at hd 128 and 128 at hd 256, on CTA pairs above; the split-K mma.sync kernel
+ * otherwise), 1 = always the split-K kernel, 2 = the tcgen05 kernel on single CTAs, 3 = the tcgen05 kernel on CTA
+ * pairs (hd 128 or 256 for both). */
 void pa_cuda_set_kernel(pa_cuda_ctx *ctx, int which);
 /* Failure-detection test hook: while on, the decode kernel's consumer warps (the tcgen05 kernels' softmax warps) first
  * wait on a barrier that nothing completes, so their bounded wait runs out after the timeout; the kernel records
