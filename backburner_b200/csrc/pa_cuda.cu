@@ -954,8 +954,8 @@ const char *pa_cuda_plan_kernel(const pa_cuda_plan *p) {
     const uint32_t q = p->sh.quant;
     if (p->prefill) {
         static const char *names[4][2][2] = {
-            {{"pa::pre::prefill_kernel<1,1>", "pa::pre::prefill_kernel<1,2>"},
-             {"pa::pre::prefill_kernel<2,1>", "pa::pre::prefill_kernel<2,2>"}},
+            {{"pa::pre::prefill_kernel<1,1,128>", "pa::pre::prefill_kernel<1,2,128>"},
+             {"pa::pre::prefill_kernel<2,1,128>", "pa::pre::prefill_kernel<2,2,128>"}},
             {{"pa::pre::prefill_pair_kernel<1,1,128>", "pa::pre::prefill_pair_kernel<1,2,128>"},
              {"pa::pre::prefill_pair_kernel<2,1,128>", "pa::pre::prefill_pair_kernel<2,2,128>"}},
             {{"pa::pre::prefill_pair_kernel<1,1,256>", "pa::pre::prefill_pair_kernel<1,1,256>"},
