@@ -211,12 +211,11 @@ class Context:
         return int(lib().pa_cuda_launch_count(self._h))
 
     # exchange of the position-shard call (shard_attn_allgather_merge) for calls made afterwards
-    EXCHANGE_AUTO, EXCHANGE_ALLGATHER, EXCHANGE_ALLREDUCE, EXCHANGE_PEER, EXCHANGE_PEER_FROM_KERNEL = 0, 1, 2, 3, 4
+    EXCHANGE_AUTO, EXCHANGE_ALLGATHER, EXCHANGE_ALLREDUCE, EXCHANGE_PEER = 0, 1, 2, 3
 
     def set_shard_exchange(self, mode: int):
         """0: by size; 1: all-gather of every rank's packed (O, m, l) and the fold; 2: max / sum all-reduces; 3: peer
-        stores over NVLink from a merge-and-store kernel; 4: peer stores pushed by the split-K attention kernel itself
-        (hd 128; else as 3)."""
+        stores over NVLink."""
         lib().pa_cuda_set_shard_exchange(self._h, int(mode))
 
     def shard_last(self):

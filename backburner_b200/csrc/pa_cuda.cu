@@ -103,8 +103,6 @@ struct pa_cuda_ctx {
     // position shards over NCCL: this rank's packed (O, m, l) and every rank's
     float *d_shard = nullptr, *d_gathered = nullptr;
     size_t d_shard_bytes = 0, d_gathered_bytes = 0;
-    uint32_t *d_xdone = nullptr;     // peer stores from the split-K kernel: finished jobs per unit (zero between calls)
-    size_t d_xdone_n = 0;
     int shard_exchange = 0;          // 0 by size, 1 all-gather + fold, 2 max / sum all-reduces
     int shard_groups = 0;            // 0 by size; else output-set groups whose exchange overlaps the next group's kernels
     int shard_last_mode = 0, shard_last_groups = 0;   // what the last shard call used
@@ -131,8 +129,6 @@ struct pa_cuda_plan {
     int nt = 1;
     uint32_t n_rt = 0;
     CUtensorMap *d_maps = nullptr;
-    // the next decode launch pushes its merged rows to the ranks (position shards over peer stores; null: off)
-    const pa::mrg::XParams *xfuse = nullptr;
     // profiling: event pairs around the decode kernel of each run (a ring, summed by pa_cuda_plan_kernel_ms)
     bool profile = false;
     std::vector<cudaEvent_t> ev;
@@ -413,10 +409,6 @@ int run_attention_sets(pa_cuda_plan *p, const uint16_t *Qs, cudaStream_t st, uin
         prm.n_consumers = p->n_consumers;
         prm.timeout_ns = ctx->timeout_ns;
         prm.stall = ctx->stall_test;
-        if (p->xfuse) {
-            prm.x = *p->xfuse;
-            prm.x_done = ctx->d_xdone;
-        }
         const bool prof = p->profile && p->ev_used + 2 <= p->ev.size();
         if (prof) cudaEventRecord(p->ev[p->ev_used], st);
         cudaError_t e;
@@ -756,7 +748,6 @@ void pa_cuda_destroy(pa_cuda_ctx *ctx) {
     if (ctx->h_status) cudaFreeHost(ctx->h_status);
     if (ctx->d_shard) cudaFree(ctx->d_shard);
     if (ctx->d_gathered) cudaFree(ctx->d_gathered);
-    if (ctx->d_xdone) cudaFree(ctx->d_xdone);
     for (auto e : ctx->xev) cudaEventDestroy(e);
     if (ctx->xstream) cudaStreamDestroy(ctx->xstream);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -1199,7 +1190,7 @@ void pa_cuda_nccl_comm_destroy(void *comm) {
 }
 
 void pa_cuda_set_shard_exchange(pa_cuda_ctx *ctx, int mode) {
-    if (ctx) ctx->shard_exchange = (mode >= 0 && mode <= 4) ? mode : 0;
+    if (ctx) ctx->shard_exchange = (mode >= 0 && mode <= 3) ? mode : 0;
 }
 void pa_cuda_set_shard_groups(pa_cuda_ctx *ctx, int groups) {
     if (ctx) ctx->shard_groups = groups > 0 ? groups : 0;
@@ -1238,24 +1229,19 @@ int pa_cuda_shard_attn_allgather_merge(pa_cuda_plan *p, const uint16_t *Qs, void
     // partials into every rank, the two all-reduces ~2(N-1)/N of one
     const bool big = part * sizeof(float) >= kShardReduceBytes;
     int mode = ctx->shard_exchange ? ctx->shard_exchange : big ? (world > 2 ? 2 : 1) : 3;
-    const bool want_fused = mode == 4;   // peer stores pushed by the attention kernel itself, where it can
-    if (want_fused) mode = 3;
     cudaStream_t st0 = pick(ctx, stream);
-    // exchange 4 with the split-K kernel at hd 128: the attention kernel itself pushes each unit (set, KV head, 8-row
-    // group) once its last job is done, and a fold kernel follows; otherwise the exchange kernel follows the attention
-    const bool fused = want_fused && !p->prefill && p->n_jobs > 0 && p->sh.hd == 128;
-    const uint64_t n_units = (uint64_t) ns * p->sh.nkv * p->n_rg;
     if (mode == 3) {
-        // collective the first time (and when more room is needed); flags per 8-row block or per unit
-        p2p_setup(ctx, api, sc, part, std::max<uint64_t>((rows + 7) / 8, fused ? n_units : 0), st0);
+        p2p_setup(ctx, api, sc, part, (rows + 7) / 8, st0);   // collective the first time (and when more room is needed)
         if (sc->dead) return fail(ctx, PA_CUDA_ENCCL, "the communicator was aborted while setting up the peer stores");
         if (sc->p2p_state != 1) mode = (big && world > 2) ? 2 : 1;
     }
-    ctx->shard_last_mode = fused && mode == 3 ? 4 : mode;
+    ctx->shard_last_mode = mode;
     if (mode == 3) {
         // the attention kernel, then one exchange kernel: its blocks merge this rank's rows, store them into every
         // rank's receive area (the half of this call's parity) and publish them, then fold every rank's rows
         const unsigned long long epoch = ++sc->p2p_calls;
+        int rc = run_attention_sets(p, Qs, st0, 0, ns);
+        if (rc) return rc;
         pa::mrg::XParams x{};
         x.Op = p->d_op;
         x.Mp = p->d_mp;
@@ -1279,30 +1265,8 @@ int pa_cuda_shard_attn_allgather_merge(pa_cuda_plan *p, const uint16_t *Qs, void
         x.L = l;
         x.status = ctx->d_status;
         x.timeout_ns = ctx->timeout_ns;
-        int rc;
-        if (fused) {
-            if (ctx->d_xdone_n < n_units) {   // zero once: each fold zeroes its unit again for the next call
-                if (ctx->d_xdone) cudaFree(ctx->d_xdone);
-                ctx->d_xdone = nullptr;
-                ctx->d_xdone_n = 0;
-                PA_CK(cudaMalloc((void **) &ctx->d_xdone, n_units * sizeof(uint32_t)), "cudaMalloc (unit counters)");
-                PA_CK(cudaMemsetAsync(ctx->d_xdone, 0, n_units * sizeof(uint32_t), st0), "memset (unit counters)");
-                ctx->d_xdone_n = n_units;
-            }
-            p->xfuse = &x;
-            rc = run_attention_sets(p, Qs, st0, 0, ns);
-            p->xfuse = nullptr;
-            if (rc) return rc;
-            const uint32_t nkv = p->sh.nkv, nrows = p->sh.rows, n_rg = p->n_rg;
-            if (hd == 128) pa::mrg::shard_fold_kernel<128><<<(unsigned) n_units, 256, 0, st0>>>(x, ctx->d_xdone, nkv, nrows, n_rg);
-            else pa::mrg::shard_fold_kernel<256><<<(unsigned) n_units, 256, 0, st0>>>(x, ctx->d_xdone, nkv, nrows, n_rg);
-            PA_CK(cudaGetLastError(), "fold kernel launch");
-            ctx->launches++;
-        } else if ((rc = run_attention_sets(p, Qs, st0, 0, ns))) {
-            return rc;
-        }
         const unsigned blocks = (unsigned) ((rows + 7) / 8);
-        if (blocks && !fused) {
+        if (blocks) {
             if (hd == 128) pa::mrg::shard_exchange_kernel<128><<<blocks, 256, 0, st0>>>(x);
             else pa::mrg::shard_exchange_kernel<256><<<blocks, 256, 0, st0>>>(x);
             PA_CK(cudaGetLastError(), "exchange kernel launch");

@@ -28,7 +28,6 @@
 //     words are loaded before its softmax so their shared-memory latency overlaps the softmax.
 #pragma once
 #include "pa_common.cuh"
-#include "pa_merge.cuh"
 
 namespace pa {
 namespace dec {
@@ -73,12 +72,6 @@ struct Params {
     uint32_t n_consumers; // warps per CTA (launch shape)
     uint64_t timeout_ns;
     int stall;            // test hook: consumers first wait on a barrier that nothing completes (bounded)
-    // Position shards over peer stores (x_done null: off). The warp that completes the last job of its unit (output
-    // set, KV head, 8-row group) merges the unit's rows over the set's chunk slots and stores them into every rank's
-    // receive area, then publishes the unit in each rank's flags (x.push_flag[r] + unit); mrg::shard_fold_kernel folds
-    // the ranks' rows after this kernel. x_done[unit] counts the unit's finished jobs (zeroed again by the fold).
-    mrg::XParams x;
-    uint32_t *x_done;
 };
 
 __host__ __device__ constexpr int q_group_bytes(int quant) { return quant == 1 ? 34 : quant == 2 ? 18 : 64; }
@@ -140,38 +133,6 @@ __device__ __forceinline__ void q4_word(uint32_t w, uint32_t s2, uint32_t &l02, 
     l13 = hmul2(hsub2(and_or(w >> 8, m, magic), off), s2);
     h02 = hmul2(hsub2(and_or(w >> 4, m, magic), off), s2);
     h13 = hmul2(hsub2(and_or(w >> 12, m, magic), off), s2);
-}
-
-// Position shards over peer stores: merge the rows of unit (set, head h, row group rg) over the set's chunk slots and
-// store them into every rank's receive area (one warp), NB rows at a time.
-template <int HD>
-__device__ __forceinline__ void push_unit(const Params &p, uint32_t set, uint32_t h, uint32_t rg, uint32_t lane) {
-    constexpr int V = HD / 32, NB = 4;   // rows merged together (the register budget of the kernel's main loop)
-    const uint64_t nrows = (uint64_t) p.x.n_sets * p.x.rows_per_set;
-    const uint32_t r_end = min(p.rows, rg * 8 + 8);
-    for (uint32_t rb = rg * 8; rb < r_end; rb += NB) {
-        const uint32_t nr = min(r_end - rb, (uint32_t) NB);
-        const uint64_t rin = (uint64_t) h * p.rows + rb;                     // first row within the set
-        const uint64_t row0 = (uint64_t) set * p.x.rows_per_set + rin;   // ... and of the call
-        float acc[NB][V], M[NB], L[NB];
-        mrg::merge_rows_l2<HD, NB>(p.Op, p.Mp, p.Lp, p.x.op_stride, p.x.ml_stride, rin, nr,
-                                   p.x.c_range[set], p.x.c_range[set + 1], lane, acc, M, L);
-        for (uint32_t r = 0; r < p.x.world; r++) {
-            float *base = p.x.push[r] + p.x.push_off;
-#pragma unroll
-            for (int q = 0; q < NB; q++) {
-                if ((uint32_t) q >= nr) break;
-                float4 *dst = reinterpret_cast<float4 *>(base + (row0 + q) * HD + lane * V);
-#pragma unroll
-                for (int i = 0; i < V / 4; i++)
-                    dst[i] = make_float4(acc[q][4 * i], acc[q][4 * i + 1], acc[q][4 * i + 2], acc[q][4 * i + 3]);
-                if (lane == 0) {
-                    base[nrows * HD + row0 + q] = L[q] > 0.f ? M[q] : -INFINITY;
-                    base[nrows * HD + nrows + row0 + q] = L[q];
-                }
-            }
-        }
-    }
 }
 
 // ---------------------------------------------------------------- the kernel
@@ -596,28 +557,6 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
     if (g == 0) {
         if (r0 < p.rows) { p.Mp[rbase + r0] = l0 > 0.f ? m0 : -INFINITY; p.Lp[rbase + r0] = l0; }
         if (r1 < p.rows) { p.Mp[rbase + r1] = l1 > 0.f ? m1 : -INFINITY; p.Lp[rbase + r1] = l1; }
-    }
-
-    // ---- position shards over peer stores: the last job of this (set, head, row group) pushes the merged rows (hd 128;
-    // at hd 256 the merge's registers would spill in the kernels of three CTAs per SM, and an exchange kernel follows)
-    if (HD == 128 && p.x_done) {
-        const uint32_t unit = (job.set * p.nkv + h) * p.n_rg + rg;
-        uint32_t last = 0;
-        __syncwarp();
-        if (lane == 0) {
-            __threadfence();   // this warp's partial rows before its count
-            last = atomicAdd(&p.x_done[unit], 1u) + 1u == p.x.c_range[job.set + 1] - p.x.c_range[job.set];
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-            __threadfence();   // the other jobs' partial rows, counted before this one (read past L1 below)
-            push_unit<HD>(p, job.set, h, rg, lane);
-            __syncwarp();   // the warp's stores, then (cumulative system-scope fence) the unit's flag in every rank
-            if (lane < p.x.world) {
-                __threadfence_system();
-                mrg::st_release_sys(p.x.push_flag[lane] + unit, p.x.epoch);
-            }
-        }
     }
     }   // jobs
     if (!ok) abort_and_drain();

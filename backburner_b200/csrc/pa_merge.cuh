@@ -148,17 +148,15 @@ __global__ void __launch_bounds__(256) merge_kernel(const Params p) {
 // One warp's merge of parts [c0, c1) of one row: part c's row at Op + c * op_stride + rr * HD, its m and l at
 // Mp / Lp + c * ml_stride + rr. Returns sum_c w_c O_c (this lane's HD/32 dims), M and sum_c w_c l_c, w_c =
 // exp(m_c - M), parts with l <= 0 skipped (M = -inf, L = 0 when none has keys). As merge_kernel's one-warp path.
-// (L2ONLY: every load bypasses L1, for parts that other SMs wrote earlier in the same kernel)
-template <int HD, bool L2ONLY = false>
+template <int HD>
 __device__ __forceinline__ void merge_row(const float *Op, const float *Mp, const float *Lp, uint64_t op_stride,
                                           uint64_t ml_stride, uint64_t rr, uint32_t c0, uint32_t c1, uint32_t lane,
                                           float (&acc)[HD / 32], float &M, float &L) {
     constexpr int V = HD / 32;
-    auto ld = [](const float *a) -> float { return L2ONLY ? __ldcg(a) : *a; };
     M = -INFINITY;
     for (uint32_t c = c0 + lane; c < c1; c += 32) {
         const uint64_t pr = (uint64_t) c * ml_stride + rr;
-        if (ld(Lp + pr) > 0.f) M = fmaxf(M, ld(Mp + pr));
+        if (Lp[pr] > 0.f) M = fmaxf(M, Mp[pr]);
     }
 #pragma unroll
     for (int x = 16; x > 0; x >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, x));
@@ -170,9 +168,9 @@ __device__ __forceinline__ void merge_row(const float *Op, const float *Mp, cons
         float w = 0.f;
         if (c < c1) {
             const uint64_t pr = (uint64_t) c * ml_stride + rr;
-            const float lc = ld(Lp + pr);
+            const float lc = Lp[pr];
             if (lc > 0.f) {
-                w = ex2((ld(Mp + pr) - M) * LOG2E);
+                w = ex2((Mp[pr] - M) * LOG2E);
                 Ls = fmaf(w, lc, Ls);
             }
         }
@@ -183,7 +181,7 @@ __device__ __forceinline__ void merge_row(const float *Op, const float *Mp, cons
             const float4 *src = reinterpret_cast<const float4 *>(Op + (uint64_t) (cb + j) * op_stride + rr * HD + lane * V);
 #pragma unroll
             for (int i = 0; i < V / 4; i++) {
-                const float4 x = L2ONLY ? __ldcg(src + i) : src[i];
+                const float4 x = src[i];
                 if (wj != 0.f) {
                     acc[4 * i] = fmaf(wj, x.x, acc[4 * i]);
                     acc[4 * i + 1] = fmaf(wj, x.y, acc[4 * i + 1]);
@@ -196,76 +194,6 @@ __device__ __forceinline__ void merge_row(const float *Op, const float *Mp, cons
 #pragma unroll
     for (int x = 16; x > 0; x >>= 1) Ls += __shfl_xor_sync(0xffffffffu, Ls, x);
     L = Ls;
-}
-
-// The merge of up to NB rows of one set (rows rr0 .. rr0 + nr - 1, consecutive within the set) over chunk slots
-// [c0, c1) by one warp, every load past L1 (the slots were written by other SMs earlier in the same kernel): a lane takes
-// slots c0 + lane, c0 + lane + 32, ... for the maxima and weights, then each slot's rows are loaded together, so the
-// loads of all nr rows of a slot are in flight at once. acc[r]: row r's lane * (HD / 32) .. dims.
-template <int HD, int NB>
-__device__ __forceinline__ void merge_rows_l2(const float *Op, const float *Mp, const float *Lp, uint64_t op_stride,
-                                              uint64_t ml_stride, uint64_t rr0, uint32_t nr, uint32_t c0, uint32_t c1,
-                                              uint32_t lane, float (&acc)[NB][HD / 32], float (&M)[NB], float (&L)[NB]) {
-    constexpr int V = HD / 32;
-#pragma unroll
-    for (int r = 0; r < NB; r++) M[r] = -INFINITY;
-    for (uint32_t c = c0 + lane; c < c1; c += 32) {
-        const uint64_t pr = (uint64_t) c * ml_stride + rr0;
-#pragma unroll
-        for (int r = 0; r < NB; r++)
-            if ((uint32_t) r < nr && __ldcg(Lp + pr + r) > 0.f) M[r] = fmaxf(M[r], __ldcg(Mp + pr + r));
-    }
-#pragma unroll
-    for (int r = 0; r < NB; r++) {
-#pragma unroll
-        for (int x = 16; x > 0; x >>= 1) M[r] = fmaxf(M[r], __shfl_xor_sync(0xffffffffu, M[r], x));
-#pragma unroll
-        for (int i = 0; i < V; i++) acc[r][i] = 0.f;
-        L[r] = 0.f;
-    }
-    for (uint32_t cb = c0; cb < c1; cb += 32) {
-        const uint32_t c = cb + lane;
-        float w[NB];
-#pragma unroll
-        for (int r = 0; r < NB; r++) {
-            w[r] = 0.f;
-            if (c < c1 && (uint32_t) r < nr) {
-                const uint64_t pr = (uint64_t) c * ml_stride + rr0 + r;
-                const float lc = __ldcg(Lp + pr);
-                if (lc > 0.f) {
-                    w[r] = ex2((__ldcg(Mp + pr) - M[r]) * LOG2E);
-                    L[r] = fmaf(w[r], lc, L[r]);
-                }
-            }
-        }
-        const uint32_t nb = min(32u, c1 - cb);
-#pragma unroll 2
-        for (uint32_t j = 0; j < nb; j++) {   // (two slots' loads in flight)
-            const float *src = Op + (uint64_t) (cb + j) * op_stride + rr0 * HD + lane * V;
-            float4 x[NB][V / 4];
-#pragma unroll
-            for (int r = 0; r < NB; r++)
-                if ((uint32_t) r < nr)
-#pragma unroll
-                    for (int i = 0; i < V / 4; i++) x[r][i] = __ldcg(reinterpret_cast<const float4 *>(src + r * HD) + i);
-#pragma unroll
-            for (int r = 0; r < NB; r++) {
-                const float wj = __shfl_sync(0xffffffffu, w[r], j);
-                if ((uint32_t) r < nr && wj != 0.f)
-#pragma unroll
-                    for (int i = 0; i < V / 4; i++) {
-                        acc[r][4 * i] = fmaf(wj, x[r][i].x, acc[r][4 * i]);
-                        acc[r][4 * i + 1] = fmaf(wj, x[r][i].y, acc[r][4 * i + 1]);
-                        acc[r][4 * i + 2] = fmaf(wj, x[r][i].z, acc[r][4 * i + 2]);
-                        acc[r][4 * i + 3] = fmaf(wj, x[r][i].w, acc[r][4 * i + 3]);
-                    }
-            }
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < NB; r++)
-#pragma unroll
-        for (int x = 16; x > 0; x >>= 1) L[r] += __shfl_xor_sync(0xffffffffu, L[r], x);
 }
 
 // ---------------------------------------------------------------- the peer-store exchange of position shards
@@ -433,51 +361,6 @@ __global__ void __launch_bounds__(256) rescale_to_kernel(float *O, const float *
 __global__ void scale_q_kernel(const float *Q, float scale, uint64_t n, uint16_t *Qs) {
     for (uint64_t i = (uint64_t) blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t) gridDim.x * blockDim.x)
         Qs[i] = __half_as_ushort(__float2half_rn(Q[i] * scale));
-}
-
-// The fold of the peer-store exchange when the split-K attention kernel itself pushed the merged rows (dec::Params::x):
-// one block per unit (output set, KV head, 8-row group), the unit's rows held by warps 0..7. Thread 0 zeroes the unit's
-// job counter for the next call (the attention kernel that counted is complete: stream order), waits (bounded) until
-// every rank has published the unit in this rank's flags, and the warps fold the ranks' rows into O, M, L.
-template <int HD>
-__global__ void __launch_bounds__(256) shard_fold_kernel(const XParams p, uint32_t *done, uint32_t nkv, uint32_t rows,
-                                                         uint32_t n_rg) {
-    constexpr int V = HD / 32;
-    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const uint32_t unit = blockIdx.x;
-    const uint32_t rg = unit % n_rg, h = (unit / n_rg) % nkv, s = unit / (n_rg * nkv);
-    const uint64_t nrows = (uint64_t) p.n_sets * p.rows_per_set;
-    __shared__ int s_go;
-    if (threadIdx.x == 0) {
-        done[unit] = 0u;
-        bool go = *(volatile int *) p.status == ST_OK;   // a call that already failed waits no further
-        const uint64_t t0 = globaltimer_ns();
-        for (uint32_t r = 0; go && r < p.world; r++) {
-            const unsigned long long *f = p.flags + (uint64_t) r * p.blocks_cap + unit;
-            for (uint32_t it = 0; ld_acquire_sys(f) < p.epoch; it++) {
-                if ((it & 63) == 63 && globaltimer_ns() - t0 > p.timeout_ns) {
-                    atomicCAS(p.status, ST_OK, ST_TIMEOUT_PEER);
-                    go = false;
-                    break;
-                }
-            }
-        }
-        s_go = go;
-    }
-    __syncthreads();
-    const uint32_t rr = rg * 8 + warp;
-    if (!s_go || rr >= rows) return;
-    const uint64_t row = (uint64_t) s * p.rows_per_set + (uint64_t) h * rows + rr;
-    float acc[V], M, L;
-    merge_row<HD>(p.recv, p.recv + nrows * HD, p.recv + nrows * HD + nrows, p.cap, p.cap, row, 0, p.world, lane, acc, M,
-                  L);
-    float4 *dst = reinterpret_cast<float4 *>(p.O + row * HD + lane * V);
-#pragma unroll
-    for (int i = 0; i < V / 4; i++) dst[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
-    if (lane == 0) {
-        p.M[row] = L > 0.f ? M : -INFINITY;
-        p.L[row] = L;
-    }
 }
 
 }  // namespace mrg

@@ -386,8 +386,7 @@ def exchange_name(world: int, used) -> str:
         return "none (one GPU)"
     mode, groups = used
     kind = {1: "NCCL all-gather of (O,m,l) + LSE fold", 2: "NCCL all-reduce MAX of m + SUM of rescaled (O,l)",
-            3: "peer stores of the merged (O,m,l) over NVLink into every rank + bounded-wait LSE fold",
-            4: "peer stores pushed by the attention kernel over NVLink into every rank + bounded-wait LSE fold"}.get(mode, "?")
+            3: "peer stores of the merged (O,m,l) over NVLink into every rank + bounded-wait LSE fold"}.get(mode, "?")
     return kind + (f", {groups} set groups overlapped with the kernels" if groups > 1 else "")
 
 

@@ -163,14 +163,11 @@ void pa_cuda_nccl_comm_destroy(void *comm);
  * folds them by log-sum-exp into O, m, l, identical on every rank. Every rank calls it, in the same order, with plans of
  * the same n_sets and shape, and the same exchange settings. The exchange (pa_cuda_set_shard_exchange):
  *   peer stores: the merge of this rank's chunk partials stores its rows straight into every rank's receive buffer over
- *     NVLink (buffers mapped into every rank with CUDA IPC, set up collectively by the first such call) and publishes
- *     them in per-source flags there; each rank's fold waits (bounded by pa_cuda_set_timeout_ns: a missing rank's
- *     partial makes pa_cuda_status report PA_CUDA_ETIMEOUT) until every rank's rows are in, then merges. No NCCL launch
- *     on the call's path. Exchange 4, with the split-K kernel at hd 128: the attention kernel itself merges and stores
- *     each (set, KV head, 8-row group) as soon as its last chunk is done, so the stores overlap the remaining attention
- *     work, and only the fold follows (other plans: exchange 3). The choice by size below 8 MiB of partial per rank
- *     (decode, verify): exchange 3; when CUDA IPC is not available on every rank, all ranks use the all-gather
- *     instead.
+ *     NVLink (buffers mapped into every rank with CUDA IPC, set up collectively by the first such call) and counts
+ *     them in on a per-source counter there; each rank's fold waits (bounded by pa_cuda_set_timeout_ns: a missing
+ *     rank's partial makes pa_cuda_status report PA_CUDA_ETIMEOUT) until every rank's rows are in, then merges. No
+ *     NCCL launch on the call's path. The choice by size below 8 MiB of partial per rank (decode, verify); when CUDA
+ *     IPC is not available on every rank, all ranks use the all-gather instead.
  *   all-gather: one ncclAllGather of every rank's packed (O, m, l), then the fold (pa_cuda_merge_gathered): each rank
  *     receives N-1 partials. The choice by size for large partials on 2 ranks.
  *   all-reduce: the rows' maxima over the ranks (ncclAllReduce MAX straight into m), each rank's (O, l) moved to them,
@@ -183,9 +180,7 @@ void pa_cuda_nccl_comm_destroy(void *comm);
 int pa_cuda_shard_attn_allgather_merge(pa_cuda_plan *plan, const uint16_t *Qs, void *comm, float *O, float *m, float *l,
                                        void *stream);
 /* Exchange of pa_cuda_shard_attn_allgather_merge for calls made afterwards: 0 = by size (default), 1 = all-gather and
- * fold, 2 = max / sum all-reduces, 3 = peer stores from a merge-and-store kernel after the attention kernel (set groups
- * do not apply), 4 = peer stores pushed by the split-K attention kernel itself where it runs at hd 128 (else as 3;
- * pa_cuda_shard_last reports which ran). */
+ * fold, 2 = max / sum all-reduces, 3 = peer stores (set groups do not apply). */
 void pa_cuda_set_shard_exchange(pa_cuda_ctx *ctx, int mode);
 /* The exchange (1, 2 or 3) and set groups the last pa_cuda_shard_attn_allgather_merge of this context used. */
 void pa_cuda_shard_last(const pa_cuda_ctx *ctx, int *exchange, int *groups);

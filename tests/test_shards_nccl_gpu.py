@@ -2,8 +2,7 @@
 its contiguous range of positions of every output set; the ranks' packed (O, m, l) are exchanged and folded on every
 rank). Every exchange is covered: the all-gather followed by the fold, the max / sum all-reduces (with and without
 output-set groups, a group's exchange overlapping the next group's kernels), and the peer stores over NVLink (each rank's
-merged rows stored into every rank's receive buffer, the fold waiting on per-source flags), both from a merge-and-store
-kernel after the attention kernel (exchange 3) and from the split-K attention kernel itself (exchange 4, hd 128).
+merged rows stored into every rank's receive buffer, the fold waiting on per-source counters).
 
 A communicator of one rank must give what the plan alone gives; two ranks on two GPUs must agree with each other bit
 for bit and with the oracle over all positions (2e-3, as the other parity tests). A rank that leaves between steps must
@@ -24,8 +23,7 @@ from test_decode_gpu import TOL_REF
 pytestmark = pytest.mark.gpu
 
 HD, NKV, ROWS, NK, SETS = 128, 8, 5, 3000, 4
-# (exchange: 1 all-gather, 2 all-reduce, 3 peer stores from a separate kernel, 4 from the attention kernel; set groups)
-MODES = [(1, 1), (1, 3), (2, 1), (2, 3), (3, 1), (4, 1)]
+MODES = [(1, 1), (1, 3), (2, 1), (2, 3), (3, 1)]   # (exchange: 1 all-gather, 2 all-reduce, 3 peer stores; set groups)
 
 
 def _cases():
