@@ -60,12 +60,12 @@ def test_tcgen05_pair_kernel_hd256_parity(ctx, rows, nk, quant):
     _check(c, O, m, l, nk)
 
 
-# head dim 256 on the single-CTA kernel with one 128-row tile (the default from 32 to 128 rows per KV head): an 8-token
-# ATTN (48 rows), two groups (96), a full tile, ragged keys, Q4_0, and more rows than one tile (forced: several tiles
-# per head as separate CTAs)
+# head dim 256 on the single-CTA kernel with one 128-row tile (the default from 9 to 128 rows per KV head): an 8-token
+# ATTN (48 rows), a 2-token one (12), two groups (96), a full tile, ragged keys, Q4_0, and more rows than one tile
+# (forced: several tiles per head as separate CTAs)
 @pytest.mark.parametrize("rows,nk,quant", [
-    (48, 2500, orc.Q8_0), (96, 2048, orc.Q8_0), (128, 4096, orc.Q8_0), (32, 999, orc.Q4_0), (64, 1, orc.Q4_0),
-    (80, 65, orc.Q8_0), (200, 777, orc.Q8_0)])
+    (48, 2500, orc.Q8_0), (12, 3000, orc.Q8_0), (96, 2048, orc.Q8_0), (128, 4096, orc.Q8_0), (32, 999, orc.Q4_0),
+    (64, 1, orc.Q4_0), (80, 65, orc.Q8_0), (200, 777, orc.Q8_0)])
 def test_tcgen05_kernel_hd256_parity(ctx, rows, nk, quant):
     c = orc.gen_case(7500 + rows + nk + quant, 256, 8, rows, nk, quant)
     O, m, l = _run_kernel(ctx, c, 0 if rows <= 128 else 2)
@@ -74,7 +74,8 @@ def test_tcgen05_kernel_hd256_parity(ctx, rows, nk, quant):
 
 def test_hd256_plans_pick_their_kernels(ctx):
     import torch
-    for rows, want in [(24, "pa::dec::decode_kernel<256,1,8>"), (48, "pa::pre::prefill_kernel<1,1,256>"),
+    for rows, want in [(8, "pa::dec::decode_kernel<256,1,8>"), (12, "pa::pre::prefill_kernel<1,1,256>"),
+                       (48, "pa::pre::prefill_kernel<1,1,256>"),
                        (128, "pa::pre::prefill_kernel<1,1,256>"), (144, "pa::pre::prefill_pair_kernel<1,1,256>")]:
         shape = pa.shape_for(256, 8, rows, pa.Q8_0)
         K = torch.zeros((128, shape.rs), dtype=torch.uint8, device="cuda")
