@@ -62,7 +62,10 @@ def parse():
     ap.add_argument("--verify-steps", type=int, default=20)
     ap.add_argument("--verify-layers", type=int, default=LAYERS)
     ap.add_argument("--engine-calls", type=int, default=200)
-    ap.add_argument("--only", choices=["all", "decode", "prefill", "verify"], default="all",
+    ap.add_argument("--uneven-steps", type=int, default=20, help="config-4 decode steps (0: no config-4 legs)")
+    ap.add_argument("--uneven-prefill-steps", type=int, default=2)
+    ap.add_argument("--uneven-layers", type=int, default=LAYERS)
+    ap.add_argument("--only", choices=["all", "decode", "prefill", "verify", "uneven"], default="all",
                     help="run one workload only (profiling captures); the default line has all of them")
     ap.add_argument("--hd", type=int, choices=[128, 256], default=HD,
                     help="head dim of the decode workload (256: the reference server's wire geometry)")
@@ -196,10 +199,11 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------------------------- data
-def make_layer(torch, pa, layer: int, k0: int, nk: int, device, quant: int = 1):
+def make_layer(torch, pa, layer: int, k0: int, nk: int, device, quant: int = 1, student_t: bool = False):
     """Quantised K and V rows [nk][NKV*hb] for positions [k0, k0+nk) of `layer`: N(0,1) values, 4 K channels per head
-    scaled x8, Q8_0 or Q4_0 (the BASELINE distributions). The values of a position do not depend on the range asked
-    for, so every rank's shard and the parity check's full layer agree."""
+    scaled x8, Q8_0 or Q4_0 (the BASELINE distributions); student_t: V from Student-t with 3 degrees of freedom
+    (config 4: z / sqrt(chi2_3 / 3) from the same seeded generator). The values of a position do not depend on the
+    range asked for, so every rank's shard and the parity check's full layer agree."""
     quantize = pa.quantize_q8_0 if quant == pa.Q8_0 else pa.quantize_q4_0
     g = torch.Generator(device=device)
     g.manual_seed(SEED * 1000 + layer)
@@ -210,6 +214,9 @@ def make_layer(torch, pa, layer: int, k0: int, nk: int, device, quant: int = 1):
         g.manual_seed((SEED * 1000 + layer) * 4096 + c // GEN_CHUNK)
         kf = torch.randn((GEN_CHUNK, NKV, HD), generator=g, device=device)
         vf = torch.randn((GEN_CHUNK, NKV, HD), generator=g, device=device)
+        if student_t:
+            chi = torch.randn((3, GEN_CHUNK, NKV, HD), generator=g, device=device).square().sum(0)
+            vf = vf / (chi / 3.0).sqrt()
         for h in range(NKV):
             kf[:, h, ch[h]] *= 8.0
         a, b = max(k0, c) - c, min(k0 + nk, c + GEN_CHUNK) - c
@@ -226,15 +233,17 @@ def make_q(torch, steps: int, layers: int, rows: int, device, seed: int):
     return (q * (1.0 / HD ** 0.5)).to(torch.float16)
 
 
-def shard_inputs(torch, pa, device, layers: int, keys: int, rank: int, world: int, quant: int, layer_base: int):
-    """This rank's contiguous positions [k0, k0+nk) of every layer, resident on the device."""
+def shard_inputs(torch, pa, device, layers: int, keys: int, rank: int, world: int, quant: int, layer_base: int,
+                 shares=None, student_t: bool = False):
+    """This rank's contiguous positions [k0, k0+nk) of every layer (equal shards, or `shares` positions per rank),
+    resident on the device."""
     from backburner_b200 import shard
-    k0, nk = shard.shard_range(keys, world, rank)
+    k0, nk = shard.shard_range(keys, world, rank, shares)
     rs = NKV * head_bytes(quant)
     K = torch.empty((layers, nk, rs), dtype=torch.uint8, device=device)
     V = torch.empty_like(K)
     for layer in range(layers):
-        k, v = make_layer(torch, pa, layer_base + layer, k0, nk, device, quant)
+        k, v = make_layer(torch, pa, layer_base + layer, k0, nk, device, quant, student_t)
         K[layer].copy_(k)
         V[layer].copy_(v)
         del k, v
@@ -242,14 +251,15 @@ def shard_inputs(torch, pa, device, layers: int, keys: int, rank: int, world: in
 
 
 # --------------------------------------------------------------------------------------------- parity
-def parity_fp64(torch, pa, device, quant: int, keys: int, layer_ids, layer_base: int, Q, O, m, l, rows_sample):
+def parity_fp64(torch, pa, device, quant: int, keys: int, layer_ids, layer_base: int, Q, O, m, l, rows_sample,
+                student_t: bool = False):
     """The merged (O, m, l) of the sampled layers and rows against an fp64 attention over ALL `keys` positions on the
     device (exact dequantisation of the same rows, f16(q*scale) as the kernels read it): max |O/l - ref| / max |ref|
     and max |lse - lse_ref| over the sampled rows, with pa-tool's 5e-3 gate. Q: f16 [layers][NKV][rows][HD]."""
     hb = head_bytes(quant)
     eo_w, el_w = 0.0, 0.0
     for li in layer_ids:
-        Kf, Vf = make_layer(torch, pa, layer_base + li, 0, keys, device, quant)
+        Kf, Vf = make_layer(torch, pa, layer_base + li, 0, keys, device, quant, student_t)
         for h in range(NKV):
             kf = pa.dequantize(Kf[:, h * hb:(h + 1) * hb], quant, HD).double()
             vf = pa.dequantize(Vf[:, h * hb:(h + 1) * hb], quant, HD).double()
@@ -280,12 +290,14 @@ class Leg:
     (one output set per layer) and the step: the plan alone at N = 1, the library's position-shard call at N > 1."""
 
     def __init__(self, torch, dist, pa, ctx, comm, device, stream, world, rank, local, layers, keys, rows, quant,
-                 layer_base, exchange=0, groups=0, chunk_keys=0):
+                 layer_base, exchange=0, groups=0, chunk_keys=0, shares=None, student_t=False, inputs=None):
         self.torch, self.dist, self.pa, self.ctx, self.comm = torch, dist, pa, ctx, comm
         self.device, self.stream, self.world, self.rank, self.local = device, stream, world, rank, local
         self.layers, self.keys, self.rows, self.quant, self.layer_base = layers, keys, rows, quant, layer_base
         self.exchange, self.groups = exchange, groups
-        self.K, self.V, self.k0, self.nk = shard_inputs(torch, pa, device, layers, keys, rank, world, quant, layer_base)
+        # inputs: another leg's (K, V, k0, nk) of the same positions (a second query shape over the same keys)
+        self.K, self.V, self.k0, self.nk = inputs if inputs is not None else shard_inputs(
+            torch, pa, device, layers, keys, rank, world, quant, layer_base, shares, student_t)
         torch.cuda.synchronize()
         self.shape = pa.shape_for(HD, NKV, rows, quant)
         segs = [pa.Seg(self.K[i].data_ptr(), self.V[i].data_ptr(), self.nk, i) for i in range(layers)]
@@ -488,6 +500,88 @@ def bench_prefill(torch, dist, pa, ctx, comm, device, stream, world, rank, local
                          "algorithmic_flops_per_launch": flops_launch,
                          "traffic": prefill_traffic(leg.nk, layers)},
             "breakdown": breakdown(r, steps), "parity": parity, "clocks": r["clocks"], "step_ms": r["step_ms"]}
+
+
+U_KEYS, U_SHARDS, U_SEED = 229376, 8, 41   # config 4
+
+
+def uneven_shares(world: int):
+    """Config 4's 8 seeded uneven shards (10-20% of the positions each, as tests/test_configs_gpu.py draws them),
+    grouped onto `world` ranks (1, 2, 4 or 8): rank r holds shards [r*8/world, (r+1)*8/world), contiguous positions."""
+    import numpy as np
+    w = np.random.default_rng(U_SEED).uniform(0.10, 0.20, U_SHARDS)
+    shares = np.floor(w / w.sum() * U_KEYS).astype(int)
+    shares[-1] += U_KEYS - shares.sum()
+    per = U_SHARDS // world
+    return [int(shares[r * per:(r + 1) * per].sum()) for r in range(world)]
+
+
+def bench_uneven(torch, dist, pa, ctx, comm, device, stream, world, rank, local, layers: int, steps: int,
+                 prefill_steps: int):
+    """Config 4: 229,376 Q8_0 positions per layer with Student-t(3) V, split by position into 8 seeded uneven shards of
+    10-20% each (grouped onto the ranks), 64 layers: a 1-token decode (fresh seeded Q per step) and a 512-token prefill
+    over the same positions. The step time is the slowest rank's, so the uneven split shows in the whole-job rate."""
+    if U_SHARDS % world:
+        return {"skipped": f"config 4's 8 shards do not group onto {world} ranks"}
+    shares = uneven_shares(world)
+    out = {"keys": U_KEYS, "layers": layers, "shares_per_rank": shares}
+    # decode
+    leg = Leg(torch, dist, pa, ctx, comm, device, stream, world, rank, local, layers, U_KEYS, GQA, pa.Q8_0, 4000,
+              shares=shares, student_t=True)
+    Qs = make_q(torch, 16, layers, GQA, device, SEED + 17)
+    r = leg.timed(lambda i: Qs[i % 16], steps, 3, plan_only_steps=min(steps, 20))
+    ms = r["ms"] / steps
+    lb = layer_bytes(U_KEYS)["total"] * layers
+    lb_launch = layer_bytes(leg.nk)["total"] * layers
+    parity = None
+    if rank == 0:
+        last = (3 + steps - 1) % 16   # the last timed step's Q (3 warm-up steps first)
+        parity = parity_fp64(torch, pa, device, pa.Q8_0, U_KEYS, [0, layers - 1], 4000, Qs[last], leg.O, leg.m, leg.l,
+                             torch.arange(GQA, device=device), student_t=True)
+    out["decode"] = {
+        "metric": "uneven decode KV-attn GB/s (config 4: 229376 Q8_0 keys in 8 seeded shards of 10-20%, Student-t V)",
+        "value": round(lb / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ms, 4), "steps": steps,
+        "keys_per_gpu": leg.nk, "exchange": exchange_name(world, r["exchange"]),
+        "roofline": {"bound": "hbm", "achieved": round(lb_launch / (r["kernel_ms"] * 1e-3) / 1e9, 1),
+                     "peak": measured_peaks()[0], "unit": "GB/s",
+                     "frac": round(lb_launch / (r["kernel_ms"] * 1e-3) / 1e9 / measured_peaks()[0], 4),
+                     "kernel": leg.plan.kernel, "kernel_ms": round(r["kernel_ms"], 4)},
+        "breakdown": breakdown(r, steps), "parity": parity, "clocks": r["clocks"]}
+    inputs = (leg.K, leg.V, leg.k0, leg.nk)
+    leg.plan.close()
+    del Qs
+    # prefill over the same positions
+    if prefill_steps > 0:
+        rows = PF_TOKENS * GQA
+        leg2 = Leg(torch, dist, pa, ctx, comm, device, stream, world, rank, local, layers, U_KEYS, rows, pa.Q8_0, 4000,
+                   inputs=inputs)
+        g = torch.Generator(device=device)
+        g.manual_seed(SEED + 19)
+        Qp = (torch.randn((layers, NKV, rows, HD), generator=g, device=device) / HD ** 0.5).to(torch.float16)
+        r2 = leg2.timed(lambda i: Qp, prefill_steps, 2, plan_only_steps=prefill_steps)
+        ms2 = r2["ms"] / prefill_steps
+        flops = 4.0 * PF_TOKENS * Q_HEADS * HD * U_KEYS * layers
+        flops_launch = 4.0 * PF_TOKENS * Q_HEADS * HD * leg2.nk * layers
+        peak, kind = measured_tensor_peak()
+        parity2 = None
+        if rank == 0:
+            sample = torch.arange(0, rows, rows // 32, device=device)[:32]
+            parity2 = parity_fp64(torch, pa, device, pa.Q8_0, U_KEYS, [0], 4000, Qp, leg2.O, leg2.m, leg2.l, sample,
+                                  student_t=True)
+        out["prefill"] = {
+            "metric": "uneven prefill attn TFLOP/s (config 4: 512 tokens x 229376 Q8_0 keys in 8 seeded shards)",
+            "value": round(flops / (ms2 * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "ms_per_step": round(ms2, 3),
+            "steps": prefill_steps, "keys_per_gpu": leg2.nk, "exchange": exchange_name(world, r2["exchange"]),
+            "roofline": {"bound": "tensor", "achieved": round(flops_launch / (r2["kernel_ms"] * 1e-3) / 1e12, 1),
+                         "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(flops_launch / (r2["kernel_ms"] * 1e-3) / 1e12 / peak, 4), "peak_kind": kind,
+                         "kernel": leg2.plan.kernel, "kernel_ms": round(r2["kernel_ms"], 3)},
+            "breakdown": breakdown(r2, prefill_steps), "parity": parity2, "clocks": r2["clocks"]}
+        leg2.close()
+        del Qp
+    del inputs, leg
+    torch.cuda.empty_cache()
+    return out
 
 
 def prefill_traffic(nk: int, layers: int):
@@ -716,6 +810,11 @@ def main():
         prefill = bench_prefill(torch, dist, pa, ctx, comm, device, stream, world, rank, local, args.prefill_layers,
                                 args.prefill_steps)
 
+    uneven = None
+    if args.only in ("all", "uneven") and args.uneven_steps > 0 and (HD, GQA) == (128, 5):
+        uneven = bench_uneven(torch, dist, pa, ctx, comm, device, stream, world, rank, local, args.uneven_layers,
+                              args.uneven_steps, args.uneven_prefill_steps)
+
     engine = None
     if rank == 0 and world == 1 and args.only == "all" and args.engine_calls > 0:
         engine = bench_engine(pa, ctx, args.engine_calls)
@@ -745,10 +844,11 @@ def main():
                 "roofline": decode["roofline"], "cpu_baseline": cpu, "e2e": decode["e2e"],
                 "gpu_launches": r["launches"], "clocks": r["clocks"], "step_ms": r["step_ms"],
                 "breakdown": breakdown(r, args.steps), "parity": decode["parity"],
-                "verify": verify, "prefill": prefill, "engine": engine,
+                "verify": verify, "prefill": prefill, "uneven": uneven, "engine": engine,
             }
         else:
-            line = {"metric": "partial run (--only)", "verify": verify, "prefill": prefill, "n_gpus": world}
+            line = {"metric": "partial run (--only)", "verify": verify, "prefill": prefill, "uneven": uneven,
+                    "n_gpus": world}
         print(json.dumps(line), flush=True)
     ctx.set_shard_exchange(0)
     if comm is not None:
