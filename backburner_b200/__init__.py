@@ -19,7 +19,7 @@ needs libpacuda.so and a B200; a missing library raises ``LibraryMissing``.
 from __future__ import annotations
 
 from .api import (  # noqa: F401
-    F16, Q8_0, Q4_0, PaCudaError, LibraryMissing, Shape, Seg, Context, Plan, Engine, lib, lib_path,
+    F16, Q8_0, Q4_0, QK_F16, QK_INT8, PaCudaError, LibraryMissing, Shape, Seg, Context, Plan, Engine, lib, lib_path,
     head_bytes, shape_for, attn, attn_partial, merge, merge_gathered, packed_views, normalize, fold_reply, scale_q,
     available, NcclComm, nccl_unique_id, nccl_wait, shard_attn_allgather_merge,
 )

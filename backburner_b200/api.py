@@ -10,6 +10,7 @@ from dataclasses import dataclass
 from typing import Sequence
 
 F16, Q8_0, Q4_0 = 0, 1, 2          # config_req.is_q8 (phone-attn/phone-attn.h:15)
+QK_F16, QK_INT8 = 0, 1             # QK arithmetic: f16(d*q) K, or the int8-domain QK (scripts/sme/sme_attn.c:465-508)
 _HERE = os.path.dirname(os.path.abspath(__file__))
 lib_path = os.path.join(_HERE, "libpacuda.so")
 
@@ -52,6 +53,7 @@ _SIGS = {
     "pa_cuda_launch_count": (ctypes.c_uint64, [_P]),
     "pa_cuda_set_stall_test": (None, [_P, ctypes.c_int]),
     "pa_cuda_set_kernel": (None, [_P, ctypes.c_int]),
+    "pa_cuda_set_qk_domain": (None, [_P, ctypes.c_int]),
     "pa_cuda_plan_create": (ctypes.c_int, [_P, ctypes.POINTER(_Shape), ctypes.c_uint32, ctypes.POINTER(_Seg),
                                            ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(_P)]),
     "pa_cuda_plan_scratch_bytes": (ctypes.c_size_t, [_P]),
@@ -201,6 +203,12 @@ class Context:
         """0: by shape; 1: split-K mma.sync kernel; 2: tcgen05 kernel on single CTAs; 3: tcgen05 kernel on CTA pairs
         (2 and 3: hd 128, quantised rows) — for plans created afterwards."""
         lib().pa_cuda_set_kernel(self._h, int(which))
+
+    def set_qk_domain(self, domain: int):
+        """QK_F16 (default) or QK_INT8: the reference's int8-domain QK (Q quantised per 32-block by the Q8_0 rule,
+        int32 block dot products with the Q8_0 K bytes, scores in fp32), Q8_0 rows on the split-K kernel only — for
+        plans created afterwards."""
+        lib().pa_cuda_set_qk_domain(self._h, int(domain))
 
     def set_stall_test(self, on: bool):
         """Failure-detection hook: the next decode kernels wait on a barrier nothing completes (bounded)."""

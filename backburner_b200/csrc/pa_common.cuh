@@ -1,5 +1,5 @@
 // pa_common.cuh - small sm_100a building blocks shared by the phone-attn kernels: mbarriers with bounded waits,
-// 1-D bulk (TMA engine) copies, f16 packing, byte permutes and the warp-level f16 MMA.
+// 1-D bulk (TMA engine) copies, f16 packing, byte permutes and the warp-level f16 and s8 MMAs.
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>
@@ -146,6 +146,17 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// D = A(16x32, s8, row) * B(32x8, s8, col), exact int32 (a fresh accumulator: one call is one 32-value dot product
+// per (row, column)). Fragments: a0/a2 = row g, k 4t..4t+3 / 16+4t..; a1/a3 = row g+8; b0/b1 = k 4t.. / 16+4t.., column g;
+// d0,d1 = row g, columns 2t, 2t+1; d2,d3 = row g+8.
+__device__ __forceinline__ void mma16832_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                            uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+// f16 bits (low 16 of x) -> fp32, exact
+__device__ __forceinline__ float h2f_bits(uint32_t x) { return __half2float(__ushort_as_half((unsigned short) x)); }
 
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float M_EMPTY = -1e30f;   // running max before any key (as scripts/sme/sme_attn.c:281)

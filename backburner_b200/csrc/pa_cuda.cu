@@ -80,6 +80,7 @@ struct pa_cuda_ctx {
     uint64_t launches = 0;
     int stall_test = 0;
     int kernel_choice = 0;   // 0 auto, 1 split-K mma.sync kernel, 2 tcgen05 kernel (one CTA), 3 tcgen05 on CTA pairs
+    int qk_domain = PA_CUDA_QK_F16;   // PA_CUDA_QK_INT8: int8-domain QK (Q8_0 rows, split-K kernel)
     std::string err;
     // pa::engine state (begin/end)
     pa_cuda_plan *eng_plan = nullptr;      // the current call's plan (owned by eng_cache)
@@ -126,6 +127,7 @@ struct pa_cuda_plan {
     // tcgen05 path (many query rows per KV head, hd 128): tiles of NT x 128 rows (NT x 256 on a CTA pair), tensor
     // maps of the K/V segments
     bool prefill = false, pair = false;
+    bool qk_i8 = false;   // split-K kernel with the int8-domain QK (decode_kernel<HD, 3, W>)
     int nt = 1;
     uint32_t n_rt = 0;
     CUtensorMap *d_maps = nullptr;
@@ -299,22 +301,26 @@ int decode_regs() {
     return cudaFuncGetAttributes(&a, pa::dec::decode_kernel<HD, Q, W>) == cudaSuccess ? a.numRegs : 128;
 }
 template <int HD, int W>
-int decode_regs_q(uint32_t q) {
-    return q == PA_CUDA_Q8_0 ? decode_regs<HD, 1, W>() : q == PA_CUDA_Q4_0 ? decode_regs<HD, 2, W>() : decode_regs<HD, 0, W>();
+int decode_regs_q(uint32_t q, bool i8) {
+    return q == PA_CUDA_Q8_0 ? (i8 ? decode_regs<HD, 3, W>() : decode_regs<HD, 1, W>())
+         : q == PA_CUDA_Q4_0 ? decode_regs<HD, 2, W>() : decode_regs<HD, 0, W>();
 }
 int decode_ctas_per_sm(const pa_cuda_plan *p) {
     const uint32_t hd = p->sh.hd, q = p->sh.quant;
-    const int regs = hd == 128 ? decode_regs_q<128, 8>(q) : p->w == 4 ? decode_regs_q<256, 4>(q) : decode_regs_q<256, 8>(q);
+    const bool i8 = p->qk_i8;
+    const int regs = hd == 128 ? decode_regs_q<128, 8>(q, i8)
+                   : p->w == 4 ? decode_regs_q<256, 4>(q, i8) : decode_regs_q<256, 8>(q, i8);
     const int threads = 32 * (int) p->n_consumers;
     const int by_regs = 65536 / std::max(1, threads * ((regs + 7) / 8 * 8));
     const int by_smem = (int) ((228u * 1024u) / (p->smem + 1024));
     const int by_threads = 2048 / std::max(1, threads);
     return std::max(1, std::min(std::min(by_regs, by_smem), std::min(by_threads, 32)));
 }
-// the decode-kernel instance of a geometry (hd 128 / 256; f16, Q8_0 or Q4_0 rows; warps per CTA)
+// the decode-kernel instance of a geometry (hd 128 / 256; f16, Q8_0 or Q4_0 rows, Q8_0 with the int8-domain QK; warps
+// per CTA)
 template <int HD, int W>
 cudaError_t launch_decode_q(const pa_cuda_plan *p, uint32_t nj, const pa::dec::Params &prm, cudaStream_t st, uint32_t quant) {
-    return quant == PA_CUDA_Q8_0 ? launch_decode<HD, 1, W>(p, nj, prm, st)
+    return quant == PA_CUDA_Q8_0 ? (p->qk_i8 ? launch_decode<HD, 3, W>(p, nj, prm, st) : launch_decode<HD, 1, W>(p, nj, prm, st))
          : quant == PA_CUDA_Q4_0 ? launch_decode<HD, 2, W>(p, nj, prm, st) : launch_decode<HD, 0, W>(p, nj, prm, st);
 }
 cudaError_t launch_decode_any(const pa_cuda_plan *p, uint32_t nj, const pa::dec::Params &prm, cudaStream_t st, uint32_t hd,
@@ -766,6 +772,10 @@ void pa_cuda_set_kernel(pa_cuda_ctx *ctx, int which) {
     if (ctx) ctx->kernel_choice = which;
 }
 
+void pa_cuda_set_qk_domain(pa_cuda_ctx *ctx, int domain) {
+    if (ctx) ctx->qk_domain = domain == PA_CUDA_QK_INT8 ? PA_CUDA_QK_INT8 : PA_CUDA_QK_F16;
+}
+
 void pa_cuda_set_stall_test(pa_cuda_ctx *ctx, int on) {
     if (ctx) ctx->stall_test = on ? 1 : 0;
 }
@@ -800,13 +810,21 @@ int pa_cuda_plan_create(pa_cuda_ctx *ctx, const pa_cuda_shape *shape, uint32_t n
     p->sh = *shape;
     p->n_sets = n_sets;
     if ((rc = plan_decode_shape(ctx, p))) { delete p; return rc; }
+    if (ctx->qk_domain == PA_CUDA_QK_INT8) {
+        // the int8-domain QK (sme_attn.c:465-508) reads Q8_0 bytes and runs on the split-K kernel only
+        if (shape->quant != PA_CUDA_Q8_0 || ctx->kernel_choice >= 2) {
+            delete p;
+            return fail(ctx, PA_CUDA_EUNSUPPORTED, "the int8-domain QK needs Q8_0 rows and the split-K kernel");
+        }
+        p->qk_i8 = true;
+    }
     // the tcgen05 kernel takes calls with many query rows per KV head (prefill, ATTN_BIG, long verify batches), the
     // split-K kernel the decode-sized ones (as the reference engine switches kernels by rows, pa-metal.mm:818-835)
     // (hd 256, the reference server's wire geometry: one 128-row tile per CTA up to kSingle256MaxRows rows per KV head,
     // CTA pairs above)
     const bool tc_ok = (shape->hd == 128 || shape->hd == 256) && shape->quant != PA_CUDA_F16 && encode_fn() != nullptr;
     const uint32_t min_rows = shape->hd == 128 ? kPrefillMinRows128 : kPrefillMinRows256;
-    p->prefill = tc_ok && (ctx->kernel_choice >= 2 || (ctx->kernel_choice == 0 && shape->rows >= min_rows));
+    p->prefill = tc_ok && !p->qk_i8 && (ctx->kernel_choice >= 2 || (ctx->kernel_choice == 0 && shape->rows >= min_rows));
     if (ctx->kernel_choice >= 2 && !tc_ok) {
         delete p;
         return fail(ctx, PA_CUDA_EUNSUPPORTED,
@@ -965,11 +983,14 @@ const char *pa_cuda_plan_kernel(const pa_cuda_plan *p) {
         const int k = !p->pair ? (p->sh.hd == 256 ? 3 : 0) : p->sh.hd == 256 ? 2 : 1;
         return names[k][q == PA_CUDA_Q8_0 ? 0 : 1][p->nt == 2 ? 1 : 0];
     }
-    static const char *dec[3][3] = {
-        {"pa::dec::decode_kernel<128,0,8>", "pa::dec::decode_kernel<128,1,8>", "pa::dec::decode_kernel<128,2,8>"},
-        {"pa::dec::decode_kernel<256,0,8>", "pa::dec::decode_kernel<256,1,8>", "pa::dec::decode_kernel<256,2,8>"},
-        {"pa::dec::decode_kernel<256,0,4>", "pa::dec::decode_kernel<256,1,4>", "pa::dec::decode_kernel<256,2,4>"}};
-    return dec[p->sh.hd == 128 ? 0 : p->w == 4 ? 2 : 1][q <= 2 ? q : 0];
+    static const char *dec[3][4] = {
+        {"pa::dec::decode_kernel<128,0,8>", "pa::dec::decode_kernel<128,1,8>", "pa::dec::decode_kernel<128,2,8>",
+         "pa::dec::decode_kernel<128,3,8>"},
+        {"pa::dec::decode_kernel<256,0,8>", "pa::dec::decode_kernel<256,1,8>", "pa::dec::decode_kernel<256,2,8>",
+         "pa::dec::decode_kernel<256,3,8>"},
+        {"pa::dec::decode_kernel<256,0,4>", "pa::dec::decode_kernel<256,1,4>", "pa::dec::decode_kernel<256,2,4>",
+         "pa::dec::decode_kernel<256,3,4>"}};
+    return dec[p->sh.hd == 128 ? 0 : p->w == 4 ? 2 : 1][p->qk_i8 ? 3 : q <= 2 ? q : 0];
 }
 
 int pa_cuda_plan_run(pa_cuda_plan *p, const uint16_t *Qs, float *O, float *m, float *l, void *stream) {

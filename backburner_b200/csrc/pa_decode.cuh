@@ -26,6 +26,10 @@
 //   * P is taken against a lazily raised reference max (one warp vote per tile; the cross-lane max and the O rescale
 //     run only when a score passes the reference by 2^8), and the exact row max is restored once per job; a tile's V
 //     words are loaded before its softmax so their shared-memory latency overlaps the softmax.
+//   * QUANT 3: Q8_0 rows with the int8-domain QK of scripts/sme/sme_attn.c:465-508 (sme_qk_i8blk + i8_combine): Q is
+//     quantised per 32-block by the Q8_0 rule (d = f16(max|x| / 127), q = rint(x / d)) when a job starts, one
+//     mma.m16n8k32 s8 per quant block gives the block's exact int32 dot products T for 16 keys x 8 rows, and
+//     s = sum_b float(T_b) * (dq_b * dk_b) in block order (fma). Softmax and P.V are those of QUANT 1.
 #pragma once
 #include "pa_common.cuh"
 
@@ -146,7 +150,10 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
     constexpr int NMT = HD / 16;   // k-steps of QK^T = m-tiles of P.V
     constexpr int STAGE_KEYS = stage_keys(HD);
     constexpr int NSTAGE = nstage(HD);
-    constexpr int GB = q_group_bytes(QUANT);
+    constexpr bool I8 = QUANT == 3;           // int8-domain QK over Q8_0 rows
+    constexpr int QS = I8 ? 1 : QUANT;        // the rows' storage format
+    constexpr int NBK = HD / 32;              // quant blocks in a head
+    constexpr int GB = q_group_bytes(QS);
     constexpr int PAIR = 2 * GB;   // bytes of an aligned pair of quant blocks
     static_assert(STAGE_KEYS == TILE_KEYS, "a stage is one MMA tile of keys");
 
@@ -269,8 +276,47 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
     const uint32_t g0 = gst;
 
     // Q fragments (B operand of S^T = K.Q^T): row n = g of this row group, k values permuted as dK
-    uint32_t qf[NMT][2];
-    {
+    uint32_t qf[I8 ? 1 : NMT][2];
+    // int8-domain QK: Q's int8 words per quant block (k 4t.. and 16+4t.. of the block's MMA) and the block scales of
+    // rows 2t, 2t+1 (the lane's accumulator columns)
+    uint32_t qi[I8 ? NBK : 1][2];
+    float dq[I8 ? NBK : 1][2];
+    if constexpr (I8) {
+        const uint32_t row = rg * 8 + g;
+        const bool real = row < p.rows;
+        const uint16_t *q = p.Qs + (((uint64_t) job.set * p.nkv + h) * p.rows + (real ? row : 0)) * HD;
+#pragma unroll
+        for (int b = 0; b < NBK; b++) {
+            // the block's values in the order the K words of the lane give them (see the QK step): even block (its
+            // bytes start 2 into a word) (0,1,30,31) | (8t-2..8t+1) and (8t+2..8t+5); odd block (8t..8t+3), (8t+4..8t+7)
+            float x[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                int e;
+                if (b % 2) e = 8 * (int) t + i;
+                else if (i < 4) e = t == 0 ? (i < 2 ? i : 28 + i) : 8 * (int) t - 2 + i;
+                else e = 8 * (int) t - 2 + i;
+                x[i] = real ? __half2float(__ushort_as_half(q[32 * b + e])) : 0.f;
+            }
+            float am = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) am = fmaxf(am, fabsf(x[i]));
+            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));   // the quad holds the row's 32 values
+            am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+            const float df = __half2float(__float2half_rn(__fdiv_rn(am, 127.f)));
+            const float id = df != 0.f ? __frcp_rn(df) : 0.f;
+            uint32_t wv[2] = {0u, 0u};
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int v = __float2int_rn(fmaxf(-127.f, fminf(127.f, __fmul_rn(x[i], id))));
+                wv[i / 4] |= ((uint32_t) v & 0xFFu) << (8 * (i % 4));
+            }
+            qi[b][0] = wv[0];
+            qi[b][1] = wv[1];
+            dq[b][0] = __shfl_sync(0xffffffffu, df, 8 * t);       // row 2t lives in quad 2t
+            dq[b][1] = __shfl_sync(0xffffffffu, df, 8 * t + 4);   // row 2t+1
+        }
+    } else {
         const uint32_t row = rg * 8 + g;
         const uint16_t *q = p.Qs + (((uint64_t) job.set * p.nkv + h) * p.rows + (row < p.rows ? row : 0)) * HD;
 #pragma unroll
@@ -309,7 +355,7 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
 
             // ---- S^T = K . Qs^T  (lane: keys g, g+8; its quant block(s) t (+4))
             float c[4] = {0.f, 0.f, 0.f, 0.f};
-            if constexpr (QUANT == 0) {
+            if constexpr (QS == 0) {
                 // f16 rows: ldmatrix.x4 gives each k-step's A fragment (matrices: keys 2r | 2r+1 x d +0 | +8)
                 const uint32_t r = lane % 8, mi = lane / 8;
                 const uint32_t ka = tk + kofs(2 * r + (mi & 1)) + (mi >> 1) * 16;
@@ -318,6 +364,39 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
                     uint32_t a0, a1, a2, a3;
                     ldsm_x4(ka + 32 * ks, a0, a1, a2, a3);
                     mma16816(c, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
+                }
+            } else if constexpr (I8) {
+                // a pair of quant blocks is 17 aligned words: (d,q0,q1)(q2..q5)...(q30,q31,d') then the odd block's 8
+                // words. Per block the lane takes 2 words of keys g and g+8 (even block: words 2t, 2t+1, lane 0's
+                // first one joining q0,q1 with q30,q31; odd block: words 9+2t, 10+2t), one s8 MMA gives the block's
+                // T, and the scores take float(T) * (dq * dk) in block order.
+#pragma unroll
+                for (int j = 0; j < NBK / 2; j++) {
+                    const uint32_t pb = (uint32_t) (PAIR * j);
+                    uint32_t ea[2], eb[2], oa[2], ob[2];
+                    float dke[2], dko[2];
+#pragma unroll
+                    for (int kk = 0; kk < 2; kk++) {
+                        const uint32_t rk = tk + kofs(2 * g + kk) + pb;   // MMA rows g, g+8
+                        const uint32_t w0 = lds32o<0>(rk), w8 = lds32o<32>(rk);
+                        ea[kk] = prmt(lds32(rk + 8 * t), w8, t == 0 ? 0x5432u : 0x3210u);
+                        eb[kk] = lds32(rk + 8 * t + 4);
+                        oa[kk] = lds32(rk + 36 + 8 * t);
+                        ob[kk] = lds32(rk + 40 + 8 * t);
+                        dke[kk] = h2f_bits(w0);
+                        dko[kk] = h2f_bits(w8 >> 16);
+                    }
+                    int T[4];
+                    mma16832_s8(T, ea[0], ea[1], eb[0], eb[1], qi[2 * j][0], qi[2 * j][1]);
+                    c[0] = fmaf(__int2float_rn(T[0]), __fmul_rn(dq[2 * j][0], dke[0]), c[0]);
+                    c[1] = fmaf(__int2float_rn(T[1]), __fmul_rn(dq[2 * j][1], dke[0]), c[1]);
+                    c[2] = fmaf(__int2float_rn(T[2]), __fmul_rn(dq[2 * j][0], dke[1]), c[2]);
+                    c[3] = fmaf(__int2float_rn(T[3]), __fmul_rn(dq[2 * j][1], dke[1]), c[3]);
+                    mma16832_s8(T, oa[0], oa[1], ob[0], ob[1], qi[2 * j + 1][0], qi[2 * j + 1][1]);
+                    c[0] = fmaf(__int2float_rn(T[0]), __fmul_rn(dq[2 * j + 1][0], dko[0]), c[0]);
+                    c[1] = fmaf(__int2float_rn(T[1]), __fmul_rn(dq[2 * j + 1][1], dko[0]), c[1]);
+                    c[2] = fmaf(__int2float_rn(T[2]), __fmul_rn(dq[2 * j + 1][0], dko[1]), c[2]);
+                    c[3] = fmaf(__int2float_rn(T[3]), __fmul_rn(dq[2 * j + 1][1], dko[1]), c[3]);
                 }
             } else {
 #pragma unroll
@@ -381,15 +460,15 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
             // the lane's data bytes start 2 bytes into a word for even quant blocks: load the covering words and
             // shift them into alignment (funnel shift by 8*sig bits; sig is 0 or 2), so every later index is static
             // (f16 rows: the P.V fragments come from ldmatrix.trans in the P.V loop instead)
-            constexpr int NB = QUANT == 1 ? (HD == 128 ? 16 : 32) : QUANT == 2 ? (HD == 128 ? 8 : 16) : 4;   // bytes per lane per key
+            constexpr int NB = QS == 1 ? (HD == 128 ? 16 : 32) : QS == 2 ? (HD == 128 ? 8 : 16) : 4;   // bytes per lane per key
             constexpr int NW = NB / 4;
             uint32_t VW[4][NW];
             uint32_t s01 = 0, s23 = 0;
-            if constexpr (QUANT != 0) {
+            if constexpr (QS != 0) {
             const int b = HD == 128 ? (int) g / 2 : (int) g;
             const int hh = HD == 128 ? (int) g % 2 : 0;
             const uint32_t pb = (uint32_t) (PAIR * (b / 2));
-            const uint32_t start = QUANT == 1 ? pb + ((b % 2) ? 36u : 2u) + 16u * hh : pb + ((b % 2) ? 20u : 2u) + 8u * hh;
+            const uint32_t start = QS == 1 ? pb + ((b % 2) ? 36u : 2u) + 16u * hh : pb + ((b % 2) ? 20u : 2u) + 8u * hh;
             const uint32_t sig = start % 4, wa = start - sig, shift = 8 * sig;
             const uint32_t soff = pb + ((b % 2) ? (uint32_t) GB : 0u);
             uint32_t sc[4];
@@ -456,7 +535,7 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
 
             // ---- O^T += V^T . P^T  (lane: keys 2t,2t+1,2t+8,2t+9; head-dim rows dV(mt, g, 0/1))
             {
-                if constexpr (QUANT == 0) {
+                if constexpr (QS == 0) {
                     // f16 rows: ldmatrix.x4.trans gives each m-tile's A fragment (matrices: keys 2r | 2r+1 of the P^T
                     // order x d +0 | +8); keys past the stage's valid count are zeroed in the fragment (their rows
                     // may hold anything, and 0 * NaN would poison O)
@@ -473,7 +552,7 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
                         ldsm_x4_t(va + 32 * mt, a0, a1, a2, a3);
                         mma16816(o[mt], a0 & m01, a1 & m01, a2 & m23, a3 & m23, pb0, pb1);
                     }
-                } else if constexpr (QUANT == 1) {
+                } else if constexpr (QS == 1) {
 #pragma unroll
                     for (int mt = 0; mt < NMT; mt++) {
                         constexpr uint32_t SEL[2] = {0x5140u, 0x7362u};   // (a.e, b.e, a.e+1, b.e+1), e = 2mt
@@ -544,7 +623,7 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
     const uint32_t r0 = rg * 8 + 2 * t, r1 = r0 + 1;
 #pragma unroll
     for (int mt = 0; mt < NMT; mt++) {
-        const int d0 = dV(QUANT, HD, mt, (int) g, 0), d1 = dV(QUANT, HD, mt, (int) g, 1);
+        const int d0 = dV(QS, HD, mt, (int) g, 0), d1 = dV(QS, HD, mt, (int) g, 1);
         if (r0 < p.rows) {
             p.Op[(rbase + r0) * HD + d0] = o[mt][0];
             p.Op[(rbase + r0) * HD + d1] = o[mt][2];

@@ -660,11 +660,11 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
                             sts128(kbase + ((c ^ (key % 8)) * 16), h0, h1, h2, h3);
                         }
                     } else {
-                        uint32_t D[4];
+                        uint32_t AW[4];
                         switch (w0) {
 #define PA_ALIGN4(W0)                                                                        \
     case W0:                                                                                 \
-        _Pragma("unroll") for (int i = 0; i < 4; i++) D[i] = __funnelshift_r(W[W0 + i], W[W0 + i + 1], shift); \
+        _Pragma("unroll") for (int i = 0; i < 4; i++) AW[i] = __funnelshift_r(W[W0 + i], W[W0 + i + 1], shift); \
         break;
                             PA_ALIGN4(0) PA_ALIGN4(1) PA_ALIGN4(2) PA_ALIGN4(3) default: PA_ALIGN4(4)
 #undef PA_ALIGN4
@@ -674,7 +674,7 @@ __global__ void __launch_bounds__(32 * cta_warps(NT), 1) prefill_kernel(const __
                         const uint32_t m = 0x000F000Fu, magic = 0x64006400u, off8 = 0x64086408u;
 #pragma unroll
                         for (int i = 0; i < 4; i++) {
-                            const uint32_t y = prmt(D[i], D[i], 0x3120u);   // bytes (x0, x2, x1, x3)
+                            const uint32_t y = prmt(AW[i], AW[i], 0x3120u);   // bytes (x0, x2, x1, x3)
                             lo[2 * i] = hmul2(hsub2(and_or(y, m, magic), off8), sc2);
                             lo[2 * i + 1] = hmul2(hsub2(and_or(y >> 8, m, magic), off8), sc2);
                             hi[2 * i] = hmul2(hsub2(and_or(y >> 4, m, magic), off8), sc2);

@@ -70,6 +70,9 @@ def parse():
     ap.add_argument("--hd", type=int, choices=[128, 256], default=HD,
                     help="head dim of the decode workload (256: the reference server's wire geometry)")
     ap.add_argument("--gqa", type=int, default=GQA, help="query rows per KV head of the decode workload")
+    ap.add_argument("--qk", choices=["f16", "int8"], default="f16",
+                    help="QK arithmetic of the Q8_0 decode workloads: f16 (default) or the reference's int8-domain QK "
+                         "(scripts/sme/sme_attn.c:465-508; its fp64 error is past the 5e-3 parity gate)")
     args = ap.parse_args()
     set_geometry(args.hd, args.gqa)
     return args
@@ -718,6 +721,8 @@ def main():
     if not pa.available():
         raise RuntimeError("libpacuda.so did not load on this GPU (build it with python -m backburner_b200.build)")
     ctx = pa.Context(local)
+    if args.qk == "int8":
+        ctx.set_qk_domain(pa.QK_INT8)
     comm = None
     if world > 1:
         # the library's own communicator; torch only carries its unique id from rank 0 to the others
@@ -834,7 +839,7 @@ def main():
                 "config": {"workload": ("config 1: decode" if (HD, GQA) == (128, 5) else "decode") +
                                        ", 1 token/step, fresh seeded Q per step", "layers": L,
                            "keys": args.keys, "keys_per_gpu": decode["keys_per_gpu"], "nkv": NKV, "q_heads": Q_HEADS,
-                           "hd": HD, "quant": "q8_0",
+                           "hd": HD, "quant": "q8_0", "qk": args.qk,
                            "parallelism": f"sequence shards x{world}" + (
                                ", pa_cuda_shard_attn_allgather_merge: " + exchange_name(world, r["exchange"])
                                if world > 1 else ""),

@@ -16,6 +16,7 @@
  *   pa_cuda_normalize      attn_core's O/l, lse           phone-attn/phone-attn.h:651-655
  *   pa_cuda_fold_reply     co-attention slot of a reply   phone-attn/phone-attn.h:18-20 (host merge in the absent llama.cpp)
  *   pa_cuda_scale_q        f16(q * scale)                 phone-attn/phone-attn.h:595-599, scripts/sme/sme_attn.c:276-280
+ *   pa_cuda_set_qk_domain  sme_qk_i8blk + i8_combine      scripts/sme/sme_attn.c:465-508 (int8-domain QK, opt-in)
  *   pa_cuda_alloc_page,
  *   pa_cuda_free_page,
  *   pa_cuda_begin,
@@ -97,6 +98,17 @@ void pa_cuda_set_timeout_ns(pa_cuda_ctx *ctx, uint64_t ns);
  * otherwise), 1 = always the split-K kernel, 2 = the tcgen05 kernel on single CTAs, 3 = the tcgen05 kernel on CTA
  * pairs (hd 128 or 256 for both). */
 void pa_cuda_set_kernel(pa_cuda_ctx *ctx, int which);
+/* QK arithmetic for plans created afterwards. PA_CUDA_QK_F16 (default): K dequantised to f16(d*q) and S = Qs.K^T in
+ * f16 with fp32 accumulation (sme_attn_partial, scripts/sme/sme_attn.c:274-306). PA_CUDA_QK_INT8: the reference's
+ * compressed-domain QK (sme_qk_i8blk + i8_combine, scripts/sme/sme_attn.c:465-508): Q quantised per 32-block by the
+ * Q8_0 rule (d = f16(max|x|/127), q = rint(x/d)), per-block int32 dot products with the Q8_0 K bytes on the s8 tensor
+ * path, S = sum_b T_b * dq_b * dk_b in fp32; softmax and P.V unchanged. Q8_0 rows only and on the split-K kernel at
+ * every row count: creating a plan for other rows, or with pa_cuda_set_kernel 2 / 3, fails with PA_CUDA_EUNSUPPORTED.
+ * Its scores differ from the f16 path's by Q's int8 rounding (about 1e-2 of O on the reference's distributions), so it
+ * is opt-in. pa_cuda_attn_noalloc (no context) always uses PA_CUDA_QK_F16. */
+#define PA_CUDA_QK_F16 0
+#define PA_CUDA_QK_INT8 1
+void pa_cuda_set_qk_domain(pa_cuda_ctx *ctx, int domain);
 /* Failure-detection test hook: while on, the decode kernel's consumer warps (the tcgen05 kernels' softmax warps) first
  * wait on a barrier that nothing completes, so their bounded wait runs out after the timeout; the kernel records
  * PA_CUDA_ETIMEOUT, every role unwinds and returns without trapping, and the context stays usable. Off by default. */
