@@ -121,6 +121,19 @@ __host__ __device__ inline int dV(int quant, int hd, int mt, int g, int half) {
     return 32 * b + e + (mt % 2 ? 16 : 0) + half;
 }
 
+// Int8-domain QK (QUANT 3): per quant block, lane t of a quad feeds k = 4t..4t+3 and 16+4t..16+4t+3 of the block's
+// m16n8k32 MMA with two 4-byte words of each key row. A pair of Q8_0 blocks is 17 aligned words:
+// (d,q0,q1)(q2..q5)...(q26..q29)(q30,q31,d') then the odd block's 8 words. i8_word(odd, t, w) is the byte offset in the
+// pair of the lane's word w (0, 1); for the even block, lane 0's word 0 (d,q0,q1) is joined with the q30,q31 half of
+// word 8 by one PRMT (selector 0x5432). i8_elem(odd, t, i) is the block element of byte i (0..7) of those two words, the
+// order Q's int8 values take in the B fragment.
+__host__ __device__ inline int i8_word(int odd, int t, int w) { return odd ? 36 + 8 * t + 4 * w : 8 * t + 4 * w; }
+__host__ __device__ inline int i8_elem(int odd, int t, int i) {
+    if (odd) return 8 * t + i;
+    if (t == 0 && i < 4) return i < 2 ? i : 28 + i;   // (q0, q1, q30, q31)
+    return 8 * t - 2 + i;
+}
+
 // ---------------------------------------------------------------- fragment builders
 // 4 int8 values (one aligned word) -> two f16x2 of f16(d * q): (v0,v1) and (v2,v3)
 __device__ __forceinline__ void q8_word(uint32_t w, uint32_t s2, uint32_t &lo, uint32_t &hi) {
@@ -287,17 +300,11 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
         const uint16_t *q = p.Qs + (((uint64_t) job.set * p.nkv + h) * p.rows + (real ? row : 0)) * HD;
 #pragma unroll
         for (int b = 0; b < NBK; b++) {
-            // the block's values in the order the K words of the lane give them (see the QK step): even block (its
-            // bytes start 2 into a word) (0,1,30,31) | (8t-2..8t+1) and (8t+2..8t+5); odd block (8t..8t+3), (8t+4..8t+7)
+            // the block's values in the order the K words of the lane give them (i8_elem)
             float x[8];
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                int e;
-                if (b % 2) e = 8 * (int) t + i;
-                else if (i < 4) e = t == 0 ? (i < 2 ? i : 28 + i) : 8 * (int) t - 2 + i;
-                else e = 8 * (int) t - 2 + i;
-                x[i] = real ? __half2float(__ushort_as_half(q[32 * b + e])) : 0.f;
-            }
+            for (int i = 0; i < 8; i++)
+                x[i] = real ? __half2float(__ushort_as_half(q[32 * b + i8_elem(b % 2, (int) t, i)])) : 0.f;
             float am = 0.f;
 #pragma unroll
             for (int i = 0; i < 8; i++) am = fmaxf(am, fabsf(x[i]));
@@ -366,10 +373,8 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
                     mma16816(c, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
                 }
             } else if constexpr (I8) {
-                // a pair of quant blocks is 17 aligned words: (d,q0,q1)(q2..q5)...(q30,q31,d') then the odd block's 8
-                // words. Per block the lane takes 2 words of keys g and g+8 (even block: words 2t, 2t+1, lane 0's
-                // first one joining q0,q1 with q30,q31; odd block: words 9+2t, 10+2t), one s8 MMA gives the block's
-                // T, and the scores take float(T) * (dq * dk) in block order.
+                // per block the lane takes 2 words of keys g and g+8 (i8_word), one s8 MMA gives the block's T, and
+                // the scores take float(T) * (dq * dk) in block order
 #pragma unroll
                 for (int j = 0; j < NBK / 2; j++) {
                     const uint32_t pb = (uint32_t) (PAIR * j);
@@ -379,10 +384,10 @@ __global__ void __launch_bounds__(32 * W, min_ctas(HD, W)) decode_kernel(const P
                     for (int kk = 0; kk < 2; kk++) {
                         const uint32_t rk = tk + kofs(2 * g + kk) + pb;   // MMA rows g, g+8
                         const uint32_t w0 = lds32o<0>(rk), w8 = lds32o<32>(rk);
-                        ea[kk] = prmt(lds32(rk + 8 * t), w8, t == 0 ? 0x5432u : 0x3210u);
-                        eb[kk] = lds32(rk + 8 * t + 4);
-                        oa[kk] = lds32(rk + 36 + 8 * t);
-                        ob[kk] = lds32(rk + 40 + 8 * t);
+                        ea[kk] = prmt(lds32(rk + i8_word(0, (int) t, 0)), w8, t == 0 ? 0x5432u : 0x3210u);
+                        eb[kk] = lds32(rk + i8_word(0, (int) t, 1));
+                        oa[kk] = lds32(rk + i8_word(1, (int) t, 0));
+                        ob[kk] = lds32(rk + i8_word(1, (int) t, 1));
                         dke[kk] = h2f_bits(w0);
                         dko[kk] = h2f_bits(w8 >> 16);
                     }

@@ -104,6 +104,65 @@ int main() {
     assert out.returncode == 0 and "ok" in out.stdout, out.stdout + out.stderr
 
 
+def test_int8_qk_lane_words_match_q_order(tmp_path):
+    """i8_word / i8_elem (pa_decode.cuh), compiled as host code: for both blocks of a Q8_0 pair and every lane of a
+    quad, the two K words the int8-domain QK loads (lane 0's first even-block word joined with word 8 by PRMT 0x5432)
+    carry, byte for byte, the block elements the lane's Q bytes are quantised from; the lanes together cover each
+    block's 32 elements once; every word is 4-byte aligned inside the 68-byte pair and the scales sit where the kernel
+    reads them (even block: word 0 bytes 0-1; odd block: word 8 bytes 2-3)."""
+    src = tmp_path / "i8maps.cu"
+    src.write_text(r'''
+#include <cstdio>
+#include <cstdint>
+#include "pa_decode.cuh"
+static uint32_t word(const uint8_t *p, int off) {
+  return (uint32_t) p[off] | (uint32_t) p[off + 1] << 8 | (uint32_t) p[off + 2] << 16 | (uint32_t) p[off + 3] << 24;
+}
+static uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {   // byte permute of (b:a), the PTX prmt default mode
+  uint64_t x = (uint64_t) b << 32 | a;
+  uint32_t d = 0;
+  for (int i = 0; i < 4; i++) d |= (uint32_t) ((x >> (8 * ((sel >> (4 * i)) & 7))) & 0xFF) << (8 * i);
+  return d;
+}
+int main() {
+  // a pair whose element bytes name themselves: even block element e = 0x40 + e, odd block element e = 0x80 + e
+  uint8_t pair[68];
+  pair[0] = 0xD0; pair[1] = 0xD1; pair[34] = 0xE0; pair[35] = 0xE1;
+  for (int e = 0; e < 32; e++) { pair[2 + e] = (uint8_t) (0x40 + e); pair[36 + e] = (uint8_t) (0x80 + e); }
+  if ((word(pair, 0) & 0xFFFF) != 0xD1D0u || (word(pair, 32) >> 16) != 0xE1E0u) { printf("scales\n"); return 1; }
+  for (int odd = 0; odd < 2; odd++) {
+    int seen[32] = {0};
+    for (int t = 0; t < 4; t++) {
+      uint32_t w[2];
+      for (int k = 0; k < 2; k++) {
+        const int off = pa::dec::i8_word(odd, t, k);
+        if (off % 4 || off < 0 || off + 4 > 68) { printf("word offset %d\n", off); return 1; }
+        w[k] = word(pair, off);
+      }
+      if (!odd) w[0] = prmt(w[0], word(pair, 32), t == 0 ? 0x5432u : 0x3210u);
+      for (int i = 0; i < 8; i++) {
+        const int e = pa::dec::i8_elem(odd, t, i);
+        if (e < 0 || e > 31) { printf("element %d\n", e); return 1; }
+        const uint8_t got = (uint8_t) (w[i / 4] >> (8 * (i % 4)));
+        if (got != (uint8_t) ((odd ? 0x80 : 0x40) + e)) { printf("odd %d lane %d byte %d: %02x\n", odd, t, i, got); return 1; }
+        seen[e]++;
+      }
+    }
+    for (int e = 0; e < 32; e++) if (seen[e] != 1) { printf("element %d seen %d times\n", e, seen[e]); return 1; }
+  }
+  printf("ok\n");
+  return 0;
+}
+''')
+    exe = tmp_path / "i8maps"
+    nvcc = "/usr/local/cuda/bin/nvcc" if os.path.exists("/usr/local/cuda/bin/nvcc") else "nvcc"
+    r = subprocess.run([nvcc, "-std=c++17", "-I", os.path.join(ROOT, "backburner_b200", "csrc"), "-o", str(exe),
+                        str(src)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0 and "ok" in out.stdout, out.stdout + out.stderr
+
+
 def test_pair_kernel_layouts_and_dequant_maps(tmp_path):
     """The CTA-pair tcgen05 kernel's shared-memory map and dequant addressing (pa_prefill_pair.cuh), compiled as host
     code, for Q8_0 / Q4_0, head dim 128 (NT = 1, 2) and 256, both CTAs of a pair and every head offset: the layout fits
