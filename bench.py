@@ -71,7 +71,7 @@ def parse():
                     help="head dim of the decode workload (256: the reference server's wire geometry)")
     ap.add_argument("--gqa", type=int, default=GQA, help="query rows per KV head of the decode workload")
     ap.add_argument("--qk", choices=["f16", "int8"], default="f16",
-                    help="QK arithmetic of the Q8_0 decode workloads: f16 (default) or the reference's int8-domain QK "
+                    help="QK arithmetic of the config-1 decode workload: f16 (default) or the reference's int8-domain QK "
                          "(scripts/sme/sme_attn.c:465-508; its fp64 error is past the 5e-3 parity gate)")
     args = ap.parse_args()
     set_geometry(args.hd, args.gqa)
@@ -721,8 +721,6 @@ def main():
     if not pa.available():
         raise RuntimeError("libpacuda.so did not load on this GPU (build it with python -m backburner_b200.build)")
     ctx = pa.Context(local)
-    if args.qk == "int8":
-        ctx.set_qk_domain(pa.QK_INT8)
     comm = None
     if world > 1:
         # the library's own communicator; torch only carries its unique id from rank 0 to the others
@@ -735,8 +733,11 @@ def main():
     # ---- config 1: decode
     decode = None
     if args.only in ("all", "decode"):
+        # --qk int8: the config-1 decode plan only (the other workloads keep the f16-domain QK and their kernels)
+        ctx.set_qk_domain(pa.QK_INT8 if args.qk == "int8" else pa.QK_F16)
         leg = Leg(torch, dist, pa, ctx, comm, device, stream, world, rank, local, L, args.keys, GQA, pa.Q8_0, 0,
                   chunk_keys=args.chunk_keys)
+        ctx.set_qk_domain(pa.QK_F16)
         total_steps = args.warmup + args.steps
         Qs = make_q(torch, total_steps, L, GQA, device, SEED + 7)      # [steps][L][NKV][GQA][HD]
         r = leg.timed(lambda i: Qs[i], args.steps, args.warmup, plan_only_steps=min(args.steps, 64))
