@@ -61,7 +61,8 @@ struct Plan;
 constexpr size_t kEngCache = 256;                 // plans at most
 constexpr size_t kEngCacheBytes = 1ull << 30;     // and at most this much plan scratch (partials, job lists)
 struct EngEntry {
-    std::vector<uint64_t> key;           // geometry, groups, packed tokens, then (k, v, nkeys) per page
+    std::vector<uint64_t> key;           // geometry, groups, packed tokens, kernel choice, QK arithmetic, then (k, v,
+                                         // nkeys) per page
     pa_cuda_plan *plan = nullptr;
     cudaGraphExec_t graph = nullptr;     // Q upload, kernels, result readback (captured by pa_cuda_arm)
     uint64_t graph_launches = 0;         // kernel launches one replay makes
@@ -1451,7 +1452,10 @@ int eng_prepare(pa_cuda_ctx *ctx, const pa_cuda_page *pages, const uint32_t *nke
     sh.rows = nt ? 6u * (uint32_t) nt : (uint32_t) NR;
     int rc = check_shape(ctx, &sh);
     if (rc) return rc;
+    // the context's kernel choice and QK arithmetic are part of the key: a call after pa_cuda_set_kernel or
+    // pa_cuda_set_qk_domain gets a plan built under the new setting, not a cached one
     std::vector<uint64_t> key = {sh.hd, sh.nkv, sh.rows, sh.quant, sh.rs, sh.hb, (uint64_t) ng, (uint64_t) nt,
+                                 (uint64_t) (uint32_t) ctx->kernel_choice, (uint64_t) (uint32_t) ctx->qk_domain,
                                  (uint64_t) n_pages};
     for (int i = 0; i < n_pages; i++) {
         key.push_back((uint64_t) (uintptr_t) pages[i].k);
